@@ -1,0 +1,209 @@
+/*
+ * yfattn.h — C ABI of the B200 (sm_100a) paged Q8_0 KV attention library.
+ *
+ * This is the drop-in boundary for the attention path of the yforge engine
+ * (askidmobile/qwen36-server) over its persistent paged int8 KV pool
+ * (`--kv-pool q8`, src/cli.rs:111-115,286-290).  The engine's Rust side calls
+ * the functions below through `extern "C"` with raw device pointers, the way
+ * its own `real::paged_attn` call takes raw pool pointers instead of candle
+ * tensors (docs/plans/2026-08-24-qwen35-4b-benchmark.md:600-607).
+ *
+ * Conventions
+ *  - Every pointer argument named d_* is device memory of the pool's device.
+ *    Host arrays are named h_*.
+ *  - The caller owns every buffer passed in.  Calls on the hot path never
+ *    allocate; the split-KV workspace size comes from yf_attn_workspace_size.
+ *  - Every call is asynchronous on the given CUDA stream (cudaStream_t passed
+ *    as void*; NULL is the legacy default stream).
+ *  - The return value is YF_OK or a YF_E_* code from host-side validation.
+ *    yf_last_error() gives a message for the last failure on this thread.
+ *  - Values that only the device knows (page ids in the block table, sequence
+ *    lengths) are checked inside the kernels: an out-of-range page or length
+ *    is skipped and recorded in the pool's device status word, never trapped.
+ *    yf_pool_status() reads and optionally clears that word.
+ *  - Distinct pools may be used from distinct threads; one pool is not
+ *    internally locked (the engine drives it from one thread).
+ *
+ * KV pool format ("Q8_0 pages")
+ *  - One pool holds n_layers planes.  A page is page_size tokens of every KV
+ *    head; pages are shared by all layers (page p of layer l and layer l+1
+ *    belong to the same token range), as with the engine's block tables.
+ *  - A value group of group_size consecutive head_dim elements (32 = GGML
+ *    Q8_0, or head_dim = the engine's own one-scale-per-row int8 pool) is
+ *    stored as int8 q and one f16 scale d, value = q * d.  Quantization is
+ *    GGML's Q8_0 rule: d = amax/127, q = roundf(x * (1/d)), d stored as f16.
+ *  - Within a layer plane, page p / kv head h is one contiguous block of
+ *    page_size/16 "tiles" of 16 tokens.  A tile is
+ *        [K int8 16*D][K scales f16 16*(D/G)][V int8 16*D][V scales f16 16*(D/G)]
+ *    with the int8 and scale bytes permuted inside the tile so that one
+ *    16-byte load per lane delivers tensor-core fragments directly.
+ *    yf_pool_tile_offset() states the permutation for any (token, dim).
+ */
+#ifndef YFATTN_H
+#define YFATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define YF_API __attribute__((visibility("default")))
+#else
+#define YF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define YFATTN_ABI_VERSION 1
+
+/* Return codes of every entry point. */
+#define YF_OK 0
+#define YF_E_INVALID 1     /* bad argument: null pointer, negative size, bad alignment */
+#define YF_E_UNSUPPORTED 2 /* shape not built (head_dim, page_size, group size, GQA ratio) */
+#define YF_E_NOMEM 3       /* device allocation or page allocation failed */
+#define YF_E_CUDA 4        /* a CUDA runtime call failed */
+#define YF_E_RANGE 5       /* length, layer or page id beyond the pool's capacity */
+#define YF_E_WORKSPACE 6   /* workspace smaller than yf_attn_workspace_size */
+#define YF_E_STATE 7       /* page allocator misuse: double free, free of a free page */
+
+/* Bits of the pool's device status word (set by kernels, read by yf_pool_status). */
+#define YF_DEV_BAD_PAGE 1u     /* a block-table entry was >= n_pages: that page was skipped */
+#define YF_DEV_LEN_OVERFLOW 2u /* a sequence length exceeded max_blocks*page_size: clamped */
+#define YF_DEV_BAD_POS 4u      /* a KV write position was outside the block table: row skipped */
+#define YF_DEV_BAD_ROWS 8u     /* a query-row count exceeded max_seqlen_q (or its keys): rows clamped */
+#define YF_DEV_TIMEOUT 16u     /* a bounded wait on a page copy gave up: output of that CTA invalid */
+
+typedef struct yf_pool yf_pool;
+
+typedef struct yf_pool_desc {
+    int32_t n_layers;   /* layer planes in the pool (>= 1) */
+    int32_t n_pages;    /* physical pages per layer plane */
+    int32_t n_kv_heads; /* KV heads (Hkv) */
+    int32_t head_dim;   /* D: 128 or 256 */
+    int32_t page_size;  /* tokens per page: 16 or 64 */
+    int32_t group_size; /* quant group along head_dim: 32 (Q8_0) or head_dim (row scale) */
+    int32_t device;     /* CUDA device ordinal that owns the pool; < 0 = host-only pool */
+    int32_t reserved;
+    void* device_mem;   /* optional caller-owned buffer of yf_pool_bytes(desc) bytes, or NULL */
+} yf_pool_desc;
+
+/* Thread-local message for the last non-YF_OK return on this thread. */
+YF_API const char* yf_last_error(void);
+YF_API int yf_abi_version(void);
+
+/* ---- pool: layout and lifetime --------------------------------------------
+ * Replaces the engine's PagedKvPool {k, v, k_scale, v_scale}
+ * (docs/plans/2026-08-27-tiered-kv-cache.md:352-353) whose size follows
+ * src/vram_plan.rs:249-261. */
+
+/* Bytes of one (page, kv head) block and of the whole pool. */
+YF_API size_t yf_pool_page_head_bytes(const yf_pool_desc* desc);
+YF_API size_t yf_pool_bytes(const yf_pool_desc* desc);
+/* Byte offset inside a 16-token tile of the int8 value of (token t in 0..15,
+ * dim d) for K (is_v=0) or V (is_v=1); the f16 scale offset of (t, group) is
+ * returned by yf_pool_scale_offset.  Pure functions of the format. */
+YF_API int64_t yf_pool_tile_offset(const yf_pool_desc* desc, int is_v, int t, int d);
+YF_API int64_t yf_pool_scale_offset(const yf_pool_desc* desc, int is_v, int t, int group);
+
+/* Creates a pool; allocates device memory unless desc->device_mem is given.
+ * The memory is zero-filled.  All pages start free with refcount 0.
+ * desc->device < 0 makes a host-only pool: the page allocator alone, with no
+ * device memory (every device call on it returns YF_E_INVALID). */
+YF_API int yf_pool_create(const yf_pool_desc* desc, yf_pool** out_pool);
+YF_API int yf_pool_destroy(yf_pool* pool);
+YF_API int yf_pool_get_desc(const yf_pool* pool, yf_pool_desc* out_desc);
+/* Device address of a layer plane (for export by the caller, debugging). */
+YF_API int yf_pool_layer_ptr(const yf_pool* pool, int32_t layer, void** out_ptr);
+
+/* ---- pool: page allocator (host side) --------------------------------------
+ * The engine builds static tables bt[slot*max_blocks+j] = slot*max_blocks+j
+ * (docs/plans/2026-08-27-tiered-kv-cache.md:52-58); this allocator replaces
+ * that arithmetic with a free list plus refcounts so that pages can be
+ * fragmented and shared between slots. */
+
+/* Takes n pages off the free list (refcount 1 each) into h_pages_out.
+ * YF_E_NOMEM (and nothing taken) when fewer than n pages are free. */
+YF_API int yf_pool_alloc_pages(yf_pool* pool, int32_t n, int32_t* h_pages_out);
+/* Adds one reference to each listed page (prefix sharing). */
+YF_API int yf_pool_retain_pages(yf_pool* pool, int32_t n, const int32_t* h_pages);
+/* Drops one reference; a page whose count reaches 0 returns to the free list.
+ * YF_E_STATE if a listed page is already free (nothing is changed then). */
+YF_API int yf_pool_free_pages(yf_pool* pool, int32_t n, const int32_t* h_pages);
+YF_API int yf_pool_free_count(const yf_pool* pool, int32_t* out_free);
+YF_API int yf_pool_refcount(const yf_pool* pool, int32_t page, int32_t* out_refcount);
+
+/* Reads the device status word (synchronizes the pool's device) into
+ * *out_bits; clears it when clear != 0. */
+YF_API int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear);
+
+/* ---- KV write: Q8_0 quantize-and-scatter ------------------------------------
+ * yf_kv_append_paged replaces kv_append_paged_f16 (fork quantized.cu:6996,
+ * cited at docs/plans/2026-08-27-tiered-kv-cache.md:61-64): one new row per
+ * batch entry.  d_k, d_v: f16 [B, Hkv, D] contiguous.  Row b is written at
+ * token position d_pos[b] of batch entry b, i.e. page
+ * d_block_table[b*max_blocks + pos/page_size], slot pos%page_size.
+ * A position outside the table is skipped and flags YF_DEV_BAD_POS (the
+ * engine instead clamped to window-1 and overwrote the last slot). */
+YF_API int yf_kv_append_paged(yf_pool* pool, int32_t layer, const void* d_k, const void* d_v,
+                              const int32_t* d_pos, const uint32_t* d_block_table, int32_t max_blocks,
+                              int32_t batch, void* stream);
+
+/* Replaces launch_append_multi (fork quantized.cu:7040, called from
+ * forward_attn_prefill_paged: docs/plans/2026-08-27-mtp-cuda-graphs.md:132-134):
+ * T contiguous rows per batch entry.  d_k, d_v: f16 [total_rows, Hkv, D];
+ * rows d_cu_rows[b] .. d_cu_rows[b+1]-1 belong to entry b and go to positions
+ * d_start_pos[b] + i.  max_rows bounds d_cu_rows[b+1]-d_cu_rows[b]. */
+YF_API int yf_kv_append_paged_multi(yf_pool* pool, int32_t layer, const void* d_k, const void* d_v,
+                                    const int32_t* d_cu_rows, const int32_t* d_start_pos,
+                                    const uint32_t* d_block_table, int32_t max_blocks, int32_t batch,
+                                    int32_t max_rows, void* stream);
+
+/* ---- attention ---------------------------------------------------------------
+ * Split-KV workspace for a call with these shapes (0 is a valid answer). */
+YF_API size_t yf_attn_workspace_size(const yf_pool* pool, int32_t n_q_heads, int32_t batch,
+                                     int32_t max_seqlen_q, int32_t max_seqlen_k);
+
+/* Batched decode: replaces dispatch_flash_decode_paged(cuda, q, k, v, lens,
+ * table, scale) (src/bin/decode_gqa_probe.rs:26,40-46) and the q8 decode
+ * branch of real::paged_attn.  d_q: f16 [B, Hq, D]; d_cu_seqlens_k: uint32
+ * [B+1] (entry b has d_cu_seqlens_k[b+1]-d_cu_seqlens_k[b] keys, as the probe's
+ * `lens`); d_block_table: uint32 [B, max_blocks]; d_out: f16 [B, Hq, D].
+ * max_seqlen_k bounds every entry's length (it sizes the split grid).
+ * An entry with zero keys produces zeros. */
+YF_API int yf_attn_decode(yf_pool* pool, int32_t layer, const void* d_q, int32_t n_q_heads,
+                          const uint32_t* d_cu_seqlens_k, const uint32_t* d_block_table,
+                          int32_t max_blocks, int32_t batch, int32_t max_seqlen_k, float scale,
+                          void* d_out, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Causal chunked prefill and MTP verify: replaces forward_attn_prefill_paged
+ * (docs/plans/2026-08-27-mtp-cuda-graphs.md:132,244-248) and
+ * forward_verify_paged (:279-284, per_row_gqa at :537-541).
+ * d_q: f16 [total_q, Hq, D]; entry b owns query rows d_cu_seqlens_q[b] ..
+ * d_cu_seqlens_q[b+1]-1 and Tk_b = d_cu_seqlens_k[b+1]-d_cu_seqlens_k[b]
+ * keys already in the pool (prefix plus the new rows).  Query row i of entry
+ * b sees keys 0 .. Tk_b - Tq_b + i ("row i sees 0..kv0+i").
+ * d_out: f16 [total_q, Hq, D]. */
+YF_API int yf_attn_prefill(yf_pool* pool, int32_t layer, const void* d_q, int32_t n_q_heads,
+                           const uint32_t* d_cu_seqlens_q, const uint32_t* d_cu_seqlens_k,
+                           const uint32_t* d_block_table, int32_t max_blocks, int32_t batch,
+                           int32_t max_seqlen_q, int32_t max_seqlen_k, float scale, void* d_out,
+                           void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* ---- prefix snapshot export / restore ----------------------------------------
+ * Byte copies of whole pages (all KV heads, one layer) with their scales and
+ * no requantization, as StateSnapshot::to_host / to_device do for the int8
+ * pool (src/prefix_cache.rs:71-91 and :361; injected by inject_slot_snapshot,
+ * src/engine_batched.rs:1724,1738).  The snapshot buffer holds the n pages
+ * back to back, yf_pool_page_head_bytes * n_kv_heads bytes each; it may be
+ * host (pinned or pageable) or device memory. */
+YF_API int yf_pool_export_pages(yf_pool* pool, int32_t layer, int32_t n, const int32_t* h_pages,
+                                void* dst, void* stream);
+YF_API int yf_pool_restore_pages(yf_pool* pool, int32_t layer, int32_t n, const int32_t* h_pages,
+                                 const void* src, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YFATTN_H */

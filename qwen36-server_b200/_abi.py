@@ -1,0 +1,110 @@
+"""ctypes binding of libyfattn.so (the C ABI declared in include/yfattn.h).
+
+The library is loaded from this package directory.  There is no fallback: if
+the shared object is missing the import fails and says how to build it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libyfattn.so")
+
+YF_OK = 0
+YF_E_INVALID = 1
+YF_E_UNSUPPORTED = 2
+YF_E_NOMEM = 3
+YF_E_CUDA = 4
+YF_E_RANGE = 5
+YF_E_WORKSPACE = 6
+YF_E_STATE = 7
+
+YF_DEV_BAD_PAGE = 1
+YF_DEV_LEN_OVERFLOW = 2
+YF_DEV_BAD_POS = 4
+YF_DEV_BAD_ROWS = 8
+YF_DEV_TIMEOUT = 16
+
+ERROR_NAMES = {
+    YF_E_INVALID: "YF_E_INVALID", YF_E_UNSUPPORTED: "YF_E_UNSUPPORTED", YF_E_NOMEM: "YF_E_NOMEM",
+    YF_E_CUDA: "YF_E_CUDA", YF_E_RANGE: "YF_E_RANGE", YF_E_WORKSPACE: "YF_E_WORKSPACE", YF_E_STATE: "YF_E_STATE",
+}
+
+
+class YfError(RuntimeError):
+    """A non-zero return code of the C ABI, with yf_last_error()'s message."""
+
+    def __init__(self, code: int, func: str, msg: str):
+        super().__init__(f"{func}: {ERROR_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class PoolDesc(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int32), ("n_pages", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("group_size", ctypes.c_int32),
+        ("device", ctypes.c_int32), ("reserved", ctypes.c_int32), ("device_mem", ctypes.c_void_p),
+    ]
+
+
+_i32, _u32, _sz, _vp, _f32 = ctypes.c_int32, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float
+_ci = ctypes.c_int
+_P_i32 = ctypes.POINTER(ctypes.c_int32)
+
+# name -> (restype, argtypes); every function of include/yfattn.h
+SIGNATURES = {
+    "yf_last_error": (ctypes.c_char_p, []),
+    "yf_abi_version": (_ci, []),
+    "yf_pool_page_head_bytes": (_sz, [_vp]),
+    "yf_pool_bytes": (_sz, [_vp]),
+    "yf_pool_tile_offset": (ctypes.c_int64, [_vp, _ci, _ci, _ci]),
+    "yf_pool_scale_offset": (ctypes.c_int64, [_vp, _ci, _ci, _ci]),
+    "yf_pool_create": (_ci, [_vp, ctypes.POINTER(_vp)]),
+    "yf_pool_destroy": (_ci, [_vp]),
+    "yf_pool_get_desc": (_ci, [_vp, _vp]),
+    "yf_pool_layer_ptr": (_ci, [_vp, _i32, ctypes.POINTER(_vp)]),
+    "yf_pool_alloc_pages": (_ci, [_vp, _i32, _vp]),
+    "yf_pool_retain_pages": (_ci, [_vp, _i32, _vp]),
+    "yf_pool_free_pages": (_ci, [_vp, _i32, _vp]),
+    "yf_pool_free_count": (_ci, [_vp, _P_i32]),
+    "yf_pool_refcount": (_ci, [_vp, _i32, _P_i32]),
+    "yf_pool_status": (_ci, [_vp, ctypes.POINTER(_u32), _ci]),
+    "yf_kv_append_paged": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
+    "yf_kv_append_paged_multi": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "yf_attn_workspace_size": (_sz, [_vp, _i32, _i32, _i32, _i32]),
+    "yf_attn_decode": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "yf_attn_prefill": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
+                              _vp]),
+    "yf_pool_export_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
+    "yf_pool_restore_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libyfattn.so (no fallback) and declares every exported signature."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built: run `python qwen36-server_b200/build.py` "
+                              "or __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int, func: str) -> None:
+    if rc != YF_OK:
+        msg = lib().yf_last_error()
+        raise YfError(rc, func, msg.decode() if msg else "")
+
+
+def call(name: str, *args) -> None:
+    """Calls an int-returning entry point and raises YfError on a non-zero code."""
+    check(getattr(lib(), name)(*args), name)

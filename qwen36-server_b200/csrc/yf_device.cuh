@@ -1,0 +1,136 @@
+// Device-side helpers: shared-memory addressing, mbarriers, 1-D bulk copies
+// (TMA, no multicast), warp MMA, and int8 -> f16 unpacking.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace yf {
+
+// Iterations of a bounded mbarrier wait before it gives up (each try_wait
+// itself suspends for a hardware-defined interval), i.e. seconds, not a hang.
+constexpr uint32_t kMaxWaitIters = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the given phase parity; false if it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMaxWaitIters; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    uint64_t g;
+    asm volatile("cvta.to.global.u64 %0, %1;" : "=l"(g) : "l"(src));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(g), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_u32(p)));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(const void* p) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lds32(const void* p) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
+    return v;
+}
+
+// D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col).
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Signed int8 bytes -> exact f16 pairs.  The byte x is biased to x+128,
+// placed as the low mantissa byte of the f16 0x6400 (= 1024), which gives
+// exactly 1024 + x + 128; subtracting 1152 leaves x.
+__device__ __forceinline__ uint32_t h2_sub_1152(uint32_t v) {
+    uint32_t r;
+    const uint32_t k = 0x64806480u;  // (1152, 1152) in f16
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(k));
+    return r;
+}
+// bytes 0,1 of a biased word -> f16x2 (lo = byte 0)
+__device__ __forceinline__ uint32_t s8lo_to_h2(uint32_t wb) {
+    return h2_sub_1152(__byte_perm(wb, 0x64646464u, 0x4140));
+}
+// bytes 2,3 of a biased word -> f16x2 (lo = byte 2)
+__device__ __forceinline__ uint32_t s8hi_to_h2(uint32_t wb) {
+    return h2_sub_1152(__byte_perm(wb, 0x64646464u, 0x4342));
+}
+__device__ __forceinline__ uint32_t bias8(uint32_t w) { return w ^ 0x80808080u; }
+
+__device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// {lo, hi} floats -> f16x2 with lo in the low half (round to nearest even).
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+}  // namespace yf

@@ -1,0 +1,98 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "yfattn.h"
+
+namespace yf {
+
+// Tokens per tile: the unit one warp consumes per pipeline step.
+constexpr int kTileTokens = 16;
+
+// Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).
+struct TileGeom {
+    int D;       // head_dim
+    int NB;      // scale groups per row (D / group_size)
+    int tile;    // whole tile
+    int ks_off;  // K scales
+    int v_off;   // V values
+    int vs_off;  // V scales
+};
+
+inline TileGeom tile_geom(int D, int NB) {
+    TileGeom g;
+    g.D = D;
+    g.NB = NB;
+    g.ks_off = 16 * D;
+    g.v_off = 16 * D + 32 * NB;
+    g.vs_off = 32 * D + 32 * NB;
+    g.tile = 32 * D + 64 * NB;
+    return g;
+}
+
+}  // namespace yf
+
+struct yf_pool {
+    yf_pool_desc desc;
+    uint8_t* base = nullptr;  // device: [n_layers][n_pages][n_kv_heads][page_head_bytes]
+    bool owns_mem = false;
+    size_t bytes = 0;
+    size_t tile_bytes = 0;
+    size_t page_head_bytes = 0;
+    size_t page_bytes = 0;   // all kv heads of one page in one layer
+    size_t layer_bytes = 0;
+    uint32_t* d_status = nullptr;  // device status word (YF_DEV_* bits)
+    int sm_count = 148;
+    std::vector<int32_t> refcount;
+    std::vector<int32_t> free_stack;  // LIFO of free page ids
+};
+
+namespace yf {
+
+// Records a message for yf_last_error() and returns code.
+int fail(int code, const char* fmt, ...);
+// Maps a CUDA error to YF_E_CUDA with the call site in the message.
+int cuda_fail(cudaError_t e, const char* what);
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Split-KV plan of one attention call; identical in the workspace query and
+// the launch so that the caller's workspace always fits.
+struct SplitPlan {
+    int rows_per_cta;  // query rows (q heads x query positions) of one CTA: 8 or 16
+    int n_row_groups;  // ceil(G * max_seqlen_q / rows_per_cta)
+    int chunk_tiles;   // 16-token tiles per CTA
+    int max_chunks;    // ceil(max tiles / chunk_tiles)
+    size_t ws_bytes;   // partial O + lse
+};
+
+SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k);
+
+struct AttnArgs {
+    const yf_pool* pool;
+    int layer;
+    const __half* q;
+    int n_q_heads;
+    const uint32_t* cu_q;  // nullptr for decode (entry b owns query row b)
+    const uint32_t* cu_k;
+    const uint32_t* block_table;
+    int max_blocks;
+    int batch;
+    int max_seqlen_q;
+    int max_seqlen_k;
+    float scale;
+    __half* out;
+    void* workspace;
+    size_t workspace_bytes;
+    cudaStream_t stream;
+};
+
+// Split-KV attention for decode / verify / small query blocks (yf_decode.cu).
+int launch_splitkv(const AttnArgs& a, const SplitPlan& plan);
+
+}  // namespace yf

@@ -1,0 +1,384 @@
+// Pool lifetime, page allocator, snapshot export/restore, argument checks and
+// the attention entry points of the C ABI (include/yfattn.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "yf_internal.h"
+
+namespace {
+thread_local char g_err[512] = "";
+}
+
+namespace yf {
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(YF_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static int check_desc(const yf_pool_desc* d) {
+    if (!d) return fail(YF_E_INVALID, "desc is null");
+    if (d->n_layers < 1 || d->n_pages < 1 || d->n_kv_heads < 1)
+        return fail(YF_E_INVALID, "n_layers, n_pages and n_kv_heads must be >= 1");
+    if (d->head_dim != 128 && d->head_dim != 256)
+        return fail(YF_E_UNSUPPORTED, "head_dim %d: built for 128 and 256", d->head_dim);
+    if (d->page_size != 16 && d->page_size != 64)
+        return fail(YF_E_UNSUPPORTED, "page_size %d: built for 16 and 64", d->page_size);
+    if (d->group_size != 32 && d->group_size != d->head_dim)
+        return fail(YF_E_UNSUPPORTED, "group_size %d: built for 32 and head_dim", d->group_size);
+    return YF_OK;
+}
+
+static size_t tile_bytes_of(const yf_pool_desc* d) {
+    return tile_geom(d->head_dim, d->head_dim / d->group_size).tile;
+}
+
+// Splits the tile range of every (entry, kv head, row group) into chunks so
+// that the grid covers the SMs several times over; the last chunk of each
+// unit is partial, so more, smaller chunks keep the tail short.
+SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k) {
+    SplitPlan p;
+    const int H = pool->desc.n_kv_heads;
+    const int G = n_q_heads / H;
+    const int rows = G * (max_seqlen_q > 0 ? max_seqlen_q : 1);
+    p.rows_per_cta = (rows <= 8 || pool->desc.head_dim > 128) ? 8 : 16;
+    p.n_row_groups = (rows + p.rows_per_cta - 1) / p.rows_per_cta;
+    const int tiles = (max_seqlen_k + kTileTokens - 1) / kTileTokens;
+    const long long units = (long long)batch * H * p.n_row_groups;
+    const long long target = (long long)pool->sm_count * 16;
+    const char* ov = getenv("YF_CHUNK_TILES");  // host-side tuning override
+    int chunk;
+    if (ov && atoi(ov) > 0) {
+        chunk = atoi(ov);
+    } else {
+        long long c = (units * tiles + target - 1) / target;
+        if (c < 8) c = 8;
+        c = (c + 3) / 4 * 4;
+        if (c > (1 << 20)) c = 1 << 20;
+        chunk = (int)c;
+    }
+    p.chunk_tiles = chunk;
+    p.max_chunks = tiles > 0 ? (tiles + chunk - 1) / chunk : 1;
+    if (p.max_chunks <= 1) {
+        p.ws_bytes = 0;
+    } else {
+        const size_t items = (size_t)units * p.max_chunks;
+        p.ws_bytes = items * p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
+    }
+    return p;
+}
+
+}  // namespace yf
+
+using namespace yf;
+
+extern "C" {
+
+const char* yf_last_error(void) { return g_err; }
+int yf_abi_version(void) { return YFATTN_ABI_VERSION; }
+
+size_t yf_pool_page_head_bytes(const yf_pool_desc* d) {
+    if (check_desc(d) != YF_OK) return 0;
+    return (size_t)(d->page_size / kTileTokens) * tile_bytes_of(d);
+}
+
+size_t yf_pool_bytes(const yf_pool_desc* d) {
+    const size_t phb = yf_pool_page_head_bytes(d);
+    if (!phb) return 0;
+    return (size_t)d->n_layers * d->n_pages * d->n_kv_heads * phb;
+}
+
+int64_t yf_pool_tile_offset(const yf_pool_desc* d, int is_v, int t, int dim) {
+    if (check_desc(d) != YF_OK || t < 0 || t >= 16 || dim < 0 || dim >= d->head_dim) return -1;
+    const TileGeom g = tile_geom(d->head_dim, d->head_dim / d->group_size);
+    if (!is_v) {
+        const int b = dim / 32, r = dim % 32;
+        return (int64_t)b * 512 + ((t % 8) * 4 + r / 8) * 16 + (t / 8) * 8 + r % 8;
+    }
+    const int m = dim / 16, i = dim % 16;
+    const int tig = (t % 8) / 2, j = (t & 1) * 2 + t / 8;
+    return (int64_t)g.v_off + (m / 2) * 512 + ((i % 8) * 4 + tig) * 16 + (m % 2) * 8 + (i / 8) * 4 + j;
+}
+
+int64_t yf_pool_scale_offset(const yf_pool_desc* d, int is_v, int t, int group) {
+    if (check_desc(d) != YF_OK || t < 0 || t >= 16) return -1;
+    const int NB = d->head_dim / d->group_size;
+    if (group < 0 || group >= NB) return -1;
+    const TileGeom g = tile_geom(d->head_dim, NB);
+    if (!is_v) return (int64_t)g.ks_off + 2 * (((t % 8) * 2 + t / 8) * NB + group);
+    const int tig = (t % 8) / 2, j = (t & 1) * 2 + t / 8;
+    return (int64_t)g.vs_off + 2 * ((tig * NB + group) * 4 + j);
+}
+
+int yf_pool_create(const yf_pool_desc* desc, yf_pool** out_pool) {
+    if (!out_pool) return fail(YF_E_INVALID, "out_pool is null");
+    *out_pool = nullptr;
+    const int rc = check_desc(desc);
+    if (rc) return rc;
+    yf_pool* p = new (std::nothrow) yf_pool();
+    if (!p) return fail(YF_E_NOMEM, "host allocation failed");
+    p->desc = *desc;
+    p->tile_bytes = tile_bytes_of(desc);
+    p->page_head_bytes = yf_pool_page_head_bytes(desc);
+    p->page_bytes = p->page_head_bytes * desc->n_kv_heads;
+    p->layer_bytes = p->page_bytes * desc->n_pages;
+    p->bytes = p->layer_bytes * desc->n_layers;
+    p->refcount.assign(desc->n_pages, 0);
+    p->free_stack.resize(desc->n_pages);
+    for (int i = 0; i < desc->n_pages; ++i) p->free_stack[i] = desc->n_pages - 1 - i;  // pops 0,1,2,...
+    if (desc->device < 0) {  // host-only pool: the page allocator without device memory
+        p->desc.device_mem = nullptr;
+        *out_pool = p;
+        return YF_OK;
+    }
+    cudaError_t e = cudaSetDevice(desc->device);
+    if (e != cudaSuccess) {
+        delete p;
+        return cuda_fail(e, "cudaSetDevice");
+    }
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, desc->device) == cudaSuccess && sms > 0)
+        p->sm_count = sms;
+    if (desc->device_mem) {
+        if (!aligned(desc->device_mem, 256)) {
+            delete p;
+            return fail(YF_E_INVALID, "device_mem must be 256-byte aligned");
+        }
+        p->base = static_cast<uint8_t*>(desc->device_mem);
+        p->owns_mem = false;
+    } else {
+        e = cudaMalloc(&p->base, p->bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            delete p;
+            return fail(YF_E_NOMEM, "cudaMalloc of %zu pool bytes: %s", p->bytes, cudaGetErrorString(e));
+        }
+        p->owns_mem = true;
+    }
+    e = cudaMalloc(&p->d_status, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(p->base, 0, p->bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        if (p->owns_mem) cudaFree(p->base);
+        if (p->d_status) cudaFree(p->d_status);
+        delete p;
+        return cuda_fail(e, "pool initialisation");
+    }
+    *out_pool = p;
+    return YF_OK;
+}
+
+int yf_pool_destroy(yf_pool* pool) {
+    if (!pool) return YF_OK;
+    if (pool->base || pool->d_status) {
+        cudaSetDevice(pool->desc.device);
+        if (pool->owns_mem && pool->base) cudaFree(pool->base);
+        if (pool->d_status) cudaFree(pool->d_status);
+    }
+    delete pool;
+    return YF_OK;
+}
+
+int yf_pool_get_desc(const yf_pool* pool, yf_pool_desc* out) {
+    if (!pool || !out) return fail(YF_E_INVALID, "null argument");
+    *out = pool->desc;
+    out->device_mem = pool->base;
+    return YF_OK;
+}
+
+int yf_pool_layer_ptr(const yf_pool* pool, int32_t layer, void** out_ptr) {
+    if (!pool || !out_ptr) return fail(YF_E_INVALID, "null argument");
+    if (!pool->base) return fail(YF_E_INVALID, "host-only pool has no device memory");
+    if (layer < 0 || layer >= pool->desc.n_layers) return fail(YF_E_RANGE, "layer %d out of range", layer);
+    *out_ptr = pool->base + (size_t)layer * pool->layer_bytes;
+    return YF_OK;
+}
+
+int yf_pool_alloc_pages(yf_pool* pool, int32_t n, int32_t* out) {
+    if (!pool || n < 0 || (n > 0 && !out)) return fail(YF_E_INVALID, "bad alloc arguments");
+    if ((size_t)n > pool->free_stack.size())
+        return fail(YF_E_NOMEM, "requested %d pages, %zu free", n, pool->free_stack.size());
+    for (int i = 0; i < n; ++i) {
+        const int32_t pg = pool->free_stack.back();
+        pool->free_stack.pop_back();
+        pool->refcount[pg] = 1;
+        out[i] = pg;
+    }
+    return YF_OK;
+}
+
+int yf_pool_retain_pages(yf_pool* pool, int32_t n, const int32_t* pages) {
+    if (!pool || n < 0 || (n > 0 && !pages)) return fail(YF_E_INVALID, "bad retain arguments");
+    for (int i = 0; i < n; ++i) {
+        if (pages[i] < 0 || pages[i] >= pool->desc.n_pages) return fail(YF_E_RANGE, "page %d out of range", pages[i]);
+        if (pool->refcount[pages[i]] <= 0) return fail(YF_E_STATE, "retain of free page %d", pages[i]);
+    }
+    for (int i = 0; i < n; ++i) pool->refcount[pages[i]] += 1;
+    return YF_OK;
+}
+
+int yf_pool_free_pages(yf_pool* pool, int32_t n, const int32_t* pages) {
+    if (!pool || n < 0 || (n > 0 && !pages)) return fail(YF_E_INVALID, "bad free arguments");
+    // Validate the whole list first (counting repeats) so that a bad list changes nothing.
+    std::vector<int32_t> drops;
+    drops.reserve(n);
+    for (int i = 0; i < n; ++i) {
+        const int32_t pg = pages[i];
+        if (pg < 0 || pg >= pool->desc.n_pages) return fail(YF_E_RANGE, "page %d out of range", pg);
+        int seen = 0;
+        for (int32_t x : drops) seen += (x == pg);
+        if (pool->refcount[pg] - seen <= 0) return fail(YF_E_STATE, "free of free page %d", pg);
+        drops.push_back(pg);
+    }
+    for (int32_t pg : drops)
+        if (--pool->refcount[pg] == 0) pool->free_stack.push_back(pg);
+    return YF_OK;
+}
+
+int yf_pool_free_count(const yf_pool* pool, int32_t* out_free) {
+    if (!pool || !out_free) return fail(YF_E_INVALID, "null argument");
+    *out_free = (int32_t)pool->free_stack.size();
+    return YF_OK;
+}
+
+int yf_pool_refcount(const yf_pool* pool, int32_t page, int32_t* out) {
+    if (!pool || !out) return fail(YF_E_INVALID, "null argument");
+    if (page < 0 || page >= pool->desc.n_pages) return fail(YF_E_RANGE, "page %d out of range", page);
+    *out = pool->refcount[page];
+    return YF_OK;
+}
+
+int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear) {
+    if (!pool || !out_bits) return fail(YF_E_INVALID, "null argument");
+    if (!pool->d_status) return fail(YF_E_INVALID, "host-only pool has no device status");
+    cudaSetDevice(pool->desc.device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(out_bits, pool->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(pool->d_status, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "status read");
+    return YF_OK;
+}
+
+// Page copies between the pool and a snapshot buffer: one cudaMemcpyAsync per
+// run of consecutive page ids.
+static int copy_pages(yf_pool* pool, int32_t layer, int32_t n, const int32_t* pages, uint8_t* ext,
+                      bool to_pool, void* stream) {
+    if (!pool || n < 0 || (n > 0 && (!pages || !ext))) return fail(YF_E_INVALID, "bad page-copy arguments");
+    if (!pool->base) return fail(YF_E_INVALID, "host-only pool has no device memory");
+    if (layer < 0 || layer >= pool->desc.n_layers) return fail(YF_E_RANGE, "layer %d out of range", layer);
+    for (int i = 0; i < n; ++i)
+        if (pages[i] < 0 || pages[i] >= pool->desc.n_pages) return fail(YF_E_RANGE, "page %d out of range", pages[i]);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t* lb = pool->base + (size_t)layer * pool->layer_bytes;
+    const size_t pb = pool->page_bytes;
+    int i = 0;
+    while (i < n) {
+        int j = i + 1;
+        while (j < n && pages[j] == pages[j - 1] + 1) ++j;
+        uint8_t* dev = lb + (size_t)pages[i] * pb;
+        uint8_t* ext_i = ext + (size_t)i * pb;
+        const cudaError_t e = to_pool ? cudaMemcpyAsync(dev, ext_i, (size_t)(j - i) * pb, cudaMemcpyDefault, s)
+                                      : cudaMemcpyAsync(ext_i, dev, (size_t)(j - i) * pb, cudaMemcpyDefault, s);
+        if (e != cudaSuccess) return cuda_fail(e, "page copy");
+        i = j;
+    }
+    return YF_OK;
+}
+
+int yf_pool_export_pages(yf_pool* pool, int32_t layer, int32_t n, const int32_t* pages, void* dst, void* stream) {
+    return copy_pages(pool, layer, n, pages, static_cast<uint8_t*>(dst), false, stream);
+}
+
+int yf_pool_restore_pages(yf_pool* pool, int32_t layer, int32_t n, const int32_t* pages, const void* src,
+                          void* stream) {
+    return copy_pages(pool, layer, n, pages, static_cast<uint8_t*>(const_cast<void*>(src)), true, stream);
+}
+
+// ---- attention entry points ------------------------------------------------
+
+static int check_attn(const yf_pool* pool, int32_t layer, const void* q, int32_t hq, const void* cu_k,
+                      const void* bt, int32_t max_blocks, int32_t batch, int32_t max_q, int32_t max_k,
+                      float scale, const void* out) {
+    if (!pool) return fail(YF_E_INVALID, "pool is null");
+    if (!pool->base) return fail(YF_E_INVALID, "host-only pool has no device memory");
+    if (batch < 0) return fail(YF_E_INVALID, "batch %d < 0", batch);
+    if (batch == 0) return YF_OK;
+    if (!q || !cu_k || !bt || !out) return fail(YF_E_INVALID, "null device pointer");
+    if (!aligned(q, 16) || !aligned(out, 16)) return fail(YF_E_INVALID, "q and out must be 16-byte aligned");
+    if (layer < 0 || layer >= pool->desc.n_layers) return fail(YF_E_RANGE, "layer %d out of range", layer);
+    const int H = pool->desc.n_kv_heads;
+    if (hq < H || hq % H != 0) return fail(YF_E_INVALID, "n_q_heads %d is not a multiple of n_kv_heads %d", hq, H);
+    if (max_blocks < 1) return fail(YF_E_INVALID, "max_blocks %d < 1", max_blocks);
+    if (max_q < 1) return fail(YF_E_INVALID, "max_seqlen_q %d < 1", max_q);
+    if (max_k < 0) return fail(YF_E_INVALID, "max_seqlen_k %d < 0", max_k);
+    if ((long long)max_k > (long long)max_blocks * pool->desc.page_size)
+        return fail(YF_E_RANGE, "max_seqlen_k %d exceeds max_blocks*page_size %lld", max_k,
+                    (long long)max_blocks * pool->desc.page_size);
+    if (!(scale == scale) || scale <= 0.0f || scale > 1e30f) return fail(YF_E_INVALID, "scale must be finite and > 0");
+    if (batch > 65535) return fail(YF_E_UNSUPPORTED, "batch %d > 65535", batch);
+    if ((long long)H * ((long long)(hq / H) * max_q + 7) / 8 > 65535)
+        return fail(YF_E_UNSUPPORTED, "too many query rows per kv head for one launch");
+    return YF_OK;
+}
+
+size_t yf_attn_workspace_size(const yf_pool* pool, int32_t hq, int32_t batch, int32_t max_q, int32_t max_k) {
+    if (!pool || batch <= 0 || hq < pool->desc.n_kv_heads || hq % pool->desc.n_kv_heads) return 0;
+    return plan_split(pool, hq, batch, max_q, max_k).ws_bytes;
+}
+
+static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,
+                    const uint32_t* cu_k, const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_q,
+                    int32_t max_k, float scale, void* out, void* ws, size_t ws_bytes, void* stream) {
+    const int rc = check_attn(pool, layer, q, hq, cu_k, bt, max_blocks, batch, max_q, max_k, scale, out);
+    if (rc || batch == 0) return rc;
+    const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k);
+    if (plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
+        return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", plan.ws_bytes,
+                    ws ? ws_bytes : (size_t)0);
+    AttnArgs a;
+    a.pool = pool;
+    a.layer = layer;
+    a.q = static_cast<const __half*>(q);
+    a.n_q_heads = hq;
+    a.cu_q = cu_q;
+    a.cu_k = cu_k;
+    a.block_table = bt;
+    a.max_blocks = max_blocks;
+    a.batch = batch;
+    a.max_seqlen_q = max_q;
+    a.max_seqlen_k = max_k;
+    a.scale = scale;
+    a.out = static_cast<__half*>(out);
+    a.workspace = ws;
+    a.workspace_bytes = ws_bytes;
+    a.stream = static_cast<cudaStream_t>(stream);
+    return launch_splitkv(a, plan);
+}
+
+int yf_attn_decode(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_k,
+                   const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_k, float scale, void* out,
+                   void* ws, size_t ws_bytes, void* stream) {
+    return run_attn(pool, layer, q, hq, nullptr, cu_k, bt, max_blocks, batch, 1, max_k, scale, out, ws, ws_bytes,
+                    stream);
+}
+
+int yf_attn_prefill(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,
+                    const uint32_t* cu_k, const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_q,
+                    int32_t max_k, float scale, void* out, void* ws, size_t ws_bytes, void* stream) {
+    if (batch > 0 && !cu_q) return fail(YF_E_INVALID, "cu_seqlens_q is null");
+    return run_attn(pool, layer, q, hq, cu_q, cu_k, bt, max_blocks, batch, max_q, max_k, scale, out, ws, ws_bytes,
+                    stream);
+}
+
+}  // extern "C"

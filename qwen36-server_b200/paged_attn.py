@@ -1,0 +1,285 @@
+"""Host-side mirror of the engine's paged-KV attention operator surface.
+
+The names follow the reference's call sites so that engine-side code and the
+parity tests read like the reference's own:
+
+  * ``PagedKvPool``                 -- real::paged_kv_cuda's PagedKvPool
+                                       (docs/plans/2026-08-27-tiered-kv-cache.md:352-353),
+                                       plus a free-list page allocator with refcounts
+  * ``kv_append_paged``             -- kv_append_paged_f16, one row per slot (fork quantized.cu:6996)
+  * ``launch_append_multi``         -- T contiguous rows per slot (fork quantized.cu:7040)
+  * ``dispatch_flash_decode_paged`` -- src/bin/decode_gqa_probe.rs:26,40-46 (q, pool, lens, table, scale)
+  * ``forward_attn_prefill_paged``  -- causal chunk "row i sees 0..kv0+i"
+                                       (docs/plans/2026-08-27-mtp-cuda-graphs.md:132,244-248)
+  * ``forward_verify_paged``        -- MTP verify of k draft rows (same doc, :279-284, :537-541)
+  * ``PagedKvPool.export_pages`` / ``restore_pages`` -- StateSnapshot::to_host / to_device
+                                       of int8 pages + scales (src/prefix_cache.rs:71-91, :361)
+
+Tensors are torch tensors on the pool's device; torch only supplies device
+memory and the current stream.  Every call goes through libyfattn.so; errors
+raise ``YfError`` (the reference's calls return candle_core::Error).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Sequence
+
+import torch
+
+from . import _abi
+from ._abi import YfError, call, lib
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _i32(t, device) -> torch.Tensor:
+    """Block tables, lengths and positions travel as int32 (read as uint32 where the ABI says so)."""
+    if not torch.is_tensor(t):
+        t = torch.as_tensor(t)
+    if t.dtype != torch.int32:
+        t = t.to(torch.int32)
+    return t.to(device).contiguous()
+
+
+class PagedKvPool:
+    """The persistent Q8_0 KV pool of one model: ``n_layers`` planes of ``n_pages`` pages.
+
+    ``device=None`` builds a host-only pool that carries only the page allocator.
+    """
+
+    def __init__(self, n_layers: int, n_pages: int, n_kv_heads: int, head_dim: int, page_size: int = 16,
+                 group_size: int = 32, device: Optional[int] = 0):
+        self.desc = _abi.PoolDesc(n_layers, n_pages, n_kv_heads, head_dim, page_size, group_size,
+                                  -1 if device is None else int(device), 0, None)
+        self.device = None if device is None else torch.device("cuda", int(device))
+        h = ctypes.c_void_p()
+        call("yf_pool_create", ctypes.byref(self.desc), ctypes.byref(h))
+        self._h = h
+        self._ws = None
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    n_layers = property(lambda self: self.desc.n_layers)
+    n_pages = property(lambda self: self.desc.n_pages)
+    n_kv_heads = property(lambda self: self.desc.n_kv_heads)
+    head_dim = property(lambda self: self.desc.head_dim)
+    page_size = property(lambda self: self.desc.page_size)
+    group_size = property(lambda self: self.desc.group_size)
+
+    @property
+    def page_head_bytes(self) -> int:
+        return lib().yf_pool_page_head_bytes(ctypes.byref(self.desc))
+
+    @property
+    def page_bytes(self) -> int:
+        return self.page_head_bytes * self.n_kv_heads
+
+    @property
+    def bytes(self) -> int:
+        return lib().yf_pool_bytes(ctypes.byref(self.desc))
+
+    def layer_ptr(self, layer: int) -> int:
+        p = ctypes.c_void_p()
+        call("yf_pool_layer_ptr", self._h, layer, ctypes.byref(p))
+        return p.value or 0
+
+    def layer_bytes_view(self, layer: int) -> torch.Tensor:
+        """A uint8 tensor aliasing one layer plane (device memory owned by the pool)."""
+        return _alias_u8(self.layer_ptr(layer), self.n_pages * self.page_bytes, self.device)
+
+    # -- allocator ------------------------------------------------------------------
+    def alloc_pages(self, n: int) -> list:
+        out = (ctypes.c_int32 * max(n, 1))()
+        call("yf_pool_alloc_pages", self._h, n, out)
+        return list(out[:n])
+
+    def retain_pages(self, pages: Sequence[int]) -> None:
+        arr = (ctypes.c_int32 * max(len(pages), 1))(*pages)
+        call("yf_pool_retain_pages", self._h, len(pages), arr)
+
+    def free_pages(self, pages: Sequence[int]) -> None:
+        arr = (ctypes.c_int32 * max(len(pages), 1))(*pages)
+        call("yf_pool_free_pages", self._h, len(pages), arr)
+
+    def free_count(self) -> int:
+        v = ctypes.c_int32()
+        call("yf_pool_free_count", self._h, ctypes.byref(v))
+        return v.value
+
+    def refcount(self, page: int) -> int:
+        v = ctypes.c_int32()
+        call("yf_pool_refcount", self._h, page, ctypes.byref(v))
+        return v.value
+
+    def status(self, clear: bool = True) -> int:
+        """Device status bits (YF_DEV_*); synchronizes the device."""
+        v = ctypes.c_uint32()
+        call("yf_pool_status", self._h, ctypes.byref(v), 1 if clear else 0)
+        return v.value
+
+    # -- snapshots ------------------------------------------------------------------
+    def export_pages(self, layer: int, pages: Sequence[int], out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Bytes of ``pages`` (one layer, all kv heads) back to back; pinned host memory by default."""
+        n = len(pages)
+        if out is None:
+            out = torch.empty(n * self.page_bytes, dtype=torch.uint8, pin_memory=True)
+        arr = (ctypes.c_int32 * max(n, 1))(*pages)
+        call("yf_pool_export_pages", self._h, layer, n, arr, ctypes.c_void_p(out.data_ptr()), _stream(self.device))
+        return out
+
+    def restore_pages(self, layer: int, pages: Sequence[int], snapshot: torch.Tensor) -> None:
+        """Copies a snapshot made by export_pages into ``pages`` (no requantization)."""
+        n = len(pages)
+        if snapshot.numel() * snapshot.element_size() < n * self.page_bytes:
+            raise YfError(_abi.YF_E_INVALID, "restore_pages", "snapshot smaller than the page list")
+        arr = (ctypes.c_int32 * max(n, 1))(*pages)
+        call("yf_pool_restore_pages", self._h, layer, n, arr, ctypes.c_void_p(snapshot.data_ptr()),
+             _stream(self.device))
+
+    # -- workspace ------------------------------------------------------------------
+    def workspace_size(self, n_q_heads: int, batch: int, max_seqlen_q: int, max_seqlen_k: int) -> int:
+        return lib().yf_attn_workspace_size(self._h, n_q_heads, batch, max_seqlen_q, max_seqlen_k)
+
+    def workspace(self, nbytes: int) -> Optional[torch.Tensor]:
+        """A cached device buffer of at least ``nbytes`` (grown, never shrunk)."""
+        if nbytes <= 0:
+            return None
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().yf_pool_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _alias_u8(ptr: int, n: int, device: torch.device) -> torch.Tensor:
+    """Wraps foreign device memory as a uint8 tensor without copying (lifetime: the owner's)."""
+
+    class _Holder:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 2,
+                                    "strides": None}
+
+    return torch.as_tensor(_Holder(), device=device)
+
+
+# ---- KV write ------------------------------------------------------------------------
+
+def _check_rows(pool: PagedKvPool, k: torch.Tensor, v: torch.Tensor) -> None:
+    if k.dtype != torch.float16 or v.dtype != torch.float16:
+        raise YfError(_abi.YF_E_INVALID, "kv write", "k and v must be float16")
+    if k.shape != v.shape or k.dim() != 3 or k.shape[1] != pool.n_kv_heads or k.shape[2] != pool.head_dim:
+        raise YfError(_abi.YF_E_INVALID, "kv write", f"k/v must be [rows, {pool.n_kv_heads}, {pool.head_dim}]")
+    if not (k.is_contiguous() and v.is_contiguous()):
+        raise YfError(_abi.YF_E_INVALID, "kv write", "k and v must be contiguous")
+
+
+def kv_append_paged(pool: PagedKvPool, layer: int, k: torch.Tensor, v: torch.Tensor, pos, block_table) -> None:
+    """Quantize one new K/V row per batch entry into its page: k, v f16 [B, Hkv, D]; pos int [B]."""
+    _check_rows(pool, k, v)
+    pos = _i32(pos, pool.device)
+    bt = _i32(block_table, pool.device)
+    call("yf_kv_append_paged", pool.handle, layer, _ptr(k), _ptr(v), _ptr(pos), _ptr(bt), bt.shape[1], k.shape[0],
+         _stream(pool.device))
+
+
+def launch_append_multi(pool: PagedKvPool, layer: int, k: torch.Tensor, v: torch.Tensor, cu_rows, start_pos,
+                        block_table, max_rows: Optional[int] = None) -> None:
+    """Quantize T contiguous rows per entry: k, v f16 [total_rows, Hkv, D]; entry b's rows
+    cu_rows[b]..cu_rows[b+1]-1 go to positions start_pos[b]+i."""
+    _check_rows(pool, k, v)
+    if max_rows is None:
+        max_rows = _max_len(cu_rows)
+    cu = _i32(cu_rows, pool.device)
+    sp = _i32(start_pos, pool.device)
+    bt = _i32(block_table, pool.device)
+    call("yf_kv_append_paged_multi", pool.handle, layer, _ptr(k), _ptr(v), _ptr(cu), _ptr(sp), _ptr(bt),
+         bt.shape[1], cu.numel() - 1, max_rows, _stream(pool.device))
+
+
+# ---- attention -----------------------------------------------------------------------
+
+def _max_len(cu) -> int:
+    c = torch.as_tensor(cu).to("cpu", torch.int64)
+    return int((c[1:] - c[:-1]).max()) if c.numel() > 1 else 0
+
+
+def _ws_args(pool: PagedKvPool, workspace: Optional[torch.Tensor], nbytes: int):
+    if workspace is None:
+        workspace = pool.workspace(nbytes)
+    size = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    return _ptr(workspace), size
+
+
+def dispatch_flash_decode_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, lens, table, scale: float,
+                                max_seqlen_k: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                                workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Batched paged decode attention.  q f16 [B, Hq, D]; lens = cu_seqlens_k [B+1] (as the
+    probe's ``lens``); table [B, max_blocks].  Returns f16 [B, Hq, D]."""
+    B, Hq, D = q.shape
+    if q.dtype != torch.float16 or D != pool.head_dim or not q.is_contiguous():
+        raise YfError(_abi.YF_E_INVALID, "dispatch_flash_decode_paged", "q must be contiguous f16 [B, Hq, D]")
+    if max_seqlen_k is None:
+        max_seqlen_k = _max_len(lens)
+    lens = _i32(lens, pool.device)
+    table = _i32(table, pool.device)
+    if out is None:
+        out = torch.empty_like(q)
+    ws, ws_bytes = _ws_args(pool, workspace, pool.workspace_size(Hq, B, 1, max_seqlen_k))
+    call("yf_attn_decode", pool.handle, layer, _ptr(q), Hq, _ptr(lens), _ptr(table), table.shape[1], B,
+         max_seqlen_k, ctypes.c_float(scale), _ptr(out), ws, ws_bytes, _stream(pool.device))
+    return out
+
+
+def forward_attn_prefill_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, cu_seqlens_q, cu_seqlens_k, table,
+                               scale: float, max_seqlen_q: Optional[int] = None,
+                               max_seqlen_k: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                               workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal attention of query blocks against the pool.  q f16 [total_q, Hq, D]; entry b's
+    rows cu_seqlens_q[b].. see keys 0..Tk_b-Tq_b+i (its new K/V rows must already be written)."""
+    T, Hq, D = q.shape
+    if q.dtype != torch.float16 or D != pool.head_dim or not q.is_contiguous():
+        raise YfError(_abi.YF_E_INVALID, "forward_attn_prefill_paged", "q must be contiguous f16 [T, Hq, D]")
+    if max_seqlen_q is None:
+        max_seqlen_q = _max_len(cu_seqlens_q)
+    if max_seqlen_k is None:
+        max_seqlen_k = _max_len(cu_seqlens_k)
+    max_seqlen_q = max(int(max_seqlen_q), 1)
+    cq = _i32(cu_seqlens_q, pool.device)
+    ck = _i32(cu_seqlens_k, pool.device)
+    table = _i32(table, pool.device)
+    B = ck.numel() - 1
+    if out is None:
+        out = torch.empty_like(q)
+    ws, ws_bytes = _ws_args(pool, workspace, pool.workspace_size(Hq, B, max_seqlen_q, max_seqlen_k))
+    call("yf_attn_prefill", pool.handle, layer, _ptr(q), Hq, _ptr(cq), _ptr(ck), _ptr(table), table.shape[1], B,
+         max_seqlen_q, max_seqlen_k, ctypes.c_float(scale), _ptr(out), ws, ws_bytes, _stream(pool.device))
+    return out
+
+
+def forward_verify_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, cu_seqlens_q, cu_seqlens_k, table,
+                         scale: float, **kw) -> torch.Tensor:
+    """MTP verify: k draft rows per slot, row j sees ctx+j+1 keys (the draft rows are in the pool).
+    The same causal call as prefill; with k*G <= 16 rows per kv head it runs the split-KV kernel
+    with GQA folded into the MMA N dimension (the reference's per_row_gqa decode mode)."""
+    return forward_attn_prefill_paged(q, pool, layer, cu_seqlens_q, cu_seqlens_k, table, scale, **kw)
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,155 @@
+"""Seeded synthetic workloads with the shapes of the five benchmark configurations.
+
+The reference measures on its own prompts (not in its tree); these seeded
+stand-ins carry the configurations' shapes, length distributions and value
+distributions: K/V ~ N(0,1) (optionally with a fraction of +-8-sigma outliers),
+q ~ N(0,1), 16-token pages scattered over a shared pool by a seeded
+permutation so that every slot's page table is fragmented.
+
+  decode_small   1 slot, ctx 4096, Hq 32 x D 128, Hkv 8
+  decode_batch   16 slots, ctx ~ U[1024, 32768], Hq 32 x D 128, Hkv 8, 1% outliers at 8 sigma
+  decode_long    1 slot, ctx 131072, Hq 16 x D 256, Hkv 2
+  prefill_chunk  4 entries x (8192 restored prefix + 2048-token chunk), Hq 32 x D 128, Hkv 8
+  mtp_verify     64 slots x 4 draft rows, ctx ~ U[4096, 65536], Hq 32 x D 128, Hkv 8, 36 layers
+
+"ctx" counts every key the step attends to, the step's own new rows included.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+
+
+@dataclass
+class Workload:
+    name: str
+    n_q_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ctx: np.ndarray              # keys per entry after the step's rows are written
+    q_rows: np.ndarray           # query rows per entry (1 for decode)
+    page_size: int = 16
+    group_size: int = 32
+    n_layers: int = 1
+    outlier_frac: float = 0.0
+    seed: int = 0
+    extra_pages: int = 0
+    block_table: np.ndarray = field(default=None, repr=False)
+    n_pages: int = 0
+
+    def __post_init__(self):
+        self.ctx = np.asarray(self.ctx, np.int64)
+        self.q_rows = np.asarray(self.q_rows, np.int64)
+        if self.block_table is None:
+            self.block_table, self.n_pages = fragmented_tables(self.ctx, self.page_size, self.seed,
+                                                               self.extra_pages)
+
+    @property
+    def batch(self) -> int:
+        return len(self.ctx)
+
+    @property
+    def max_blocks(self) -> int:
+        return self.block_table.shape[1]
+
+    @property
+    def prefix(self) -> np.ndarray:
+        """Keys already in the pool before the step writes its own rows."""
+        return self.ctx - self.q_rows
+
+    @property
+    def cu_k(self) -> np.ndarray:
+        return np.concatenate([[0], np.cumsum(self.ctx)]).astype(np.int32)
+
+    @property
+    def cu_q(self) -> np.ndarray:
+        return np.concatenate([[0], np.cumsum(self.q_rows)]).astype(np.int32)
+
+    @property
+    def kv_bytes_per_token(self) -> int:
+        """Q8_0 bytes of one token of K and V in one layer: 2 * Hkv * (D + 2 * D / group)."""
+        return 2 * self.n_kv_heads * (self.head_dim + 2 * self.head_dim // self.group_size)
+
+    def kv_bytes(self, layers: Optional[int] = None) -> int:
+        """Algorithmic KV bytes one step reads (every key of every entry, once per layer)."""
+        return int(self.ctx.sum()) * self.kv_bytes_per_token * (layers or self.n_layers)
+
+    def attn_flops(self) -> float:
+        """QK^T + PV flops: 4 * D * Hq per (query row, visible key) pair."""
+        pairs = 0
+        for tk, tq in zip(self.ctx.tolist(), self.q_rows.tolist()):
+            pairs += tq * (tk - tq) + tq * (tq + 1) // 2
+        return 4.0 * self.head_dim * self.n_q_heads * pairs * self.n_layers
+
+
+def fragmented_tables(ctx: np.ndarray, page_size: int, seed: int, extra_pages: int = 0):
+    """Block tables drawn from one shared pool sized for the sum of contexts: the pool's
+    page ids are permuted with a seeded generator and dealt out to the slots in order,
+    so consecutive positions of a slot land on unrelated pages."""
+    pages = (np.asarray(ctx) + page_size - 1) // page_size
+    n_pages = max(int(pages.sum()) + extra_pages, 1)
+    perm = np.random.default_rng(seed ^ 0x5EED).permutation(n_pages).astype(np.int32)
+    max_blocks = max(int(pages.max()) if len(pages) else 1, 1)
+    table = np.zeros((len(ctx), max_blocks), np.int32)
+    off = 0
+    for b, n in enumerate(pages.tolist()):
+        table[b, :n] = perm[off:off + n]
+        off += n
+    return table, n_pages
+
+
+def decode_small(seed: int = 1) -> Workload:
+    return Workload("decode_small", 32, 8, 128, ctx=[4096], q_rows=[1], seed=seed)
+
+
+def decode_batch(seed: int = 2, n_slots: int = 16) -> Workload:
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(1024, 32768, size=n_slots, endpoint=True)
+    return Workload("decode_batch", 32, 8, 128, ctx=ctx, q_rows=np.ones(n_slots), outlier_frac=0.01, seed=seed)
+
+
+def decode_long(seed: int = 3, ctx: int = 131072) -> Workload:
+    return Workload("decode_long", 16, 2, 256, ctx=[ctx], q_rows=[1], seed=seed)
+
+
+def prefill_chunk(seed: int = 4, batch: int = 4, prefix: int = 8192, chunk: int = 2048) -> Workload:
+    return Workload("prefill_chunk", 32, 8, 128, ctx=[prefix + chunk] * batch, q_rows=[chunk] * batch, seed=seed)
+
+
+def mtp_verify(seed: int = 5, n_slots: int = 64, drafts: int = 4, n_layers: int = 36) -> Workload:
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(4096, 65536, size=n_slots, endpoint=True)
+    return Workload("mtp_verify", 32, 8, 128, ctx=ctx, q_rows=[drafts] * n_slots, n_layers=n_layers, seed=seed)
+
+
+CONFIGS = {
+    "decode_small": decode_small,
+    "decode_batch": decode_batch,
+    "decode_long": decode_long,
+    "prefill_chunk": prefill_chunk,
+    "mtp_verify": mtp_verify,
+}
+
+
+def kv_rows_np(rng: np.random.Generator, n_rows: int, n_kv_heads: int, head_dim: int,
+               outlier_frac: float = 0.0) -> np.ndarray:
+    """f16 [n_rows, Hkv, D] ~ N(0,1) with a fraction of entries replaced by +-8."""
+    x = rng.standard_normal((n_rows, n_kv_heads, head_dim), dtype=np.float32)
+    if outlier_frac > 0:
+        m = rng.random(x.shape) < outlier_frac
+        x[m] = 8.0 * np.where(rng.random(int(m.sum())) < 0.5, -1.0, 1.0)
+    return x.astype(np.float16)
+
+
+def kv_rows_torch(gen, n_rows: int, n_kv_heads: int, head_dim: int, outlier_frac: float, device):
+    """Device-side twin of kv_rows_np for full-size pools (same distribution, torch's RNG)."""
+    import torch
+
+    x = torch.randn((n_rows, n_kv_heads, head_dim), generator=gen, device=device, dtype=torch.float32)
+    if outlier_frac > 0:
+        u = torch.rand(x.shape, generator=gen, device=device)
+        s = torch.where(torch.rand(x.shape, generator=gen, device=device) < 0.5, -8.0, 8.0)
+        x = torch.where(u < outlier_frac, s, x)
+    return x.to(torch.float16)

@@ -1,0 +1,112 @@
+"""The C ABI without a GPU: exported symbols, layout functions, the page allocator of a
+host-only pool and host-side argument validation."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from qwen36_server_b200 import _abi
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "yfattn.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    return re.findall(r"^YF_API [^;]*?\b(yf_\w+)\(", src, flags=re.M)
+
+
+def test_library_exports_every_declared_symbol(yf):
+    names = declared_functions()
+    assert len(names) >= 20
+    L = yf.lib()
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_abi.SIGNATURES), set(names) ^ set(_abi.SIGNATURES)
+    assert L.yf_abi_version() == 1
+
+
+@pytest.mark.parametrize("D,P,G", [(128, 16, 32), (256, 64, 32), (256, 64, 256), (128, 16, 128), (256, 16, 32)])
+def test_layout_offsets_match_oracle(yf, oracle, D, P, G):
+    L = yf.lib()
+    d = _abi.PoolDesc(1, 4, 2, D, P, G, -1, 0, None)
+    od = oracle.PoolDesc(1, 4, 2, D, P, G)
+    ko, vo, kso, vso = oracle.layout_maps(od)
+    lk = np.array([[L.yf_pool_tile_offset(ctypes.byref(d), 0, t, x) for x in range(D)] for t in range(16)])
+    lv = np.array([[L.yf_pool_tile_offset(ctypes.byref(d), 1, t, x) for x in range(D)] for t in range(16)])
+    assert np.array_equal(lk, ko) and np.array_equal(lv, vo)
+    for t in range(16):
+        for s in range(D // G):
+            assert L.yf_pool_scale_offset(ctypes.byref(d), 0, t, s) == kso[t, s]
+            assert L.yf_pool_scale_offset(ctypes.byref(d), 1, t, s) == vso[t, s]
+    every = np.concatenate([ko.ravel(), vo.ravel(), kso.ravel(), kso.ravel() + 1, vso.ravel(), vso.ravel() + 1])
+    assert np.array_equal(np.sort(every), np.arange(od.tile_bytes))  # a bijection onto the tile
+    assert L.yf_pool_page_head_bytes(ctypes.byref(d)) == od.page_head_bytes
+    assert L.yf_pool_bytes(ctypes.byref(d)) == od.pool_bytes
+    assert L.yf_pool_tile_offset(ctypes.byref(d), 0, 16, 0) == -1
+
+
+def test_unsupported_shapes_are_refused(yf):
+    for D, P, G in [(64, 16, 32), (128, 32, 32), (128, 16, 64)]:
+        desc = _abi.PoolDesc(1, 4, 2, D, P, G, -1, 0, None)
+        h = ctypes.c_void_p()
+        assert yf.lib().yf_pool_create(ctypes.byref(desc), ctypes.byref(h)) == _abi.YF_E_UNSUPPORTED
+        assert b"built for" in yf.lib().yf_last_error()
+
+
+def test_page_allocator(yf):
+    pool = yf.PagedKvPool(2, 10, 8, 128, device=None)
+    assert pool.free_count() == 10
+    a = pool.alloc_pages(4)
+    assert a == [0, 1, 2, 3] and pool.free_count() == 6
+    assert all(pool.refcount(p) == 1 for p in a)
+    pool.retain_pages([1, 2])          # a prefix shared with a second slot
+    pool.free_pages(a)
+    assert pool.free_count() == 8 and pool.refcount(1) == 1 and pool.refcount(0) == 0
+    with pytest.raises(yf.YfError) as e:
+        pool.free_pages([0])           # already free
+    assert e.value.code == _abi.YF_E_STATE
+    with pytest.raises(yf.YfError) as e:
+        pool.free_pages([1, 1])        # one reference left, two drops: nothing changes
+    assert e.value.code == _abi.YF_E_STATE and pool.refcount(1) == 1
+    pool.free_pages([1, 2])
+    assert pool.free_count() == 10
+    with pytest.raises(yf.YfError) as e:
+        pool.alloc_pages(11)
+    assert e.value.code == _abi.YF_E_NOMEM and pool.free_count() == 10
+    with pytest.raises(yf.YfError) as e:
+        pool.retain_pages([3])
+    assert e.value.code == _abi.YF_E_STATE
+    with pytest.raises(yf.YfError) as e:
+        pool.free_pages([10])
+    assert e.value.code == _abi.YF_E_RANGE
+    # freed pages come back LIFO: a fragmented table after interleaved frees
+    x = pool.alloc_pages(6)
+    pool.free_pages([x[1], x[4]])
+    assert sorted(pool.alloc_pages(2)) == sorted([x[1], x[4]])
+    pool.close()
+
+
+def test_device_calls_on_host_only_pool_are_invalid(yf):
+    pool = yf.PagedKvPool(1, 4, 2, 128, device=None)
+    L = yf.lib()
+    rc = L.yf_attn_decode(pool.handle, 0, 16, 8, 16, 16, 1, 1, 16, ctypes.c_float(0.1), 16, None, 0, None)
+    assert rc == _abi.YF_E_INVALID
+    rc = L.yf_kv_append_paged(pool.handle, 0, 16, 16, 16, 16, 1, 1, None)
+    assert rc == _abi.YF_E_INVALID
+    v = ctypes.c_uint32()
+    assert L.yf_pool_status(pool.handle, ctypes.byref(v), 0) == _abi.YF_E_INVALID
+    pool.close()
+
+
+def test_workspace_size_plan(yf):
+    pool = yf.PagedKvPool(1, 4, 8, 128, device=None)
+    L = yf.lib()
+    # small single-slot decode: one chunk, no workspace
+    assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 0
+    # a long batch needs partials: rows_per_cta * (D + 1) floats per item
+    ws = L.yf_attn_workspace_size(pool.handle, 32, 16, 1, 32768)
+    assert ws > 0 and ws % (8 * 129 * 4) == 0
+    assert L.yf_attn_workspace_size(pool.handle, 30, 16, 1, 32768) == 0   # Hq not a multiple of Hkv
+    pool.close()
