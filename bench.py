@@ -1,0 +1,494 @@
+"""Benchmark of the paged Q8_0 KV attention path (one JSON line on rank 0).
+
+Default workload (decode_batch): one continuous-batching decode step of one
+attention layer for 16 slots with ctx ~ U[1024, 32768], Hq 32 x D 128, Hkv 8,
+Q8_0 K/V in 16-token pages scattered over a shared pool.  A step is the KV
+write of the 16 new rows (quantize-and-scatter) plus split-KV decode
+attention over every slot's keys.  With --gpus N each rank runs its own 16
+slots (weak scaling, no collective on the data path); value = all ranks'
+tokens / max-over-ranks time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl reference]
+
+--impl reference times the CPU restatement of the path (oracle/, the
+reference's own candle CPU path cannot be built here) on a bounded sample of
+the same workload with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+import __graft_entry__ as graft  # noqa: E402
+
+graft.load_package()
+
+METRIC = "paged int8-KV decode attn tokens/s & KV GB/s (% HBM peak) at 1/2/4/8 B200"
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(config: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", f"splitkv_{config}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.path = os.path.join("/tmp", f"yf_clocks_{os.getpid()}.csv")
+        try:
+            import torch
+
+            pr = torch.cuda.get_device_properties(device_index)
+            self.bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        except Exception:
+            self.bus = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.bus:
+            cmd.insert(1, f"--id={self.bus}")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+
+
+class Step:
+    """One workload resident on one GPU, with pre-bound C-ABI calls for the timed loop."""
+
+    def __init__(self, wl, device: int, layers_resident: int = 1):
+        import torch
+
+        yf = graft.load_package()
+        from qwen36_server_b200 import workloads as W
+
+        self.torch, self.yf, self.wl = torch, yf, wl
+        self.dev = torch.device("cuda", device)
+        torch.cuda.set_device(self.dev)
+        self.L = yf.lib()
+        self.layers = layers_resident
+        self.pool = yf.PagedKvPool(layers_resident, wl.n_pages, wl.n_kv_heads, wl.head_dim, wl.page_size,
+                                   wl.group_size, device=device)
+        gen = torch.Generator(device=self.dev)
+        gen.manual_seed(wl.seed)
+        bt = torch.from_numpy(wl.block_table).to(self.dev)
+        self.bt = bt
+        # history: every key before the step's own rows, written through the multi-row writer
+        prefix = wl.prefix
+        for layer in range(layers_resident):
+            chunk_rows = 1 << 18
+            # write entry by entry in bounded row chunks to keep the f16 staging small
+            for b in range(wl.batch):
+                n = int(prefix[b])
+                for s in range(0, n, chunk_rows):
+                    m = min(chunk_rows, n - s)
+                    k = W.kv_rows_torch(gen, m, wl.n_kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+                    v = W.kv_rows_torch(gen, m, wl.n_kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+                    yf.launch_append_multi(self.pool, layer, k, v, [0, m], [s], bt[b:b + 1], max_rows=m)
+        T = int(wl.q_rows.sum())
+        self.T = T
+        self.k_new = W.kv_rows_torch(gen, T, wl.n_kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+        self.v_new = W.kv_rows_torch(gen, T, wl.n_kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+        self.q = torch.randn((T, wl.n_q_heads, wl.head_dim), generator=gen, device=self.dev).half()
+        self.out = torch.empty_like(self.q)
+        i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(self.dev)  # noqa: E731
+        self.cu_k = i32(wl.cu_k)
+        self.cu_q = i32(wl.cu_q)
+        self.start = i32(wl.prefix)
+        self.decode = bool((wl.q_rows == 1).all())
+        self.max_q = int(wl.q_rows.max())
+        self.max_k = int(wl.ctx.max())
+        ws = self.pool.workspace_size(wl.n_q_heads, wl.batch, self.max_q if not self.decode else 1, self.max_k)
+        self.ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.dev)
+        self.ws_bytes = ws
+        torch.cuda.synchronize()
+        st = self.pool.status()
+        if st:
+            raise RuntimeError(f"device status {st} after building the workload")
+        self._bind()
+
+    def _bind(self):
+        wl, L, P = self.wl, self.L, ctypes.c_void_p
+        s = P(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        h = self.pool.handle
+        scale = ctypes.c_float(self.yf.default_scale(wl.head_dim))
+        ptr = lambda t: P(t.data_ptr())  # noqa: E731
+        self.calls = []
+        for layer in range(self.wl.n_layers):
+            pl = layer % self.layers
+            if self.decode:
+                w = (L.yf_kv_append_paged, (h, pl, ptr(self.k_new), ptr(self.v_new), ptr(self.start), ptr(self.bt),
+                                            wl.max_blocks, wl.batch, s))
+                a = (L.yf_attn_decode, (h, pl, ptr(self.q), wl.n_q_heads, ptr(self.cu_k), ptr(self.bt),
+                                        wl.max_blocks, wl.batch, self.max_k, scale, ptr(self.out), ptr(self.ws),
+                                        self.ws_bytes, s))
+            else:
+                w = (L.yf_kv_append_paged_multi, (h, pl, ptr(self.k_new), ptr(self.v_new), ptr(self.cu_q),
+                                                  ptr(self.start), ptr(self.bt), wl.max_blocks, wl.batch,
+                                                  self.max_q, s))
+                a = (L.yf_attn_prefill, (h, pl, ptr(self.q), wl.n_q_heads, ptr(self.cu_q), ptr(self.cu_k),
+                                         ptr(self.bt), wl.max_blocks, wl.batch, self.max_q, self.max_k, scale,
+                                         ptr(self.out), ptr(self.ws), self.ws_bytes, s))
+            self.calls.append((w, a))
+
+    def run(self):
+        for (wf, wa), (af, aa) in self.calls:
+            if wf(*wa) or af(*aa):
+                raise RuntimeError(self.L.yf_last_error().decode())
+
+    def run_attn(self):
+        for _, (af, aa) in self.calls:
+            if af(*aa):
+                raise RuntimeError(self.L.yf_last_error().decode())
+
+    def launches_per_step(self) -> int:
+        plan_chunks = self.ws_bytes > 0
+        return self.wl.n_layers * (2 + (1 if plan_chunks else 0))
+
+
+def make_workload(name: str, rank: int):
+    from qwen36_server_b200 import workloads as W
+
+    fn = W.CONFIGS[name]
+    base_seed = fn.__defaults__[0]
+    return fn(seed=base_seed + 1000 * rank)
+
+
+def gpu_arm(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    wl = make_workload(args.config, rank)
+    layers_resident = wl.n_layers
+    if args.config == "mtp_verify":
+        free = torch.cuda.mem_get_info(local_rank)[0]
+        per_layer = wl.kv_bytes(1)
+        layers_resident = max(1, min(wl.n_layers, int(0.8 * free // per_layer)))
+    step = Step(wl, local_rank, layers_resident)
+    stream = torch.cuda.current_stream(step.dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step.run()
+    barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step.run()
+    t1.record(stream)
+    barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+
+    # dominant kernel: attention alone (split-KV kernel + its combine), events per launch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in evs:
+        a.record(stream)
+        step.run_attn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps / wl.n_layers
+    clk = clocks.stop()
+
+    # end to end through the public API with host buffers: H2D of the step's inputs, D2H of the output
+    pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
+    h_in = [(pin(t), t) for t in (step.q, step.k_new, step.v_new, step.start, step.cu_k)]
+    h_out = torch.empty(step.out.shape, dtype=step.out.dtype, pin_memory=True)
+    bytes_in = sum(h.numel() * h.element_size() for h, _ in h_in)
+    bytes_out = h_out.numel() * h_out.element_size()
+    for _ in range(max(1, args.warmup)):
+        for h, d in h_in:
+            d.copy_(h, non_blocking=True)
+        step.run()
+        h_out.copy_(step.out, non_blocking=True)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for h, d in h_in:
+            d.copy_(h, non_blocking=True)
+        step.run()
+        h_out.copy_(step.out, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    t = torch.tensor([ms, e2e_ms, attn_ms], dtype=torch.float64, device=step.dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, attn_ms = t.tolist()
+    status = step.pool.status()
+
+    tokens = step.T * world
+    kv_bytes = wl.kv_bytes()
+    hbm, tflops, peak_kind = peaks()
+    alg_bytes_attn = wl.kv_bytes(1)
+    achieved_gbs = alg_bytes_attn / (attn_ms * 1e-3) / 1e9
+    if wl.name == "prefill_chunk":
+        roof = {"bound": "tensor", "achieved": wl.attn_flops() / wl.n_layers / (attn_ms * 1e-3) / 1e12,
+                "peak": tflops, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = profile_traffic(args.config)
+    roof["kernel"] = "splitkv_kernel + splitkv_combine (one attention call)"
+    roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback"
+    roof["algorithmic_bytes_per_launch"] = alg_bytes_attn
+    roof["launch_ms"] = attn_ms
+
+    line = {
+        "metric": METRIC,
+        "value": tokens / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 (int8 KV unpacked exactly to f16 for mma, f32 accumulate)",
+        "data": "synthetic (seeded N(0,1) K/V, fragmented seeded page tables)",
+        "config": {
+            "workload": describe(wl),
+            "slots_per_gpu": wl.batch,
+            "query_rows_per_gpu": step.T,
+            "sum_ctx_per_gpu": int(wl.ctx.sum()),
+            "layers": wl.n_layers,
+            "layers_resident": step.layers,
+            "kv_bytes_per_step_per_gpu": kv_bytes,
+            "l2": "inputs larger than L2: the pool read per step exceeds 126 MB" if wl.kv_bytes(1) > 126e6
+            else "pool fits in L2 (small workload)",
+            "parallelism": f"slot-sharded x{world} (each rank its own slots, no collective)",
+        },
+        "kv_gbs": kv_bytes * world / (ms * 1e-3) / 1e9,
+        "hbm_frac_step": kv_bytes / (ms * 1e-3) / 1e9 / hbm,
+        "roofline": roof,
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": bytes_in,
+                "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
+        "gpu_launches": step.launches_per_step() * args.steps,
+        "clocks": clk,
+        "device_status": status,
+    }
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+    return line
+
+
+def describe(wl) -> str:
+    c = wl.ctx
+    rng = f"ctx {int(c.min())}..{int(c.max())} (sum {int(c.sum())})" if len(c) > 1 else f"ctx {int(c[0])}"
+    return (f"{wl.name}: {wl.batch} entries x {int(wl.q_rows.max())} query rows, {rng}, "
+            f"Hq {wl.n_q_heads} x D {wl.head_dim}, Hkv {wl.n_kv_heads}, Q8_0 (group {wl.group_size}) "
+            f"{wl.page_size}-token pages, {wl.n_layers} layer(s)")
+
+
+# ---------------------------------------------------------------------------------------
+# CPU: the oracle's restatement of the path on a bounded sample
+
+
+class CpuSample:
+    """A sample of the workload's entries (their own keys only) prepared for the CPU oracle."""
+
+    def __init__(self, wl, max_tokens: int):
+        from qwen36_server_b200 import workloads as W
+
+        self.O = graft.load_oracle()
+        order = np.argsort(wl.ctx)
+        pick, tot = [], 0
+        for i in order[len(order) // 2:].tolist() + order[:len(order) // 2].tolist():   # median first
+            if tot + wl.ctx[i] > max_tokens and pick:
+                continue
+            pick.append(i)
+            tot += int(wl.ctx[i])
+        pick = sorted(pick)
+        self.sub = W.Workload("cpu", wl.n_q_heads, wl.n_kv_heads, wl.head_dim, ctx=wl.ctx[pick],
+                              q_rows=wl.q_rows[pick], page_size=wl.page_size, group_size=wl.group_size,
+                              outlier_frac=wl.outlier_frac, seed=wl.seed)
+        s = self.sub
+        self.desc = self.O.PoolDesc(1, s.n_pages, s.n_kv_heads, s.head_dim, s.page_size, s.group_size)
+        rng = np.random.default_rng(s.seed)
+        n = int(s.ctx.sum())
+        k = W.kv_rows_np(rng, n, s.n_kv_heads, s.head_dim, s.outlier_frac)
+        v = W.kv_rows_np(rng, n, s.n_kv_heads, s.head_dim, s.outlier_frac)
+        self.pool = np.zeros(self.desc.pool_bytes, np.uint8)
+        entry = np.repeat(np.arange(s.batch), s.ctx).astype(np.int32)
+        pos = np.concatenate([np.arange(c) for c in s.ctx]).astype(np.int32)
+        hist = np.ones(n, bool)
+        starts = np.concatenate([[0], np.cumsum(s.ctx)])[:-1]
+        for b in range(s.batch):
+            hist[starts[b] + s.prefix[b]: starts[b] + s.ctx[b]] = False
+        self.O.np_kv_write_rows(self.desc, self.pool, 0, k[hist], v[hist], entry[hist], pos[hist], s.block_table)
+        self.new = (k[~hist], v[~hist], entry[~hist], pos[~hist])
+        self.q = rng.standard_normal((int(s.q_rows.sum()), s.n_q_heads, s.head_dim)).astype(np.float16)
+        self.threads = os.cpu_count() or 1
+        self.tokens = int(s.q_rows.sum())
+        self.n_layers = wl.n_layers
+
+    def step(self):
+        s = self.sub
+        k, v, e, p = self.new
+        for _ in range(self.n_layers):
+            self.O.c_kv_write_rows(self.desc, self.pool, 0, k, v, e, p, s.block_table)
+            self.O.c_attn(self.desc, self.pool, 0, self.q, s.cu_q, s.cu_k, s.block_table,
+                          1.0 / np.sqrt(s.head_dim), self.threads)
+
+
+def cpu_baseline(wl, seconds: float):
+    samp = CpuSample(wl, max_tokens=int(2.5e5))
+    samp.step()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        samp.step()
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": samp.tokens / dt, "unit": "tokens/s", "cores": samp.threads, "kind": "port",
+            "sample": f"{samp.sub.batch} of {wl.batch} entries ({int(samp.sub.ctx.sum())} keys, "
+                      f"{samp.n_layers} layer(s)), {n} steps; oracle/yf_oracle.c double-precision attention "
+                      f"+ Q8_0 scatter"}
+
+
+def reference_arm(args):
+    wl = make_workload(args.config, 0)
+    samp = CpuSample(wl, max_tokens=int(args.ref_tokens))
+    for _ in range(args.warmup):
+        samp.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        samp.step()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = samp.tokens / dt
+    return {
+        "impl": "reference",
+        "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64 (oracle)", "data": "synthetic",
+        "config": {"workload": describe(wl), "sample": describe(samp.sub)},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": samp.threads, "kind": "port",
+                         "sample": f"{samp.sub.batch} of {wl.batch} entries per step; the reference's candle "
+                                   "CPU path cannot be built here (no Rust toolchain, fork not vendored)"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="decode_batch",
+                    choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify"])
+    ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-tokens", type=float, default=1.2e5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(reference_arm(args)), flush=True)
+        return
+
+    import torch
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = gpu_arm(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

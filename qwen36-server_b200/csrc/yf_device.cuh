@@ -9,7 +9,7 @@ namespace yf {
 
 // Iterations of a bounded mbarrier wait before it gives up (each try_wait
 // itself suspends for a hardware-defined interval), i.e. seconds, not a hang.
-constexpr uint32_t kMaxWaitIters = 1u << 24;
+constexpr uint32_t kMaxWaitIters = 1u << 20;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
