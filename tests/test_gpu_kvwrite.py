@@ -81,9 +81,10 @@ def test_out_of_range_rows_are_skipped_and_flagged(yf, oracle, cuda):
     img = pool_image(pool)
     desc = oracle.PoolDesc(1, 4, 2, 128)
     ref = np.zeros(desc.pool_bytes, np.uint8)
-    oracle.np_kv_write_rows(desc, ref, 0, np.ones((1, 2, 128), np.float16), np.ones((1, 2, 128), np.float16),
-                            [0], [0], np.array([[0, 1]]))
-    assert np.array_equal(img, ref)                                      # only the valid row landed
+    ones = np.ones((2, 2, 128), np.float16)
+    # the valid rows: entry 1 at position 5 (first call) and entry 0 at position 0 (second call)
+    oracle.np_kv_write_rows(desc, ref, 0, ones, ones, [1, 0], [5, 0], np.array([[0, 1], [2, 9]]))
+    assert np.array_equal(img, ref)
     with pytest.raises(yf.YfError) as e:
         yf.kv_append_paged(pool, 3, k, k, [0, 0], bt)
     assert e.value.code == _abi.YF_E_RANGE
