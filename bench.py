@@ -21,7 +21,6 @@ import ctypes
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -62,57 +61,65 @@ def profile_traffic(config: str):
 
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Polls NVML (read-only: SM clock, max SM clock, clock-event reasons) every ~2 ms in a
+    thread while the timed loops run; falls back to nothing if NVML is unavailable."""
+
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device_index: int):
-        self.proc = None
-        self.path = os.path.join("/tmp", f"yf_clocks_{os.getpid()}.csv")
+        import threading
+
+        self.samples, self.reasons, self.h, self.smax = [], 0, None, None
+        self.stop_evt = threading.Event()
+        self.thread = None
         try:
+            import pynvml
             import torch
 
+            pynvml.nvmlInit()
+            self.nv = pynvml
             pr = torch.cuda.get_device_properties(device_index)
-            self.bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.smax = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.bus = None
+            self.h = None
+
+    def _reasons(self) -> int:
+        nv = self.nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(fn(self.h))
+
+    def _run(self):
+        while not self.stop_evt.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self._reasons()
+            except Exception:
+                pass
+            self.stop_evt.wait(0.002)
 
     def start(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
-        if self.bus:
-            cmd.insert(1, f"--id={self.bus}")
-        try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        import threading
+
+        if self.h is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.f.close()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        self.stop_evt.set()
+        self.thread.join()
+        names = [n for n, bit in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.smax, "reasons": names, "samples": len(self.samples),
+                "source": "NVML, polled every 2 ms during the timed loops"}
 
 
 # ---------------------------------------------------------------------------------------
@@ -260,7 +267,6 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         b.record(stream)
     torch.cuda.synchronize()
     attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps / wl.n_layers
-    clk = clocks.stop()
 
     # end to end through the public API with host buffers: H2D of the step's inputs, D2H of the output
     pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
@@ -285,6 +291,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
 
     t = torch.tensor([ms, e2e_ms, attn_ms], dtype=torch.float64, device=step.dev)
     if world > 1:
@@ -450,8 +457,8 @@ def reference_arm(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="decode_batch",
                     choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify"])
     ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
