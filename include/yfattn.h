@@ -176,6 +176,22 @@ YF_API int yf_attn_decode(yf_pool* pool, int32_t layer, const void* d_q, int32_t
                           int32_t max_blocks, int32_t batch, int32_t max_seqlen_k, float scale,
                           void* d_out, void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* yf_attn_decode without a workspace argument, for callers that cannot
+ * allocate device memory: their memory is planned once at start-up and handed
+ * out by an allocator they cannot reach from the FFI layer, so a cudaMalloc
+ * of their own would break that budget and may fail mid-request.  No
+ * counterpart in the reference.  The split-KV partials go to a 16 MiB array
+ * built into the library (held by every GPU that loads it, until exit); a
+ * call whose yf_attn_workspace_size exceeds 16 MiB returns YF_E_WORKSPACE.
+ * The first call on a device looks up that array's device address, so make
+ * it before any stream capture.  All calls share the array: calls whose
+ * kernels overlap on the GPU race and must be serialised by the caller.
+ * Allocates nothing. */
+YF_API int yf_attn_decode_noalloc(yf_pool* pool, int32_t layer, const void* d_q, int32_t n_q_heads,
+                                  const uint32_t* d_cu_seqlens_k, const uint32_t* d_block_table,
+                                  int32_t max_blocks, int32_t batch, int32_t max_seqlen_k, float scale,
+                                  void* d_out, void* stream);
+
 /* Causal chunked prefill and MTP verify: replaces forward_attn_prefill_paged
  * (docs/plans/2026-08-27-mtp-cuda-graphs.md:132,244-248) and
  * forward_verify_paged (:279-284, per_row_gqa at :537-541).

@@ -74,6 +74,7 @@ SIGNATURES = {
     "yf_kv_append_paged_multi": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "yf_attn_workspace_size": (_sz, [_vp, _i32, _i32, _i32, _i32]),
     "yf_attn_decode": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "yf_attn_decode_noalloc": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),
     "yf_attn_prefill": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
                               _vp]),
     "yf_pool_export_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
