@@ -215,8 +215,16 @@ class Step:
                 raise RuntimeError(self.L.yf_last_error().decode())
 
     def launches_per_step(self) -> int:
-        plan_chunks = self.ws_bytes > 0
-        return self.wl.n_layers * (2 + (1 if plan_chunks else 0))
+        """KV write + split-KV attention per layer, + the separate combine kernel when the
+        partials cannot be merged inside the attention kernel (fused combine off, or more
+        units than the pool's arrival counters)."""
+        wl = self.wl
+        rows = wl.n_q_heads // wl.n_kv_heads * (1 if self.decode else self.max_q)
+        rpc = 8 if (rows <= 8 or wl.head_dim > 128) else 16
+        units = wl.batch * wl.n_kv_heads * -(-rows // rpc)
+        fused = os.environ.get("YF_FUSED_COMBINE", "1") != "0" and units <= (1 << 16)
+        separate = self.ws_bytes > 0 and not fused
+        return wl.n_layers * (2 + (1 if separate else 0))
 
 
 def make_workload(name: str, rank: int):

@@ -18,10 +18,14 @@
 // O^T = V^T P^T (dims in M); int8 is unpacked to exact f16 in registers and
 // the Q8_0 group scales are applied to the per-group partial dot products (K)
 // and to P (V), so the tensor cores see only exact integers.  Softmax is
-// online, base 2, with warp-shuffle row maxima; rows of one CTA end in a
-// shared-memory merge of the 4 warps.  A unit that needs one chunk writes f16
-// output directly; otherwise normalised partials + lse go to the workspace
-// and splitkv_combine merges them.
+// online, base 2, with warp-shuffle row maxima and a lazy rescale; rows of one
+// CTA end in a shared-memory merge of the 4 warps.  A unit that needs one
+// chunk writes f16 output directly; otherwise normalised partials + lse go to
+// the workspace and the CTA that finishes the unit's last chunk (an arrival
+// counter in the pool) merges them, so no second launch is needed.  Lane 0
+// loads each tile's page id one tile ahead so the block-table read stays off
+// the copy's critical path.  Calls on one pool must be stream-ordered (the
+// counters are per pool).
 #include <cfloat>
 
 #include "yf_device.cuh"
@@ -31,7 +35,10 @@ namespace yf {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kBarBytes = 128;
+constexpr int kHdrBytes = 256;  // mbarriers + per-stage page-valid flags
+// Lazy softmax rescale: the running max only moves when a tile's max exceeds it by
+// more than 2^8 in probability terms, so most tiles skip the O rescale; p <= 256.
+constexpr float kRescaleThresh = 8.0f;
 
 struct SplitParams {
     const uint8_t* layer_base;
@@ -53,6 +60,7 @@ struct SplitParams {
     __half* out;
     float* ws_o;
     float* ws_lse;
+    uint32_t* counters;  // per-unit arrival counters for the fused combine, or null
     uint32_t* status;
 };
 
@@ -86,6 +94,40 @@ __device__ __forceinline__ bool unit_geom(const SplitParams& p, int b, int rg, U
     return true;
 }
 
+// Merges the n_chunks partials (normalised O, base-2 lse) of one unit into f16 output.
+// Loads go through L2 (ld.global.cg): the partials were written by other CTAs.
+template <int D, int RPC>
+__device__ __forceinline__ void combine_unit(const SplitParams& p, const UnitGeom& u, int h, size_t item0, int tid,
+                                             int nthreads) {
+    for (int e = tid; e < RPC * (D / 4); e += nthreads) {
+        const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
+        const int row = u.row_begin + r;
+        if (row >= u.rows_total) continue;
+        float M = -INFINITY;
+        for (int c = 0; c < u.n_chunks; ++c) M = fmaxf(M, __ldcg(p.ws_lse + (item0 + c) * RPC + r));
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < u.n_chunks; ++c) {
+            const float lv = __ldcg(p.ws_lse + (item0 + c) * RPC + r);
+            if (lv == -INFINITY) continue;
+            const float f = fast_exp2(lv - M);
+            L += f;
+            const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((item0 + c) * RPC + r) * D + d4));
+            acc.x = fmaf(f, ov.x, acc.x);
+            acc.y = fmaf(f, ov.y, acc.y);
+            acc.z = fmaf(f, ov.z, acc.z);
+            acc.w = fmaf(f, ov.w, acc.w);
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        const int j = row / p.G, gi = row % p.G;
+        __half* op = p.out + ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D + d4;
+        uint2 pk;
+        pk.x = pack_h2(acc.x * inv, acc.y * inv);
+        pk.y = pack_h2(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(op) = pk;
+    }
+}
+
 template <int D, int NB, int NT, int TPP, int STAGES>
 __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) {
     constexpr int TB = 32 * D + 64 * NB;  // tile bytes
@@ -99,17 +141,20 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     constexpr int RPC = 8 * NT;   // query rows per CTA
     constexpr int DP = D + 4;     // padded row stride of the merge buffer
     static_assert(MPG % 2 == 0, "m-tiles come in pairs per 16-byte V word");
-    static_assert(kBarBytes >= kWarps * STAGES * 8, "barrier area too small");
+    static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
     static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
 
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-    uint8_t* stages = smem + kBarBytes;
+    uint8_t* sflag = smem + kWarps * STAGES * 8;
+    uint8_t* stages = smem + kHdrBytes;
+    __shared__ int s_last;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
-    const int c = blockIdx.x, b = blockIdx.z;
-    const int h = blockIdx.y % p.H, rg = blockIdx.y / p.H;
+    // chunk index is the slowest grid dimension: every unit's first chunks are dispatched first
+    const int c = blockIdx.z, b = blockIdx.y;
+    const int h = blockIdx.x % p.H, rg = blockIdx.x / p.H;
 
     UnitGeom u;
     if (!unit_geom<TPP, RPC>(p, b, rg, u, threadIdx.x == 0 && c == 0)) return;
@@ -154,26 +199,32 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
     const long long page_stride = p.phb * p.H;
 
-    auto issue = [&](int slot, int kt) {
-        const uint32_t page = __ldg(btrow + kt / TPP);
+    uint8_t* myflag = sflag + warp * STAGES;
+    // lane 0 only: copy tile kt (page id already loaded) into `slot`; a page id past the pool
+    // completes the stage without a copy and marks it invalid.
+    auto issue = [&](int slot, int kt, uint32_t page) {
         if (page < (uint32_t)p.n_pages) {
+            myflag[slot] = 1;
             mbar_arrive_expect_tx(&mybar[slot], TB);
             bulk_g2s(mystage + slot * TB, head_base + (size_t)page * page_stride + (kt % TPP) * TB, TB,
                      &mybar[slot]);
         } else {
+            myflag[slot] = 0;
             atomicOr(p.status, YF_DEV_BAD_PAGE);
             mbar_arrive(&mybar[slot]);
         }
     };
+    auto tile_of = [&](int i) { return tile_begin + warp + i * kWarps; };
 
+    uint32_t next_page = 0;  // lane 0: page id of the next tile to issue, loaded one tile ahead
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < STAGES; ++s) mbar_init(&mybar[s], 1);
         fence_mbar_init();
+        for (int s = 0; s < STAGES && s < my_n; ++s) issue(s, tile_of(s), __ldg(btrow + tile_of(s) / TPP));
+        if (STAGES < my_n) next_page = __ldg(btrow + tile_of(STAGES) / TPP);
     }
     __syncwarp();
-    if (lane == 0)
-        for (int s = 0; s < STAGES && s < my_n; ++s) issue(s, tile_begin + warp + s * kWarps);
 
     float m_run[NT][2], l_run[NT][2];
     float o[MT][NT][4];
@@ -193,15 +244,14 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     for (int i = 0; i < my_n; ++i) {
         const int slot = i % STAGES;
         const uint32_t parity = (uint32_t)(i / STAGES) & 1u;
-        const int kt = tile_begin + warp + i * kWarps;
+        const int kt = tile_of(i);
         const bool arrived = __all_sync(0xffffffffu, mbar_wait(&mybar[slot], parity));
         if (!arrived) {
             if (lane == 0) atomicOr(p.status, YF_DEV_TIMEOUT);
             break;
         }
         done = i + 1;
-        const bool valid = __ldg(btrow + kt / TPP) < (uint32_t)p.n_pages;
-        if (valid) {
+        if (myflag[slot]) {
             const uint8_t* T = mystage + slot * TB;
             // ---- K scales of tokens g and g+8
             float ks0[NB], ks1[NB];
@@ -268,6 +318,9 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
             for (int nt = 0; nt < NT; ++nt) {
                 float pr[2][2];
 #pragma unroll
+                bool need = false;
+                float alpha[2];
+#pragma unroll
                 for (int col = 0; col < 2; ++col) {
                     float v0 = sacc[nt][col] * p.scale_log2;
                     float v1 = sacc[nt][2 + col] * p.scale_log2;
@@ -277,17 +330,26 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    const float mnew = fmaxf(m_run[nt][col], mx);
-                    const float muse = mnew == -INFINITY ? 0.f : mnew;
-                    const float alpha = fast_exp2(m_run[nt][col] - muse);
+                    alpha[col] = 1.f;
+                    if (mx > m_run[nt][col] + kRescaleThresh) {
+                        // m_run == -inf gives alpha = exp2(-inf) = 0 (nothing accumulated yet)
+                        alpha[col] = fast_exp2(m_run[nt][col] - mx);
+                        m_run[nt][col] = mx;
+                        l_run[nt][col] *= alpha[col];
+                        need = true;
+                    }
+                    const float muse = m_run[nt][col] == -INFINITY ? 0.f : m_run[nt][col];
                     pr[col][0] = fast_exp2(v0 - muse);
                     pr[col][1] = fast_exp2(v1 - muse);
-                    l_run[nt][col] = fmaf(l_run[nt][col], alpha, pr[col][0] + pr[col][1]);
-                    m_run[nt][col] = mnew;
+                    l_run[nt][col] += pr[col][0] + pr[col][1];
+                }
+                if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
-                        o[mt][nt][col] *= alpha;
-                        o[mt][nt][2 + col] *= alpha;
+                        o[mt][nt][0] *= alpha[0];
+                        o[mt][nt][2] *= alpha[0];
+                        o[mt][nt][1] *= alpha[1];
+                        o[mt][nt][3] *= alpha[1];
                     }
                 }
                 // P^T B-fragment: lane (g, tig) needs P[tok 2tig, 2tig+8][row g] and
@@ -332,7 +394,10 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
             }
         }
         __syncwarp();
-        if (lane == 0 && i + STAGES < my_n) issue(slot, tile_begin + warp + (i + STAGES) * kWarps);
+        if (lane == 0 && i + STAGES < my_n) {
+            issue(slot, tile_of(i + STAGES), next_page);
+            if (i + STAGES + 1 < my_n) next_page = __ldg(btrow + tile_of(i + STAGES + 1) / TPP);
+        }
     }
     // A warp that gave up waits (bounded) for the copies it still has in flight.
     if (done < my_n) {
@@ -377,7 +442,8 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     __syncthreads();
 
     const bool direct = u.n_chunks == 1;
-    const size_t item = (((size_t)b * p.H + h) * p.n_row_groups + rg) * p.max_chunks + c;
+    const size_t unit = ((size_t)b * p.H + h) * p.n_row_groups + rg;
+    const size_t item = unit * p.max_chunks + c;
     for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
         const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
         const int row = u.row_begin + r;
@@ -416,6 +482,20 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
             if (d4 == 0) p.ws_lse[item * RPC + r] = L > 0.f ? M + __log2f(L) : -INFINITY;
         }
     }
+    if (direct || !p.counters) return;
+
+    // Fused combine: the CTA that finishes a unit's last chunk merges all its partials.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(&p.counters[unit], 1u);
+        s_last = prev == (uint32_t)u.n_chunks - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    combine_unit<D, RPC>(p, u, h, unit * p.max_chunks, threadIdx.x, kThreads);
+    if (threadIdx.x == 0) p.counters[unit] = 0;  // ready for the next call on this pool
 }
 
 // Log-sum-exp merge of the chunk partials of one (entry, kv head, row group).
@@ -426,41 +506,14 @@ __global__ void __launch_bounds__(kThreads) splitkv_combine(const SplitParams p)
     UnitGeom u;
     if (!unit_geom<TPP, RPC>(p, b, rg, u, false)) return;
     if (u.n_chunks <= 1) return;
-    const size_t item0 = (((size_t)b * p.H + h) * p.n_row_groups + rg) * p.max_chunks;
-    for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
-        const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
-        const int row = u.row_begin + r;
-        if (row >= u.rows_total) continue;
-        float M = -INFINITY;
-        for (int c = 0; c < u.n_chunks; ++c) M = fmaxf(M, p.ws_lse[(item0 + c) * RPC + r]);
-        float L = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = 0; c < u.n_chunks; ++c) {
-            const float lv = p.ws_lse[(item0 + c) * RPC + r];
-            if (lv == -INFINITY) continue;
-            const float f = fast_exp2(lv - M);
-            L += f;
-            const float4 ov = *reinterpret_cast<const float4*>(p.ws_o + ((item0 + c) * RPC + r) * D + d4);
-            acc.x = fmaf(f, ov.x, acc.x);
-            acc.y = fmaf(f, ov.y, acc.y);
-            acc.z = fmaf(f, ov.z, acc.z);
-            acc.w = fmaf(f, ov.w, acc.w);
-        }
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        const int j = row / p.G, gi = row % p.G;
-        __half* op = p.out + ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D + d4;
-        uint2 pk;
-        pk.x = pack_h2(acc.x * inv, acc.y * inv);
-        pk.y = pack_h2(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(op) = pk;
-    }
+    const size_t unit = ((size_t)b * p.H + h) * p.n_row_groups + rg;
+    combine_unit<D, RPC>(p, u, h, unit * p.max_chunks, threadIdx.x, kThreads);
 }
 
-template <int D, int NB, int NT, int TPP>
+template <int D, int NB, int NT, int TPP, int STAGES>
 static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
-    constexpr int STAGES = D == 128 ? 4 : 3;
     constexpr int TB = 32 * D + 64 * NB;
-    constexpr int SMEM = kBarBytes + kWarps * STAGES * TB;
+    constexpr int SMEM = kHdrBytes + kWarps * STAGES * TB;
     auto kern = splitkv_kernel<D, NB, NT, TPP, STAGES>;
     static bool attr_set[64] = {};
     const int dev = a.pool->desc.device;
@@ -469,11 +522,11 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(splitkv)");
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    const dim3 grid(plan.max_chunks, a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch);
+    const dim3 grid(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch, plan.max_chunks);
     kern<<<grid, kThreads, SMEM, a.stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "splitkv launch");
-    if (plan.max_chunks > 1) {
+    if (plan.max_chunks > 1 && !p.counters) {
         const dim3 cg(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch);
         splitkv_combine<D, TPP, 8 * NT><<<cg, kThreads, 0, a.stream>>>(p);
         e = cudaGetLastError();
@@ -482,10 +535,16 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
     return YF_OK;
 }
 
+template <int D, int NB, int NT, int TPP>
+static int launch_st(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
+    if (plan.stages == 3) return launch_t<D, NB, NT, TPP, 3>(a, plan, p);
+    return launch_t<D, NB, NT, TPP, (D == 128 ? 4 : 3)>(a, plan, p);
+}
+
 template <int D, int NB, int NT>
 static int launch_tpp(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
-    if (a.pool->desc.page_size == 16) return launch_t<D, NB, NT, 1>(a, plan, p);
-    return launch_t<D, NB, NT, 4>(a, plan, p);
+    if (a.pool->desc.page_size == 16) return launch_st<D, NB, NT, 1>(a, plan, p);
+    return launch_st<D, NB, NT, 4>(a, plan, p);
 }
 
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
@@ -509,6 +568,8 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.out = a.out;
     p.status = a.pool->d_status;
+    const size_t units = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups;
+    p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;
     if (plan.max_chunks > 1) {
         const size_t items = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups * plan.max_chunks;
         p.ws_o = static_cast<float*>(a.workspace);

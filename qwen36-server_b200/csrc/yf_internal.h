@@ -13,6 +13,9 @@ namespace yf {
 
 // Tokens per tile: the unit one warp consumes per pipeline step.
 constexpr int kTileTokens = 16;
+// Units (entry x kv head x row group) whose split-KV partials the attention kernel can merge
+// itself; the pool keeps one arrival counter per unit.
+constexpr int kMaxCombineUnits = 1 << 16;
 
 // Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).
 struct TileGeom {
@@ -47,6 +50,7 @@ struct yf_pool {
     size_t page_bytes = 0;   // all kv heads of one page in one layer
     size_t layer_bytes = 0;
     uint32_t* d_status = nullptr;  // device status word (YF_DEV_* bits)
+    uint32_t* d_counters = nullptr;  // kMaxCombineUnits arrival counters, zero between calls
     int sm_count = 148;
     std::vector<int32_t> refcount;
     std::vector<int32_t> free_stack;  // LIFO of free page ids
@@ -68,6 +72,8 @@ struct SplitPlan {
     int n_row_groups;  // ceil(G * max_seqlen_q / rows_per_cta)
     int chunk_tiles;   // 16-token tiles per CTA
     int max_chunks;    // ceil(max tiles / chunk_tiles)
+    int stages;        // bulk-copy stages per warp
+    bool fused_combine;  // the last CTA of a unit merges its partials (no combine launch)
     size_t ws_bytes;   // partial O + lse
 };
 

@@ -67,8 +67,14 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
         if (c > (1 << 20)) c = 1 << 20;
         chunk = (int)c;
     }
+    if (tiles > 65535LL * chunk) chunk = (tiles + 65534) / 65535;  // grid z <= 65535
     p.chunk_tiles = chunk;
     p.max_chunks = tiles > 0 ? (tiles + chunk - 1) / chunk : 1;
+    p.stages = pool->desc.head_dim == 128 ? 4 : 3;
+    const char* st = getenv("YF_DECODE_STAGES");  // host-side tuning override
+    if (st && atoi(st) == 3) p.stages = 3;
+    const char* fc = getenv("YF_FUSED_COMBINE");
+    p.fused_combine = !(fc && atoi(fc) == 0);
     if (p.max_chunks <= 1) {
         p.ws_bytes = 0;
     } else {
@@ -167,11 +173,14 @@ int yf_pool_create(const yf_pool_desc* desc, yf_pool** out_pool) {
     }
     e = cudaMalloc(&p->d_status, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(uint32_t) * kMaxCombineUnits);
+    if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, sizeof(uint32_t) * kMaxCombineUnits);
     if (e == cudaSuccess) e = cudaMemset(p->base, 0, p->bytes);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         if (p->owns_mem) cudaFree(p->base);
         if (p->d_status) cudaFree(p->d_status);
+        if (p->d_counters) cudaFree(p->d_counters);
         delete p;
         return cuda_fail(e, "pool initialisation");
     }
@@ -185,6 +194,7 @@ int yf_pool_destroy(yf_pool* pool) {
         cudaSetDevice(pool->desc.device);
         if (pool->owns_mem && pool->base) cudaFree(pool->base);
         if (pool->d_status) cudaFree(pool->d_status);
+        if (pool->d_counters) cudaFree(pool->d_counters);
     }
     delete pool;
     return YF_OK;

@@ -63,14 +63,19 @@ def test_decode_batch_ragged_with_outliers(yf, oracle, cuda):
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128))
     got = run_decode(yf, pool, wl, q, cuda)
     assert np.abs(got - ref).max() <= TOL
-    # the split-KV plan must not change the result beyond rounding: one chunk vs 8-tile chunks
-    for chunk in ("8", "100000"):
-        os.environ["YF_CHUNK_TILES"] = chunk
+    # the split-KV plan must not change the result beyond rounding: 8-tile chunks merged by the
+    # fused last-CTA combine or by the separate combine kernel, 3 or 4 copy stages, one chunk
+    for env in ({"YF_CHUNK_TILES": "8"}, {"YF_CHUNK_TILES": "8", "YF_FUSED_COMBINE": "0"},
+                {"YF_CHUNK_TILES": "24", "YF_DECODE_STAGES": "3"}, {"YF_CHUNK_TILES": "100000"}):
+        os.environ.update(env)
         try:
             alt = run_decode(yf, pool, wl, q, cuda)
+            alt2 = run_decode(yf, pool, wl, q, cuda)   # counters reset between calls
         finally:
-            del os.environ["YF_CHUNK_TILES"]
-        assert np.abs(alt - ref).max() <= TOL
+            for key in env:
+                del os.environ[key]
+        assert np.abs(alt - ref).max() <= TOL, env
+        assert np.array_equal(alt, alt2), env
     assert pool.status() == 0
     pool.close()
 
