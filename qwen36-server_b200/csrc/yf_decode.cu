@@ -1,31 +1,38 @@
 // Split-KV paged Q8_0 attention for decode, MTP verify and other small query
-// blocks, plus the log-sum-exp combine of the split partials.
+// blocks, plus the log-sum-exp merge of split partials.
 //
 // Replaces the int8-pool decode/verify branch of the engine's FA2 split-KV
 // kernel (compute_attn_1rowblock_splitkv with Is_kv_q8, described at
 // docs/research/2026-09-16-head-to-head-llamacpp-and-phase-profile.md:3469-3481)
 // and flash_fwd_splitkv_combine_kernel (docs/plans/2026-09-16-prefil-parity-fa2-and-mmq.md:104-107).
 //
-// One CTA = (entry b, kv head h, group of 8 or 16 query rows, chunk of
-// 16-token tiles).  The query rows are the G = Hq/Hkv q heads of kv head h
-// times the query positions (GQA folded into the MMA N dimension), so every
-// K/V byte is read once per CTA.  Each of the 4 warps streams its own tiles:
-// lane 0 issues a 1-D bulk copy (cp.async.bulk, no multicast) of the whole
-// tile (K int8 + scales + V int8 + scales, one contiguous block of the pool)
-// into a per-warp ring of shared-memory stages, completing on an mbarrier.
-// The tile bytes are laid out so that each lane's 16-byte shared load is
-// exactly its mma.sync fragment: K feeds S^T = K Q^T (tokens in M), V feeds
-// O^T = V^T P^T (dims in M); int8 is unpacked to exact f16 in registers and
-// the Q8_0 group scales are applied to the per-group partial dot products (K)
-// and to P (V), so the tensor cores see only exact integers.  Softmax is
-// online, base 2, with warp-shuffle row maxima and a lazy rescale; rows of one
-// CTA end in a shared-memory merge of the 4 warps.  A unit that needs one
-// chunk writes f16 output directly; otherwise normalised partials + lse go to
-// the workspace and the CTA that finishes the unit's last chunk (an arrival
-// counter in the pool) merges them, so no second launch is needed.  Lane 0
-// loads each tile's page id one tile ahead so the block-table read stays off
-// the copy's critical path.  Calls on one pool must be stream-ordered (the
-// counters are per pool).
+// A "unit" is (entry b, kv head h, group of 8 or 16 query rows): the G = Hq/Hkv
+// q heads of kv head h times the entry's query positions, folded into the MMA
+// N dimension so every K/V byte is read once per unit.  The unit's keys are
+// 16-token tiles, each one contiguous block of the pool (K int8 + scales +
+// V int8 + scales).  Each of a CTA's 4 warps streams its own tiles: lane 0
+// issues a 1-D bulk copy (cp.async.bulk, no multicast) of the whole tile into
+// a per-warp ring of shared-memory stages, completing on an mbarrier, and
+// loads the next tile's page id one tile ahead.  The tile bytes are laid out
+// so that each lane's 16-byte shared load is exactly its mma.sync fragment:
+// K feeds S^T = K Q^T (tokens in M), V feeds O^T = V^T P^T (dims in M); int8
+// is unpacked to exact f16 in registers and the Q8_0 group scales multiply
+// the per-group partial dot products (K) and P (V).  Softmax is online, base
+// 2, with warp-shuffle row maxima and a lazy rescale; the 4 warps of a CTA
+// merge through shared memory.
+//
+// Two schedules share that tile code:
+//  * decode_persistent_kernel (one row group per entry, B <= 1024): a grid of
+//    (SMs x resident CTAs) splits the global sequence of (unit, tile) into
+//    equal contiguous ranges, so every CTA streams the same number of bytes
+//    and no SM idles at the tail.  A range covers whole units (written
+//    directly) and at most two unit pieces (written as partials); the CTA that
+//    finishes a unit's last piece merges the pieces (an arrival counter per
+//    unit in the pool).
+//  * splitkv_kernel (everything else): a 3-D grid of (unit, chunk of tiles)
+//    with the same last-arrival merge, or the separate splitkv_combine launch.
+// Calls on one pool must be stream-ordered (the counters belong to the pool).
+#include <algorithm>
 #include <cfloat>
 
 #include "yf_device.cuh"
@@ -37,15 +44,17 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kHdrBytes = 256;  // mbarriers + per-stage page-valid flags
 // Lazy softmax rescale: the running max only moves when a tile's max exceeds it by
-// more than 2^8 in probability terms, so most tiles skip the O rescale; p <= 256.
+// more than 8 (base 2), so most tiles skip the O rescale and p stays <= 256.
 constexpr float kRescaleThresh = 8.0f;
+static_assert(kWarps * 32 * 128 * kMaxCtasPerSm <= 65536, "register budget of the resident CTAs");
 
 struct SplitParams {
     const uint8_t* layer_base;
     int n_pages;
-    int H;   // kv heads
-    int G;   // q heads per kv head
+    int H;  // kv heads
+    int G;  // q heads per kv head
     int Hq;
+    int B;
     long long phb;  // bytes of one (page, kv head)
     const __half* q;
     const uint32_t* cu_q;  // null for decode
@@ -60,11 +69,11 @@ struct SplitParams {
     __half* out;
     float* ws_o;
     float* ws_lse;
-    uint32_t* counters;  // per-unit arrival counters for the fused combine, or null
+    uint32_t* counters;  // per-unit arrival counters for the merge, or null (separate combine)
     uint32_t* status;
 };
 
-// Geometry of one CTA's unit, computed identically by both kernels.
+// Geometry of one unit, computed identically everywhere.
 struct UnitGeom {
     int Tk, Tq, qrow0, rows_total, row_begin, n_tiles, n_chunks;
 };
@@ -94,330 +103,322 @@ __device__ __forceinline__ bool unit_geom(const SplitParams& p, int b, int rg, U
     return true;
 }
 
-// Merges the n_chunks partials (normalised O, base-2 lse) of one unit into f16 output.
-// Loads go through L2 (ld.global.cg): the partials were written by other CTAs.
-template <int D, int RPC>
-__device__ __forceinline__ void combine_unit(const SplitParams& p, const UnitGeom& u, int h, size_t item0, int tid,
-                                             int nthreads) {
-    for (int e = tid; e < RPC * (D / 4); e += nthreads) {
-        const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
-        const int row = u.row_begin + r;
-        if (row >= u.rows_total) continue;
-        float M = -INFINITY;
-        for (int c = 0; c < u.n_chunks; ++c) M = fmaxf(M, __ldcg(p.ws_lse + (item0 + c) * RPC + r));
-        float L = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = 0; c < u.n_chunks; ++c) {
-            const float lv = __ldcg(p.ws_lse + (item0 + c) * RPC + r);
-            if (lv == -INFINITY) continue;
-            const float f = fast_exp2(lv - M);
-            L += f;
-            const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((item0 + c) * RPC + r) * D + d4));
-            acc.x = fmaf(f, ov.x, acc.x);
-            acc.y = fmaf(f, ov.y, acc.y);
-            acc.z = fmaf(f, ov.z, acc.z);
-            acc.w = fmaf(f, ov.w, acc.w);
-        }
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        const int j = row / p.G, gi = row % p.G;
-        __half* op = p.out + ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D + d4;
-        uint2 pk;
-        pk.x = pack_h2(acc.x * inv, acc.y * inv);
-        pk.y = pack_h2(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(op) = pk;
-    }
+// Offset (in halves) of query / output row `row` of unit u (q and out share the layout).
+__device__ __forceinline__ size_t row_offset(const SplitParams& p, const UnitGeom& u, int h, int row, int D) {
+    const int j = row / p.G, gi = row % p.G;
+    return ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D;
 }
 
-template <int D, int NB, int NT, int TPP, int STAGES>
-__global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) {
-    constexpr int TB = 32 * D + 64 * NB;  // tile bytes
-    constexpr int KS_OFF = 16 * D;
-    constexpr int V_OFF = 16 * D + 32 * NB;
-    constexpr int VS_OFF = 32 * D + 32 * NB;
-    constexpr int CH = D / 32;    // 32-dim chunks (one 16-byte K word per lane each)
-    constexpr int CPG = CH / NB;  // chunks per scale group
-    constexpr int MT = D / 16;    // 16-dim m-tiles of O^T
-    constexpr int MPG = MT / NB;  // m-tiles per scale group
-    constexpr int RPC = 8 * NT;   // query rows per CTA
-    constexpr int DP = D + 4;     // padded row stride of the merge buffer
-    static_assert(MPG % 2 == 0, "m-tiles come in pairs per 16-byte V word");
-    static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
-    static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
+// ---- per-warp state and tile math ------------------------------------------------------
 
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-    uint8_t* sflag = smem + kWarps * STAGES * 8;
-    uint8_t* stages = smem + kHdrBytes;
-    __shared__ int s_last;
+template <int D, int NT>
+struct WarpAcc {
+    float m[NT][2];
+    float l[NT][2];
+    float o[D / 16][NT][4];
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, tig = lane & 3;
-    // chunk index is the slowest grid dimension: every unit's first chunks are dispatched first
-    const int c = blockIdx.z, b = blockIdx.y;
-    const int h = blockIdx.x % p.H, rg = blockIdx.x / p.H;
-
-    UnitGeom u;
-    if (!unit_geom<TPP, RPC>(p, b, rg, u, threadIdx.x == 0 && c == 0)) return;
-    if (c >= u.n_chunks) return;
-    const int tile_begin = c * p.chunk_tiles;
-    const int tile_end = min(tile_begin + p.chunk_tiles, u.n_tiles);
-
-    // Keys visible to the softmax rows this lane owns (columns 2tig, 2tig+1 of each n-tile).
-    int kvlen[NT][2];
+    __device__ __forceinline__ void reset() {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int col = 0; col < 2; ++col) {
-            const int r = u.row_begin + nt * 8 + 2 * tig + col;
-            const int kl = u.Tk - u.Tq + r / p.G + 1;
-            kvlen[nt][col] = r < u.rows_total ? max(0, min(kl, u.Tk)) : 0;
+        for (int nt = 0; nt < NT; ++nt) {
+            m[nt][0] = m[nt][1] = -INFINITY;
+            l[nt][0] = l[nt][1] = 0.f;
         }
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
+    }
+};
 
-    // Q^T fragments: lane holds Q[row nt*8+g][32cb + 8tig .. +7] for every chunk.
-    uint4 qf[NT][CH];
+// Q^T fragments of a unit: lane holds Q[row nt*8+g][32cb + 8tig .. +7] for every chunk cb;
+// and the key count each of the lane's softmax rows (2tig, 2tig+1 of each n-tile) sees.
+template <int D, int NT>
+__device__ __forceinline__ void load_unit_q(const SplitParams& p, const UnitGeom& u, int h, int lane,
+                                            uint4 (&qf)[NT][D / 32], int (&kvlen)[NT][2]) {
+    const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         const int r = u.row_begin + nt * 8 + g;
         if (r < u.rows_total) {
-            const int j = r / p.G, gi = r % p.G;
-            const uint4* qp = reinterpret_cast<const uint4*>(
-                p.q + ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D);
+            const uint4* qp = reinterpret_cast<const uint4*>(p.q + row_offset(p, u, h, r, D));
 #pragma unroll
-            for (int cb = 0; cb < CH; ++cb) qf[nt][cb] = __ldg(qp + cb * 4 + tig);
+            for (int cb = 0; cb < D / 32; ++cb) qf[nt][cb] = __ldg(qp + cb * 4 + tig);
         } else {
 #pragma unroll
-            for (int cb = 0; cb < CH; ++cb) qf[nt][cb] = make_uint4(0, 0, 0, 0);
+            for (int cb = 0; cb < D / 32; ++cb) qf[nt][cb] = make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int col = 0; col < 2; ++col) {
+            const int rr = u.row_begin + nt * 8 + 2 * tig + col;
+            const int kl = u.Tk - u.Tq + rr / p.G + 1;
+            kvlen[nt][col] = rr < u.rows_total ? max(0, min(kl, u.Tk)) : 0;
         }
     }
+}
 
-    // Per-warp ring of tile stages.
-    uint64_t* mybar = bars + warp * STAGES;
-    uint8_t* mystage = stages + (size_t)warp * STAGES * TB;
-    const int span = tile_end - tile_begin;
-    const int my_n = span > warp ? (span - warp + kWarps - 1) / kWarps : 0;
-    const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
-    const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
-    const long long page_stride = p.phb * p.H;
+// One 16-token tile (already in shared memory at T) into the warp's running softmax state.
+template <int D, int NB, int NT>
+__device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 (&qf)[NT][D / 32],
+                                          const int (&kvlen)[NT][2], float scale_log2, WarpAcc<D, NT>& a,
+                                          int lane) {
+    constexpr int KS_OFF = 16 * D;
+    constexpr int V_OFF = 16 * D + 32 * NB;
+    constexpr int VS_OFF = 32 * D + 32 * NB;
+    constexpr int CH = D / 32;
+    constexpr int CPG = CH / NB;
+    constexpr int MT = D / 16;
+    constexpr int MPG = MT / NB;
+    static_assert(MPG % 2 == 0, "m-tiles come in pairs per 16-byte V word");
+    const int g = lane >> 2, tig = lane & 3;
 
-    uint8_t* myflag = sflag + warp * STAGES;
-    // lane 0 only: copy tile kt (page id already loaded) into `slot`; a page id past the pool
-    // completes the stage without a copy and marks it invalid.
-    auto issue = [&](int slot, int kt, uint32_t page) {
-        if (page < (uint32_t)p.n_pages) {
-            myflag[slot] = 1;
-            mbar_arrive_expect_tx(&mybar[slot], TB);
-            bulk_g2s(mystage + slot * TB, head_base + (size_t)page * page_stride + (kt % TPP) * TB, TB,
-                     &mybar[slot]);
-        } else {
-            myflag[slot] = 0;
-            atomicOr(p.status, YF_DEV_BAD_PAGE);
-            mbar_arrive(&mybar[slot]);
+    // ---- K scales of tokens g and g+8
+    float ks0[NB], ks1[NB];
+    if constexpr (NB == 1) {
+        const uint32_t w = lds32(T + KS_OFF + 4 * g);
+        ks0[0] = h2f((uint16_t)(w & 0xffff));
+        ks1[0] = h2f((uint16_t)(w >> 16));
+    } else {
+#pragma unroll
+        for (int q4 = 0; q4 < NB / 4; ++q4) {
+            const uint4 w = lds128(T + KS_OFF + 4 * NB * g + 16 * q4);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int idx = q4 * 8 + k;  // f16 index within the lane's 2*NB values
+                const float v = h2f((uint16_t)((ww[k / 2] >> (16 * (k & 1))) & 0xffff));
+                if (idx < NB)
+                    ks0[idx] = v;
+                else
+                    ks1[idx - NB] = v;
+            }
         }
-    };
-    auto tile_of = [&](int i) { return tile_begin + warp + i * kWarps; };
-
-    uint32_t next_page = 0;  // lane 0: page id of the next tile to issue, loaded one tile ahead
-    if (lane == 0) {
-#pragma unroll
-        for (int s = 0; s < STAGES; ++s) mbar_init(&mybar[s], 1);
-        fence_mbar_init();
-        for (int s = 0; s < STAGES && s < my_n; ++s) issue(s, tile_of(s), __ldg(btrow + tile_of(s) / TPP));
-        if (STAGES < my_n) next_page = __ldg(btrow + tile_of(STAGES) / TPP);
     }
-    __syncwarp();
-
-    float m_run[NT][2], l_run[NT][2];
-    float o[MT][NT][4];
+    // ---- S^T = K Q^T, per scale group
+    float sacc[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        m_run[nt][0] = m_run[nt][1] = -INFINITY;
-        l_run[nt][0] = l_run[nt][1] = 0.f;
-    }
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+        for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
+#pragma unroll
+    for (int s = 0; s < NB; ++s) {
+        float acc[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
+            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < CPG; ++cc) {
+            const int cb = s * CPG + cc;
+            const uint4 kw = lds128(T + cb * 512 + lane * 16);
+            const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+            uint32_t a0 = s8lo_to_h2(x0), a1 = s8lo_to_h2(z0), a2 = s8hi_to_h2(x0), a3 = s8hi_to_h2(z0);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y);
+            a0 = s8lo_to_h2(x1);
+            a1 = s8lo_to_h2(z1);
+            a2 = s8hi_to_h2(x1);
+            a3 = s8hi_to_h2(z1);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].z, qf[nt][cb].w);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            sacc[nt][0] = fmaf(ks0[s], acc[nt][0], sacc[nt][0]);
+            sacc[nt][1] = fmaf(ks0[s], acc[nt][1], sacc[nt][1]);
+            sacc[nt][2] = fmaf(ks1[s], acc[nt][2], sacc[nt][2]);
+            sacc[nt][3] = fmaf(ks1[s], acc[nt][3], sacc[nt][3]);
+        }
+    }
+    // ---- online softmax (base 2) on rows 2tig, 2tig+1 of each n-tile
+    const int tok0 = kt * kTileTokens + g, tok1 = tok0 + 8;
+    uint32_t pb01[NT], pb23[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        float pr[2][2];
+        float alpha[2];
+        bool need = false;
+#pragma unroll
+        for (int col = 0; col < 2; ++col) {
+            float v0 = sacc[nt][col] * scale_log2;
+            float v1 = sacc[nt][2 + col] * scale_log2;
+            if (tok0 >= kvlen[nt][col]) v0 = -INFINITY;
+            if (tok1 >= kvlen[nt][col]) v1 = -INFINITY;
+            float mx = fmaxf(v0, v1);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            alpha[col] = 1.f;
+            if (mx > a.m[nt][col] + kRescaleThresh) {
+                // a.m == -inf gives alpha = exp2(-inf) = 0: nothing accumulated yet
+                alpha[col] = fast_exp2(a.m[nt][col] - mx);
+                a.m[nt][col] = mx;
+                a.l[nt][col] *= alpha[col];
+                need = true;
+            }
+            const float muse = a.m[nt][col] == -INFINITY ? 0.f : a.m[nt][col];
+            pr[col][0] = fast_exp2(v0 - muse);
+            pr[col][1] = fast_exp2(v1 - muse);
+            a.l[nt][col] += pr[col][0] + pr[col][1];
+        }
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                a.o[mt][nt][0] *= alpha[0];
+                a.o[mt][nt][2] *= alpha[0];
+                a.o[mt][nt][1] *= alpha[1];
+                a.o[mt][nt][3] *= alpha[1];
+            }
+        }
+        // P^T B-fragment: lane (g, tig) needs P[tok 2tig, 2tig+8][row g] and
+        // P[tok 2tig+1, 2tig+9][row g]; lane (g', tig') holds tokens g', g'+8 of
+        // rows 2tig', 2tig'+1.
+        const uint32_t X = pack_h2(pr[0][0], pr[0][1]);
+        const uint32_t Y = pack_h2(pr[1][0], pr[1][1]);
+        const int src0 = (2 * tig) * 4 + (g >> 1), src1 = src0 + 4;
+        const uint32_t x0 = __shfl_sync(0xffffffffu, X, src0);
+        const uint32_t y0 = __shfl_sync(0xffffffffu, Y, src0);
+        const uint32_t x1 = __shfl_sync(0xffffffffu, X, src1);
+        const uint32_t y1 = __shfl_sync(0xffffffffu, Y, src1);
+        pb01[nt] = (g & 1) ? y0 : x0;
+        pb23[nt] = (g & 1) ? y1 : x1;
+    }
+    // ---- O^T += V^T P^T with the V group scales folded into P
+#pragma unroll
+    for (int s = 0; s < NB; ++s) {
+        const uint2 vsw = lds64(T + VS_OFF + (tig * NB + s) * 8);
+        uint32_t b0[NT], b1[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            b0[nt] = h2mul(pb01[nt], vsw.x);
+            b1[nt] = h2mul(pb23[nt], vsw.y);
+        }
+#pragma unroll
+        for (int mp = 0; mp < MPG / 2; ++mp) {
+            const int mt0 = s * MPG + 2 * mp;
+            const uint4 vw = lds128(T + V_OFF + (mt0 / 2) * 512 + lane * 16);
+            uint32_t w0 = bias8(vw.x), w1 = bias8(vw.y);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+                mma16816(a.o[mt0][nt], s8lo_to_h2(w0), s8lo_to_h2(w1), s8hi_to_h2(w0), s8hi_to_h2(w1), b0[nt], b1[nt]);
+            w0 = bias8(vw.z);
+            w1 = bias8(vw.w);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+                mma16816(a.o[mt0 + 1][nt], s8lo_to_h2(w0), s8lo_to_h2(w1), s8hi_to_h2(w0), s8hi_to_h2(w1), b0[nt],
+                         b1[nt]);
+        }
+    }
+}
 
+// ---- per-warp tile stream -----------------------------------------------------------------
+
+// A warp's ring of tile stages.  The warp's n-th tile overall goes to slot n % STAGES with
+// phase (n / STAGES) & 1, so the ring continues across units without re-initialisation.
+template <int TB, int STAGES>
+struct TileRing {
+    uint64_t* bar;
+    uint8_t* stage;
+    uint8_t* flag;
+    int base;  // tiles this warp consumed before the current run
+
+    __device__ __forceinline__ void init(uint8_t* smem_hdr, uint8_t* smem_stages, int warp, int lane) {
+        bar = reinterpret_cast<uint64_t*>(smem_hdr) + warp * STAGES;
+        flag = smem_hdr + kWarps * STAGES * 8 + warp * STAGES;
+        stage = smem_stages + (size_t)warp * STAGES * TB;
+        base = 0;
+        if (lane == 0) {
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) mbar_init(&bar[s], 1);
+            fence_mbar_init();
+        }
+        __syncwarp();
+    }
+
+    // lane 0 only: copy the tile at `src` (null = a page id past the pool) into run position i.
+    __device__ __forceinline__ void issue(int i, const uint8_t* src, uint32_t* status) {
+        const int slot = (base + i) % STAGES;
+        if (src) {
+            flag[slot] = 1;
+            mbar_arrive_expect_tx(&bar[slot], TB);
+            bulk_g2s(stage + slot * TB, src, TB, &bar[slot]);
+        } else {
+            flag[slot] = 0;
+            atomicOr(status, YF_DEV_BAD_PAGE);
+            mbar_arrive(&bar[slot]);
+        }
+    }
+};
+
+// Streams tiles t0 + warp + 4i (i < this warp's share of n_seg tiles) of unit (b, h) through
+// the warp's ring into `a`.  A bounded wait that gives up flags YF_DEV_TIMEOUT.
+template <int D, int NB, int NT, int TPP, int STAGES>
+__device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * D + 64 * NB, STAGES>& ring, int b,
+                                            int h, int t0, int n_seg, const uint4 (&qf)[NT][D / 32],
+                                            const int (&kvlen)[NT][2], WarpAcc<D, NT>& a, int warp, int lane) {
+    constexpr int TB = 32 * D + 64 * NB;
+    const int my_n = n_seg > warp ? (n_seg - warp + kWarps - 1) / kWarps : 0;
+    const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
+    const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
+    const long long page_stride = p.phb * p.H;
+    auto tile_of = [&](int i) { return t0 + warp + i * kWarps; };
+    auto src_of = [&](int kt, uint32_t page) -> const uint8_t* {
+        return page < (uint32_t)p.n_pages ? head_base + (size_t)page * page_stride + (kt % TPP) * TB : nullptr;
+    };
+    uint32_t next_page = 0;  // lane 0: page id of the next tile to issue, loaded one tile ahead
+    if (lane == 0) {
+        for (int s = 0; s < STAGES && s < my_n; ++s)
+            ring.issue(s, src_of(tile_of(s), __ldg(btrow + tile_of(s) / TPP)), p.status);
+        if (STAGES < my_n) next_page = __ldg(btrow + tile_of(STAGES) / TPP);
+    }
+    __syncwarp();
     int done = 0;
+    bool ok = true;
     for (int i = 0; i < my_n; ++i) {
-        const int slot = i % STAGES;
-        const uint32_t parity = (uint32_t)(i / STAGES) & 1u;
-        const int kt = tile_of(i);
-        const bool arrived = __all_sync(0xffffffffu, mbar_wait(&mybar[slot], parity));
-        if (!arrived) {
+        const int pos = ring.base + i;
+        const int slot = pos % STAGES;
+        if (!__all_sync(0xffffffffu, mbar_wait(&ring.bar[slot], (uint32_t)(pos / STAGES) & 1u))) {
             if (lane == 0) atomicOr(p.status, YF_DEV_TIMEOUT);
+            ok = false;
             break;
         }
         done = i + 1;
-        if (myflag[slot]) {
-            const uint8_t* T = mystage + slot * TB;
-            // ---- K scales of tokens g and g+8
-            float ks0[NB], ks1[NB];
-            if constexpr (NB == 1) {
-                const uint32_t w = lds32(T + KS_OFF + 4 * g);
-                ks0[0] = h2f((uint16_t)(w & 0xffff));
-                ks1[0] = h2f((uint16_t)(w >> 16));
-            } else {
-#pragma unroll
-                for (int q4 = 0; q4 < NB / 4; ++q4) {
-                    const uint4 w = lds128(T + KS_OFF + 4 * NB * g + 16 * q4);
-                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int idx = q4 * 8 + k;  // f16 index within the lane's 2*NB values
-                        const float v = h2f((uint16_t)((ww[k / 2] >> (16 * (k & 1))) & 0xffff));
-                        if (idx < NB)
-                            ks0[idx] = v;
-                        else
-                            ks1[idx - NB] = v;
-                    }
-                }
-            }
-            // ---- S^T = K Q^T, per scale group
-            float sacc[NT][4];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) sacc[nt][e] = 0.f;
-#pragma unroll
-            for (int s = 0; s < NB; ++s) {
-                float acc[NT][4];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-#pragma unroll
-                for (int cc = 0; cc < CPG; ++cc) {
-                    const int cb = s * CPG + cc;
-                    const uint4 kw = lds128(T + cb * 512 + lane * 16);
-                    const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
-                    uint32_t a0 = s8lo_to_h2(x0), a1 = s8lo_to_h2(z0), a2 = s8hi_to_h2(x0), a3 = s8hi_to_h2(z0);
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y);
-                    a0 = s8lo_to_h2(x1);
-                    a1 = s8lo_to_h2(z1);
-                    a2 = s8hi_to_h2(x1);
-                    a3 = s8hi_to_h2(z1);
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].z, qf[nt][cb].w);
-                }
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    sacc[nt][0] = fmaf(ks0[s], acc[nt][0], sacc[nt][0]);
-                    sacc[nt][1] = fmaf(ks0[s], acc[nt][1], sacc[nt][1]);
-                    sacc[nt][2] = fmaf(ks1[s], acc[nt][2], sacc[nt][2]);
-                    sacc[nt][3] = fmaf(ks1[s], acc[nt][3], sacc[nt][3]);
-                }
-            }
-            // ---- online softmax (base 2) on rows 2tig, 2tig+1 of each n-tile
-            const int tok0 = kt * kTileTokens + g, tok1 = tok0 + 8;
-            uint32_t pb01[NT], pb23[NT];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float pr[2][2];
-#pragma unroll
-                bool need = false;
-                float alpha[2];
-#pragma unroll
-                for (int col = 0; col < 2; ++col) {
-                    float v0 = sacc[nt][col] * p.scale_log2;
-                    float v1 = sacc[nt][2 + col] * p.scale_log2;
-                    if (tok0 >= kvlen[nt][col]) v0 = -INFINITY;
-                    if (tok1 >= kvlen[nt][col]) v1 = -INFINITY;
-                    float mx = fmaxf(v0, v1);
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    alpha[col] = 1.f;
-                    if (mx > m_run[nt][col] + kRescaleThresh) {
-                        // m_run == -inf gives alpha = exp2(-inf) = 0 (nothing accumulated yet)
-                        alpha[col] = fast_exp2(m_run[nt][col] - mx);
-                        m_run[nt][col] = mx;
-                        l_run[nt][col] *= alpha[col];
-                        need = true;
-                    }
-                    const float muse = m_run[nt][col] == -INFINITY ? 0.f : m_run[nt][col];
-                    pr[col][0] = fast_exp2(v0 - muse);
-                    pr[col][1] = fast_exp2(v1 - muse);
-                    l_run[nt][col] += pr[col][0] + pr[col][1];
-                }
-                if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        o[mt][nt][0] *= alpha[0];
-                        o[mt][nt][2] *= alpha[0];
-                        o[mt][nt][1] *= alpha[1];
-                        o[mt][nt][3] *= alpha[1];
-                    }
-                }
-                // P^T B-fragment: lane (g, tig) needs P[tok 2tig, 2tig+8][row g] and
-                // P[tok 2tig+1, 2tig+9][row g]; lane (g', tig') holds tokens g', g'+8 of
-                // rows 2tig', 2tig'+1.
-                const uint32_t X = pack_h2(pr[0][0], pr[0][1]);
-                const uint32_t Y = pack_h2(pr[1][0], pr[1][1]);
-                const int src0 = (2 * tig) * 4 + (g >> 1), src1 = src0 + 4;
-                const uint32_t x0 = __shfl_sync(0xffffffffu, X, src0);
-                const uint32_t y0 = __shfl_sync(0xffffffffu, Y, src0);
-                const uint32_t x1 = __shfl_sync(0xffffffffu, X, src1);
-                const uint32_t y1 = __shfl_sync(0xffffffffu, Y, src1);
-                pb01[nt] = (g & 1) ? y0 : x0;
-                pb23[nt] = (g & 1) ? y1 : x1;
-            }
-            // ---- O^T += V^T P^T with the V group scales folded into P
-#pragma unroll
-            for (int s = 0; s < NB; ++s) {
-                const uint2 vsw = lds64(T + VS_OFF + (tig * NB + s) * 8);
-                uint32_t b0[NT], b1[NT];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    b0[nt] = h2mul(pb01[nt], vsw.x);
-                    b1[nt] = h2mul(pb23[nt], vsw.y);
-                }
-#pragma unroll
-                for (int mp = 0; mp < MPG / 2; ++mp) {
-                    const int mt0 = s * MPG + 2 * mp;
-                    const uint4 vw = lds128(T + V_OFF + (mt0 / 2) * 512 + lane * 16);
-                    uint32_t w0 = bias8(vw.x), w1 = bias8(vw.y);
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-                        mma16816(o[mt0][nt], s8lo_to_h2(w0), s8lo_to_h2(w1), s8hi_to_h2(w0), s8hi_to_h2(w1), b0[nt],
-                                 b1[nt]);
-                    w0 = bias8(vw.z);
-                    w1 = bias8(vw.w);
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-                        mma16816(o[mt0 + 1][nt], s8lo_to_h2(w0), s8lo_to_h2(w1), s8hi_to_h2(w0), s8hi_to_h2(w1),
-                                 b0[nt], b1[nt]);
-                }
-            }
-        }
+        if (ring.flag[slot])
+            tile_math<D, NB, NT>(ring.stage + slot * TB, tile_of(i), qf, kvlen, p.scale_log2, a, lane);
         __syncwarp();
         if (lane == 0 && i + STAGES < my_n) {
-            issue(slot, tile_of(i + STAGES), next_page);
+            ring.issue(i + STAGES, src_of(tile_of(i + STAGES), next_page), p.status);
             if (i + STAGES + 1 < my_n) next_page = __ldg(btrow + tile_of(i + STAGES + 1) / TPP);
         }
     }
-    // A warp that gave up waits (bounded) for the copies it still has in flight.
-    if (done < my_n) {
+    if (!ok) {  // wait (bounded) for the copies still in flight before the ring is reused
         for (int i = done; i < my_n && i < done + STAGES; ++i)
-            (void)mbar_wait(&mybar[i % STAGES], (uint32_t)(i / STAGES) & 1u);
+            (void)mbar_wait(&ring.bar[(ring.base + i) % STAGES], (uint32_t)((ring.base + i) / STAGES) & 1u);
     }
+    ring.base += my_n;
+}
 
-    // ---- merge the 4 warps
+// ---- 4-warp merge --------------------------------------------------------------------------
+
+// Writes each warp's (m, l, O) to shared memory (reusing the stage area: every copy of the
+// CTA is complete once all warps arrive) and synchronises the CTA.
+template <int D, int NT>
+__device__ __forceinline__ void stash_warp(uint8_t* area, WarpAcc<D, NT>& a, int warp, int lane) {
+    constexpr int RPC = 8 * NT, DP = D + 4;
+    const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int col = 0; col < 2; ++col) {
-            float l = l_run[nt][col];
+            float l = a.l[nt][col];
             l += __shfl_xor_sync(0xffffffffu, l, 4);
             l += __shfl_xor_sync(0xffffffffu, l, 8);
             l += __shfl_xor_sync(0xffffffffu, l, 16);
-            l_run[nt][col] = l;
+            a.l[nt][col] = l;
         }
-    __syncthreads();
-    float* mw = reinterpret_cast<float*>(stages);
+    __syncthreads();  // every warp is done reading its stages
+    float* mw = reinterpret_cast<float*>(area);
     float* lw = mw + kWarps * RPC;
     float* ow = lw + kWarps * RPC;
     if (g == 0) {
@@ -425,25 +426,32 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int col = 0; col < 2; ++col) {
-                mw[warp * RPC + nt * 8 + 2 * tig + col] = m_run[nt][col];
-                lw[warp * RPC + nt * 8 + 2 * tig + col] = l_run[nt][col];
+                mw[warp * RPC + nt * 8 + 2 * tig + col] = a.m[nt][col];
+                lw[warp * RPC + nt * 8 + 2 * tig + col] = a.l[nt][col];
             }
     }
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+    for (int mt = 0; mt < D / 16; ++mt)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int r = nt * 8 + 2 * tig + (e & 1);
                 const int d = 16 * mt + g + 8 * (e >> 1);
-                ow[(warp * RPC + r) * DP + d] = o[mt][nt][e];
+                ow[(warp * RPC + r) * DP + d] = a.o[mt][nt][e];
             }
     __syncthreads();
+}
 
-    const bool direct = u.n_chunks == 1;
-    const size_t unit = ((size_t)b * p.H + h) * p.n_row_groups + rg;
-    const size_t item = unit * p.max_chunks + c;
+// Merges the stashed warps of one unit: f16 output when `direct`, else the normalised
+// partial O and base-2 lse into workspace item `item`.
+template <int D, int NT>
+__device__ __forceinline__ void emit_unit(const SplitParams& p, const UnitGeom& u, int h, const uint8_t* area,
+                                          bool direct, size_t item) {
+    constexpr int RPC = 8 * NT, DP = D + 4;
+    const float* mw = reinterpret_cast<const float*>(area);
+    const float* lw = mw + kWarps * RPC;
+    const float* ow = lw + kWarps * RPC;
     for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
         const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
         const int row = u.row_begin + r;
@@ -471,34 +479,325 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
         acc.z *= inv;
         acc.w *= inv;
         if (direct) {
-            const int j = row / p.G, gi = row % p.G;
-            __half* op = p.out + ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D + d4;
             uint2 pk;
             pk.x = pack_h2(acc.x, acc.y);
             pk.y = pack_h2(acc.z, acc.w);
-            *reinterpret_cast<uint2*>(op) = pk;
+            *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, row, D) + d4) = pk;
         } else {
             *reinterpret_cast<float4*>(p.ws_o + (item * RPC + r) * D + d4) = acc;
             if (d4 == 0) p.ws_lse[item * RPC + r] = L > 0.f ? M + __log2f(L) : -INFINITY;
         }
     }
-    if (direct || !p.counters) return;
+}
 
-    // Fused combine: the CTA that finishes a unit's last chunk merges all its partials.
-    __threadfence();
+// Merges n partials (items item_of(0..n-1)) of one unit into f16 output; loads through L2
+// (the partials were written by other CTAs).
+template <int D, int RPC, typename ItemOf>
+__device__ __forceinline__ void combine_items(const SplitParams& p, const UnitGeom& u, int h, int n, ItemOf item_of) {
+    for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
+        const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
+        const int row = u.row_begin + r;
+        if (row >= u.rows_total) continue;
+        float M = -INFINITY;
+        for (int c = 0; c < n; ++c) M = fmaxf(M, __ldcg(p.ws_lse + item_of(c) * RPC + r));
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < n; ++c) {
+            const size_t it = item_of(c);
+            const float lv = __ldcg(p.ws_lse + it * RPC + r);
+            if (lv == -INFINITY) continue;
+            const float f = fast_exp2(lv - M);
+            L += f;
+            const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (it * RPC + r) * D + d4));
+            acc.x = fmaf(f, ov.x, acc.x);
+            acc.y = fmaf(f, ov.y, acc.y);
+            acc.z = fmaf(f, ov.z, acc.z);
+            acc.w = fmaf(f, ov.w, acc.w);
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        uint2 pk;
+        pk.x = pack_h2(acc.x * inv, acc.y * inv);
+        pk.y = pack_h2(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, row, D) + d4) = pk;
+    }
+}
+
+// Merges n partials of one unit (workspace items item_of(0..n-1)) in three parallel phases:
+// every lse is loaded at once, turned into normalised per-row weights in shared memory (wsm:
+// n*RPC + RPC floats), then each thread accumulates its O elements with independent loads.
+// Writes f16 output when dst_item < 0, else a partial (normalised O, base-2 lse) into
+// dst_item, which may be one of the inputs (each element is read before it is written, by
+// the same thread).
+template <int D, int RPC, typename ItemOf>
+__device__ __forceinline__ void merge_parts(const SplitParams& p, const UnitGeom& u, int h, int n, ItemOf item_of,
+                                            float* wsm, long long dst_item) {
+    float* w = wsm;
+    float* lse_out = wsm + n * RPC;
+    for (int idx = threadIdx.x; idx < n * RPC; idx += kThreads)
+        w[idx] = __ldcg(p.ws_lse + item_of(idx / RPC) * RPC + idx % RPC);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(&p.counters[unit], 1u);
-        s_last = prev == (uint32_t)u.n_chunks - 1;
+    for (int r = threadIdx.x; r < RPC; r += kThreads) {
+        float M = -INFINITY;
+        for (int k = 0; k < n; ++k) M = fmaxf(M, w[k * RPC + r]);
+        float L = 0.f;
+        for (int k = 0; k < n; ++k) {
+            const float lv = w[k * RPC + r];
+            const float f = lv == -INFINITY ? 0.f : fast_exp2(lv - M);
+            w[k * RPC + r] = f;
+            L += f;
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        for (int k = 0; k < n; ++k) w[k * RPC + r] *= inv;
+        lse_out[r] = L > 0.f ? M + __log2f(L) : -INFINITY;
     }
     __syncthreads();
-    if (!s_last) return;
+    for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
+        const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
+        const int row = u.row_begin + r;
+        if (row >= u.rows_total) continue;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int k = 0;
+        for (; k + 4 <= n; k += 4) {
+            float4 ov[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                ov[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (item_of(k + j) * RPC + r) * D + d4));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float f = w[(k + j) * RPC + r];
+                acc.x = fmaf(f, ov[j].x, acc.x);
+                acc.y = fmaf(f, ov[j].y, acc.y);
+                acc.z = fmaf(f, ov[j].z, acc.z);
+                acc.w = fmaf(f, ov[j].w, acc.w);
+            }
+        }
+        for (; k < n; ++k) {
+            const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (item_of(k) * RPC + r) * D + d4));
+            const float f = w[k * RPC + r];
+            acc.x = fmaf(f, ov.x, acc.x);
+            acc.y = fmaf(f, ov.y, acc.y);
+            acc.z = fmaf(f, ov.z, acc.z);
+            acc.w = fmaf(f, ov.w, acc.w);
+        }
+        if (dst_item < 0) {
+            uint2 pk;
+            pk.x = pack_h2(acc.x, acc.y);
+            pk.y = pack_h2(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, row, D) + d4) = pk;
+        } else {
+            __stcg(reinterpret_cast<float4*>(p.ws_o + ((size_t)dst_item * RPC + r) * D + d4), acc);
+        }
+    }
+    if (dst_item >= 0)
+        for (int r = threadIdx.x; r < RPC; r += kThreads) __stcg(p.ws_lse + (size_t)dst_item * RPC + r, lse_out[r]);
+}
+
+// Counts this CTA's arrival on counter `ctr` (one of `n_arrivals`); true for the last one,
+// which then owns the merge and resets the counter.
+__device__ __forceinline__ bool arrive_last(uint32_t* ctr, int n_arrivals, int* s_flag) {
     __threadfence();
-    combine_unit<D, RPC>(p, u, h, unit * p.max_chunks, threadIdx.x, kThreads);
+    __syncthreads();
+    if (threadIdx.x == 0) *s_flag = atomicAdd(ctr, 1u) == (uint32_t)n_arrivals - 1;
+    __syncthreads();
+    const bool last = *s_flag;
+    if (last) __threadfence();
+    return last;
+}
+
+// Single-level merge: the last of the unit's n_parts arrivals merges every part into the output.
+template <int D, int RPC, typename ItemOf>
+__device__ __forceinline__ void arrive_and_merge(const SplitParams& p, const UnitGeom& u, int h, size_t unit,
+                                                 int n_parts, ItemOf item_of, float* wsm, int* s_flag) {
+    if (!arrive_last(&p.counters[unit], n_parts, s_flag)) return;
+    merge_parts<D, RPC>(p, u, h, n_parts, item_of, wsm, -1);
     if (threadIdx.x == 0) p.counters[unit] = 0;  // ready for the next call on this pool
 }
 
-// Log-sum-exp merge of the chunk partials of one (entry, kv head, row group).
+// Two-level merge of the persistent schedule: pieces form groups of kMergeGroup; the last
+// arrival of a group merges it into the group's first slot, and the last group merges the
+// group results into the output.
+constexpr int kMergeGroup = 16;
+
+template <int D, int RPC, typename ItemOf>
+__device__ __forceinline__ void arrive_and_merge_2level(const SplitParams& p, const UnitGeom& u, int h, size_t unit,
+                                                        int n_parts, int k_self, ItemOf item_of, float* wsm,
+                                                        int* s_flag) {
+    if (n_parts <= kMergeGroup) {
+        arrive_and_merge<D, RPC>(p, u, h, unit, n_parts, item_of, wsm, s_flag);
+        return;
+    }
+    const int g0 = k_self / kMergeGroup * kMergeGroup;
+    const int gn = min(kMergeGroup, n_parts - g0);
+    const size_t first = item_of(g0);
+    uint32_t* gctr = p.counters + kMaxCombineUnits + first;
+    if (!arrive_last(gctr, gn, s_flag)) return;
+    merge_parts<D, RPC>(p, u, h, gn, [&](int k) { return item_of(g0 + k); }, wsm, (long long)first);
+    if (threadIdx.x == 0) *gctr = 0;
+    const int n_groups = (n_parts + kMergeGroup - 1) / kMergeGroup;
+    arrive_and_merge<D, RPC>(p, u, h, unit, n_groups, [&](int k) { return item_of(k * kMergeGroup); }, wsm,
+                             s_flag);
+}
+
+// ---- schedule 1: persistent, equal contiguous ranges of (unit, tile) ------------------------
+
+template <int D, int NB, int NT, int TPP, int STAGES>
+__global__ void __launch_bounds__(kThreads) decode_persistent_kernel(const SplitParams p) {
+    constexpr int TB = 32 * D + 64 * NB;
+    constexpr int RPC = 8 * NT;
+    constexpr int DP = D + 4;
+    static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
+    static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* stages = smem + kHdrBytes;
+    long long* sP = reinterpret_cast<long long*>(stages + kWarps * STAGES * TB);  // [B+1] tile prefix
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = p.H, B = p.B;
+
+    // Tiles per head of every entry and their prefix over (entry, head): unit (b, h) owns the
+    // linear tiles [sP[b] + h*E_b, sP[b] + (h+1)*E_b), E_b = (sP[b+1]-sP[b]) / H.
+    if (warp == 0) {
+        long long carry = 0;
+        for (int base = 0; base < B; base += 32) {
+            const int b = base + lane;
+            long long e = 0;
+            UnitGeom u;
+            if (b < B && unit_geom<TPP, RPC>(p, b, 0, u, blockIdx.x == 0)) e = u.n_tiles;
+            long long v = e;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const long long t = __shfl_up_sync(0xffffffffu, v, off);
+                if (lane >= off) v += t;
+            }
+            if (b < B) sP[b] = (carry + v - e) * H;
+            carry += __shfl_sync(0xffffffffu, v, 31);
+        }
+        if (lane == 0) sP[B] = carry * H;
+    }
+    __syncthreads();
+    const long long T = sP[B];
+    // N <= T: every CTA of the partition owns at least one tile, so the CTAs that meet a unit
+    // are exactly the parts its merge counts
+    const long long N = T < (long long)gridDim.x ? T : (long long)gridDim.x;
+    const bool in_partition = (long long)blockIdx.x < N;
+    const long long s = in_partition ? (long long)blockIdx.x * T / N : 0;
+    const long long e_end = in_partition ? ((long long)blockIdx.x + 1) * T / N : 0;
+    auto start_of = [&](long long c) { return c * T / N; };
+    auto cta_of = [&](long long x) { return ((x + 1) * N - 1) / T; };  // largest c with start_of(c) <= x
+
+    // Entries without keys get zero rows (no tile belongs to them).
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+        if (sP[b + 1] != sP[b]) continue;
+        UnitGeom u;
+        if (!unit_geom<TPP, RPC>(p, b, 0, u, false)) continue;
+        for (int e = threadIdx.x; e < u.rows_total * H * (D / 8); e += kThreads) {
+            const int d8 = (e % (D / 8)) * 8, rh = e / (D / 8);
+            const int row = rh % u.rows_total, h = rh / u.rows_total;
+            *reinterpret_cast<uint4*>(p.out + row_offset(p, u, h, row, D) + d8) = make_uint4(0, 0, 0, 0);
+        }
+    }
+    if (s >= e_end) return;
+
+    TileRing<TB, STAGES> ring;
+    ring.init(smem, stages, warp, lane);
+    WarpAcc<D, NT> acc;
+    uint4 qf[NT][D / 32];
+    int kvlen[NT][2];
+
+    long long x = s;
+    while (x < e_end) {
+        // entry of linear tile x: the largest b with sP[b] <= x (entries without tiles have
+        // sP[b] == sP[b+1], so the search passes over them)
+        int lo = 0, hi = B - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (sP[mid] <= x)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        const int b = lo;
+        const long long E = (sP[b + 1] - sP[b]) / H;
+        const long long off = x - sP[b];
+        const int h = (int)(off / E);
+        const int t0 = (int)(off % E);
+        const long long Us = sP[b] + (long long)h * E, Ue = Us + E;
+        const long long seg_e = e_end < Ue ? e_end : Ue;
+        UnitGeom u;
+        unit_geom<TPP, RPC>(p, b, 0, u, false);
+        load_unit_q<D, NT>(p, u, h, lane, qf, kvlen);
+        acc.reset();
+        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, acc, warp, lane);
+        stash_warp<D, NT>(stages, acc, warp, lane);
+        const bool whole = x == Us && seg_e == Ue;
+        // partial slots: 2 per CTA; slot 1 when the CTA began inside an earlier unit
+        const size_t item = (size_t)blockIdx.x * 2 + (s < Us ? 1 : 0);
+        emit_unit<D, NT>(p, u, h, stages, whole, item);
+        if (!whole) {
+            const long long c_lo = cta_of(Us), c_hi = cta_of(Ue - 1);
+            auto item_of = [&](int k) -> size_t {
+                const long long c = c_lo + k;
+                return (size_t)c * 2 + (start_of(c) < Us ? 1 : 0);
+            };
+            arrive_and_merge_2level<D, RPC>(p, u, h, (size_t)b * H + h, (int)(c_hi - c_lo + 1),
+                                            (int)(blockIdx.x - c_lo), item_of, reinterpret_cast<float*>(stages),
+                                            &s_last);
+        }
+        // the merge area is the next unit's stage area: order its generic accesses before the
+        // bulk copies that will overwrite it
+        fence_proxy_async_smem();
+        __syncthreads();
+        x = seg_e;
+    }
+}
+
+// ---- schedule 2: a 3-D grid of (unit, chunk of tiles) ----------------------------------------
+
+template <int D, int NB, int NT, int TPP, int STAGES>
+__global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) {
+    constexpr int TB = 32 * D + 64 * NB;
+    constexpr int RPC = 8 * NT;
+    constexpr int DP = D + 4;
+    static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
+    static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* stages = smem + kHdrBytes;
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // chunk index is the slowest grid dimension: every unit's first chunks are dispatched first
+    const int c = blockIdx.z, b = blockIdx.y;
+    const int h = blockIdx.x % p.H, rg = blockIdx.x / p.H;
+
+    UnitGeom u;
+    if (!unit_geom<TPP, RPC>(p, b, rg, u, threadIdx.x == 0 && c == 0)) return;
+    if (c >= u.n_chunks) return;
+    const int tile_begin = c * p.chunk_tiles;
+    const int tile_end = min(tile_begin + p.chunk_tiles, u.n_tiles);
+
+    uint4 qf[NT][D / 32];
+    int kvlen[NT][2];
+    load_unit_q<D, NT>(p, u, h, lane, qf, kvlen);
+    TileRing<TB, STAGES> ring;
+    ring.init(smem, stages, warp, lane);
+    WarpAcc<D, NT> acc;
+    acc.reset();
+    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, acc, warp, lane);
+    stash_warp<D, NT>(stages, acc, warp, lane);
+
+    const bool direct = u.n_chunks == 1;
+    const size_t unit = ((size_t)b * p.H + h) * p.n_row_groups + rg;
+    emit_unit<D, NT>(p, u, h, stages, direct, unit * p.max_chunks + c);
+    if (direct || !p.counters) return;
+    auto item_of = [&](int k) -> size_t { return unit * p.max_chunks + k; };
+    if ((u.n_chunks + 1) * RPC * 4 <= kWarps * STAGES * TB)
+        arrive_and_merge<D, RPC>(p, u, h, unit, u.n_chunks, item_of, reinterpret_cast<float*>(stages), &s_last);
+    else if (arrive_last(&p.counters[unit], u.n_chunks, &s_last)) {
+        combine_items<D, RPC>(p, u, h, u.n_chunks, item_of);
+        if (threadIdx.x == 0) p.counters[unit] = 0;
+    }
+}
+
+// Separate merge launch for schedule 2 when the pool's counters cannot be used.
 template <int D, int TPP, int RPC>
 __global__ void __launch_bounds__(kThreads) splitkv_combine(const SplitParams p) {
     const int b = blockIdx.y;
@@ -507,24 +806,50 @@ __global__ void __launch_bounds__(kThreads) splitkv_combine(const SplitParams p)
     if (!unit_geom<TPP, RPC>(p, b, rg, u, false)) return;
     if (u.n_chunks <= 1) return;
     const size_t unit = ((size_t)b * p.H + h) * p.n_row_groups + rg;
-    combine_unit<D, RPC>(p, u, h, unit * p.max_chunks, threadIdx.x, kThreads);
+    auto item_of = [&](int k) -> size_t { return unit * p.max_chunks + k; };
+    combine_items<D, RPC>(p, u, h, u.n_chunks, item_of);
+}
+
+// ---- launch ----------------------------------------------------------------------------------
+
+// Per-device flag that a kernel's dynamic shared-memory limit was raised.
+template <typename K>
+static int raise_smem(K kern, int smem, int dev, int* set_to) {
+    if (dev >= 0 && dev < 64 && set_to[dev] >= smem) return YF_OK;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(split-KV)");
+    if (dev >= 0 && dev < 64) set_to[dev] = smem;
+    return YF_OK;
 }
 
 template <int D, int NB, int NT, int TPP, int STAGES>
 static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int SMEM = kHdrBytes + kWarps * STAGES * TB;
-    auto kern = splitkv_kernel<D, NB, NT, TPP, STAGES>;
-    static bool attr_set[64] = {};
     const int dev = a.pool->desc.device;
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(splitkv)");
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    cudaError_t e;
+    if (plan.persistent) {
+        auto kern = decode_persistent_kernel<D, NB, NT, TPP, STAGES>;
+        static int set_to[64] = {};
+        const int smem = SMEM + (a.batch + 1) * (int)sizeof(long long);
+        const int rc = raise_smem(kern, SMEM + (kPersistentMaxBatch + 1) * (int)sizeof(long long), dev, set_to);
+        if (rc) return rc;
+        // every CTA must be resident at once: cap the grid by the occupancy at this batch size
+        int occ = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+        const int ctas = std::max(1, std::min(plan.persistent_ctas, occ * a.pool->sm_count));
+        kern<<<ctas, kThreads, smem, a.stream>>>(p);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_persistent launch");
     }
+    auto kern = splitkv_kernel<D, NB, NT, TPP, STAGES>;
+    static int set_to2[64] = {};
+    const int rc = raise_smem(kern, SMEM, dev, set_to2);
+    if (rc) return rc;
     const dim3 grid(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch, plan.max_chunks);
     kern<<<grid, kThreads, SMEM, a.stream>>>(p);
-    cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "splitkv launch");
     if (plan.max_chunks > 1 && !p.counters) {
         const dim3 cg(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch);
@@ -555,6 +880,7 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.H = d.n_kv_heads;
     p.G = a.n_q_heads / d.n_kv_heads;
     p.Hq = a.n_q_heads;
+    p.B = a.batch;
     p.phb = (long long)a.pool->page_head_bytes;
     p.q = a.q;
     p.cu_q = a.cu_q;
@@ -570,8 +896,9 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.status = a.pool->d_status;
     const size_t units = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups;
     p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;
-    if (plan.max_chunks > 1) {
-        const size_t items = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups * plan.max_chunks;
+    if (plan.persistent && !p.counters) return fail(YF_E_UNSUPPORTED, "persistent decode needs the merge counters");
+    if (plan.ws_bytes > 0) {
+        const size_t items = plan.persistent ? (size_t)plan.persistent_ctas * 2 : units * plan.max_chunks;
         p.ws_o = static_cast<float*>(a.workspace);
         p.ws_lse = p.ws_o + items * plan.rows_per_cta * d.head_dim;
     } else {

@@ -16,6 +16,13 @@ constexpr int kTileTokens = 16;
 // Units (entry x kv head x row group) whose split-KV partials the attention kernel can merge
 // itself; the pool keeps one arrival counter per unit.
 constexpr int kMaxCombineUnits = 1 << 16;
+// Counters of the first merge level of the persistent decode (groups of pieces of one unit),
+// indexed by the group's first partial slot; they follow the per-unit counters.
+constexpr int kMaxGroupCounters = 4096;
+// Largest batch the persistent decode schedule handles (its tile prefix lives in shared memory).
+constexpr int kPersistentMaxBatch = 1024;
+// Upper bound of resident split-KV CTAs per SM (sizes the persistent schedule's workspace).
+constexpr int kMaxCtasPerSm = 4;
 
 // Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).
 struct TileGeom {
@@ -50,7 +57,7 @@ struct yf_pool {
     size_t page_bytes = 0;   // all kv heads of one page in one layer
     size_t layer_bytes = 0;
     uint32_t* d_status = nullptr;  // device status word (YF_DEV_* bits)
-    uint32_t* d_counters = nullptr;  // kMaxCombineUnits arrival counters, zero between calls
+    uint32_t* d_counters = nullptr;  // kMaxCombineUnits + kMaxGroupCounters arrival counters, zero between calls
     int sm_count = 148;
     std::vector<int32_t> refcount;
     std::vector<int32_t> free_stack;  // LIFO of free page ids
@@ -74,6 +81,8 @@ struct SplitPlan {
     int max_chunks;    // ceil(max tiles / chunk_tiles)
     int stages;        // bulk-copy stages per warp
     bool fused_combine;  // the last CTA of a unit merges its partials (no combine launch)
+    bool persistent;     // decode_persistent_kernel: equal (unit, tile) ranges per CTA
+    int persistent_ctas;  // upper bound of its grid (the launch also caps it by occupancy)
     size_t ws_bytes;   // partial O + lse
 };
 

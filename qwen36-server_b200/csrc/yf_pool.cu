@@ -75,11 +75,23 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     if (st && atoi(st) == 3) p.stages = 3;
     const char* fc = getenv("YF_FUSED_COMBINE");
     p.fused_combine = !(fc && atoi(fc) == 0);
-    if (p.max_chunks <= 1) {
-        p.ws_bytes = 0;
+    // Persistent schedule: one row group per entry (decode, small verify blocks), a batch whose
+    // tile prefix fits in shared memory, and the merge counters available.
+    const char* ps = getenv("YF_PERSISTENT");
+    p.persistent = !(ps && atoi(ps) == 0) && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
+                   units <= kMaxCombineUnits && p.fused_combine;
+    const size_t row_bytes = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
+    if (p.persistent) {
+        // at least 16 tiles (4 per warp) per CTA, at most kMaxCtasPerSm CTAs per SM
+        const long long by_work = (units * tiles + 15) / 16;
+        long long ctas = (long long)pool->sm_count * kMaxCtasPerSm;
+        if (by_work < ctas) ctas = by_work > 0 ? by_work : 1;
+        if (2 * ctas > kMaxGroupCounters) ctas = kMaxGroupCounters / 2;
+        p.persistent_ctas = (int)ctas;
+        p.ws_bytes = (size_t)p.persistent_ctas * 2 * row_bytes;  // two partial slots per CTA
     } else {
-        const size_t items = (size_t)units * p.max_chunks;
-        p.ws_bytes = items * p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
+        p.persistent_ctas = 0;
+        p.ws_bytes = p.max_chunks <= 1 ? 0 : (size_t)units * p.max_chunks * row_bytes;
     }
     return p;
 }
@@ -173,8 +185,9 @@ int yf_pool_create(const yf_pool_desc* desc, yf_pool** out_pool) {
     }
     e = cudaMalloc(&p->d_status, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(p->d_status, 0, sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(uint32_t) * kMaxCombineUnits);
-    if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, sizeof(uint32_t) * kMaxCombineUnits);
+    const size_t n_counters = (size_t)kMaxCombineUnits + kMaxGroupCounters;
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(uint32_t) * n_counters);
+    if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, sizeof(uint32_t) * n_counters);
     if (e == cudaSuccess) e = cudaMemset(p->base, 0, p->bytes);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {

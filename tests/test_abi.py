@@ -103,10 +103,12 @@ def test_device_calls_on_host_only_pool_are_invalid(yf):
 def test_workspace_size_plan(yf):
     pool = yf.PagedKvPool(1, 4, 8, 128, device=None)
     L = yf.lib()
-    # small single-slot decode: one chunk, no workspace
-    assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 0
-    # a long batch needs partials: rows_per_cta * (D + 1) floats per item
+    row = 8 * 129 * 4   # one partial: rows_per_cta x (D + 1) floats
+    # persistent decode: two partial slots per CTA, at least 16 tiles per CTA, at most 4 CTAs/SM
+    assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 2 * 2 * row   # 32 tiles -> 2 CTAs
     ws = L.yf_attn_workspace_size(pool.handle, 32, 16, 1, 32768)
-    assert ws > 0 and ws % (8 * 129 * 4) == 0
+    assert ws == 148 * 4 * 2 * row
+    # past the persistent batch limit the chunked plan applies; short keys need no split
+    assert L.yf_attn_workspace_size(pool.handle, 32, 2000, 1, 256) == 0
     assert L.yf_attn_workspace_size(pool.handle, 30, 16, 1, 32768) == 0   # Hq not a multiple of Hkv
     pool.close()

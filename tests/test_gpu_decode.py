@@ -63,10 +63,12 @@ def test_decode_batch_ragged_with_outliers(yf, oracle, cuda):
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128))
     got = run_decode(yf, pool, wl, q, cuda)
     assert np.abs(got - ref).max() <= TOL
-    # the split-KV plan must not change the result beyond rounding: 8-tile chunks merged by the
-    # fused last-CTA combine or by the separate combine kernel, 3 or 4 copy stages, one chunk
-    for env in ({"YF_CHUNK_TILES": "8"}, {"YF_CHUNK_TILES": "8", "YF_FUSED_COMBINE": "0"},
-                {"YF_CHUNK_TILES": "24", "YF_DECODE_STAGES": "3"}, {"YF_CHUNK_TILES": "100000"}):
+    # the schedule must not change the result beyond rounding: persistent with 3 copy stages;
+    # chunked with 8-tile chunks merged by the last CTA or by the separate combine kernel; one chunk
+    chunked = {"YF_PERSISTENT": "0"}
+    for env in ({"YF_DECODE_STAGES": "3"}, {**chunked, "YF_CHUNK_TILES": "8"},
+                {**chunked, "YF_CHUNK_TILES": "8", "YF_FUSED_COMBINE": "0"},
+                {**chunked, "YF_CHUNK_TILES": "24", "YF_DECODE_STAGES": "3"}, {**chunked, "YF_CHUNK_TILES": "100000"}):
         os.environ.update(env)
         try:
             alt = run_decode(yf, pool, wl, q, cuda)
@@ -106,6 +108,13 @@ def test_zero_length_and_bad_pages(yf, oracle, cuda):
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128))
     assert np.abs(got - ref).max() <= TOL
     assert pool.status() == 0
+    # a generous max_seqlen_k sizes the persistent grid for far more tiles than exist: the
+    # partition shrinks to the real tile count
+    wide = np.zeros((wl.batch, 256), np.int32)
+    wide[:, :wl.max_blocks] = wl.block_table
+    wl_wide = W.Workload("z", 8, 2, 128, ctx=[0, 5, 40], q_rows=[1, 1, 1], block_table=wide, n_pages=wl.n_pages)
+    got = run_decode(yf, pool, wl_wide, q, cuda, max_seqlen_k=4096)
+    assert np.abs(got - ref).max() <= TOL and not got[0].any()
     bad = wl.block_table.copy()
     bad[2, 1] = 10_000                                       # a page id past the pool
     wl_bad = W.Workload("z", 8, 2, 128, ctx=[0, 5, 40], q_rows=[1, 1, 1], block_table=bad, n_pages=wl.n_pages)
@@ -133,4 +142,18 @@ def test_workspace_and_argument_errors(yf, oracle, cuda):
     with pytest.raises(yf.YfError) as e:
         yf.dispatch_flash_decode_paged(q, pool, 0, wl.cu_k, bt, 0.1, max_seqlen_k=10 ** 6)
     assert e.value.code == _abi.YF_E_RANGE
+    pool.close()
+
+
+def test_long_context_two_level_merge(yf, oracle, cuda):
+    """One slot, 2 kv heads, D 256 (the long-context decode shape) at 20000 keys: the persistent
+    schedule cuts each unit into ~80 pieces, merged in groups of 16 and then across groups."""
+    wl = W.Workload("long", 16, 2, 256, ctx=[20000], q_rows=[1], seed=121)
+    pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=122)
+    q = queries(wl, 123)
+    ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(256))
+    for _ in range(2):
+        got = run_decode(yf, pool, wl, q, cuda)
+        assert np.abs(got - ref).max() <= TOL
+    assert pool.status() == 0
     pool.close()

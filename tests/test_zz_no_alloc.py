@@ -55,9 +55,10 @@ def test_noalloc_decode_matches_workspace_decode(yf, oracle, cuda):
 
 def test_noalloc_decode_refuses_oversized_calls(yf, cuda):
     L = yf.lib()
-    # 1000 slots of up to 64K keys with 2 kv heads: the split plan needs about 31 MiB of partials
+    # 1100 slots (past the persistent schedule's batch limit) of up to 64K keys with 2 kv heads:
+    # the chunked split plan needs about 36 MiB of partials
     pool = yf.PagedKvPool(1, 64, 2, 128, device=0)
-    batch, max_k = 1000, 65536
+    batch, max_k = 1100, 65536
     assert pool.workspace_size(32, batch, 1, max_k) > SCRATCH_LIMIT
     q = torch.zeros((batch, 32, 128), dtype=torch.float16, device=cuda)
     cu = torch.zeros(batch + 1, dtype=torch.int32, device=cuda)
