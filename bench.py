@@ -138,6 +138,7 @@ class Step:
         self.torch, self.yf, self.wl = torch, yf, wl
         self.dev = torch.device("cuda", device)
         torch.cuda.set_device(self.dev)
+        self.stream = torch.cuda.Stream(self.dev)  # every timed launch goes to this stream
         self.L = yf.lib()
         self.layers = layers_resident
         self.pool = yf.PagedKvPool(layers_resident, wl.n_pages, wl.n_kv_heads, wl.head_dim, wl.page_size,
@@ -182,7 +183,7 @@ class Step:
 
     def _bind(self):
         wl, L, P = self.wl, self.L, ctypes.c_void_p
-        s = P(self.torch.cuda.current_stream(self.dev).cuda_stream)
+        s = P(self.stream.cuda_stream)
         h = self.pool.handle
         scale = ctypes.c_float(self.yf.default_scale(wl.head_dim))
         ptr = lambda t: P(t.data_ptr())  # noqa: E731
@@ -213,6 +214,21 @@ class Step:
         for _, (af, aa) in self.calls:
             if af(*aa):
                 raise RuntimeError(self.L.yf_last_error().decode())
+
+    def capture(self):
+        """CUDA graphs of one step and of its attention calls (after a warm call has set the
+        kernels' attributes); replaying them removes host launch overhead, as the engine's
+        decode graphs do."""
+        torch = self.torch
+        with torch.cuda.stream(self.stream):
+            self.run()
+        self.stream.synchronize()
+        self.g_step, self.g_attn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g_step, stream=self.stream, capture_error_mode="relaxed"):
+            self.run()
+        with torch.cuda.graph(self.g_attn, stream=self.stream, capture_error_mode="relaxed"):
+            self.run_attn()
+        self.stream.synchronize()
 
     def launches_per_step(self) -> int:
         """KV write + split-KV attention per layer, + the separate combine kernel when the
@@ -246,60 +262,68 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         per_layer = wl.kv_bytes(1)
         layers_resident = max(1, min(wl.n_layers, int(0.8 * free // per_layer)))
     step = Step(wl, local_rank, layers_resident)
-    stream = torch.cuda.current_stream(step.dev)
+    stream = step.stream
+    if args.no_graph:
+        run_step, run_attn = step.run, step.run_attn
+    else:
+        step.capture()
+        run_step, run_attn = step.g_step.replay, step.g_attn.replay
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step.run()
-    barrier()
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
-        step.run()
-    t1.record(stream)
-    barrier()
-    ms = t0.elapsed_time(t1) / args.steps
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run_step()
+        barrier()
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            run_step()
+        t1.record(stream)
+        barrier()
+        ms = t0.elapsed_time(t1) / args.steps
 
-    # dominant kernel: attention alone (split-KV kernel + its combine), events per launch
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for a, b in evs:
-        a.record(stream)
-        step.run_attn()
-        b.record(stream)
-    torch.cuda.synchronize()
-    attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps / wl.n_layers
+        # dominant kernel: the attention call alone, events around each replay
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for a, b in evs:
+            a.record(stream)
+            run_attn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps / wl.n_layers
 
-    # end to end through the public API with host buffers: H2D of the step's inputs, D2H of the output
-    pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
-    h_in = [(pin(t), t) for t in (step.q, step.k_new, step.v_new, step.start, step.cu_k)]
-    h_out = torch.empty(step.out.shape, dtype=step.out.dtype, pin_memory=True)
-    bytes_in = sum(h.numel() * h.element_size() for h, _ in h_in)
-    bytes_out = h_out.numel() * h_out.element_size()
-    for _ in range(max(1, args.warmup)):
-        for h, d in h_in:
-            d.copy_(h, non_blocking=True)
-        step.run()
-        h_out.copy_(step.out, non_blocking=True)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        for h, d in h_in:
-            d.copy_(h, non_blocking=True)
-        step.run()
-        h_out.copy_(step.out, non_blocking=True)
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    clk = clocks.stop()
+        # end to end through the public API with host buffers: H2D of the step's inputs, D2H of
+        # the output, every step
+        pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
+        h_in = [(pin(t), t) for t in (step.q, step.k_new, step.v_new, step.start, step.cu_k)]
+        h_out = torch.empty(step.out.shape, dtype=step.out.dtype, pin_memory=True)
+        bytes_in = sum(h.numel() * h.element_size() for h, _ in h_in)
+        bytes_out = h_out.numel() * h_out.element_size()
+        for _ in range(max(1, args.warmup)):
+            for h, d in h_in:
+                d.copy_(h, non_blocking=True)
+            run_step()
+            h_out.copy_(step.out, non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for h, d in h_in:
+                d.copy_(h, non_blocking=True)
+            run_step()
+            h_out.copy_(step.out, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        clk = clocks.stop()
 
     t = torch.tensor([ms, e2e_ms, attn_ms], dtype=torch.float64, device=step.dev)
     if world > 1:
@@ -348,6 +372,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
             "l2": "inputs larger than L2: the pool read per step exceeds 126 MB" if wl.kv_bytes(1) > 126e6
             else "pool fits in L2 (small workload)",
             "parallelism": f"slot-sharded x{world} (each rank its own slots, no collective)",
+            "launch": "direct C-ABI calls" if args.no_graph else "CUDA graph replay of the step's C-ABI calls",
         },
         "kv_gbs": kv_bytes * world / (ms * 1e-3) / 1e9,
         "hbm_frac_step": kv_bytes / (ms * 1e-3) / 1e9 / hbm,
@@ -471,6 +496,7 @@ def main():
                     choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify"])
     ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-tokens", type=float, default=1.2e5)
     args = ap.parse_args()

@@ -551,41 +551,57 @@ __device__ __forceinline__ void merge_parts(const SplitParams& p, const UnitGeom
         lse_out[r] = L > 0.f ? M + __log2f(L) : -INFINITY;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
+    // every thread owns EPT float4 elements; per batch of PB parts it issues all EPT*PB loads
+    // before the first use, so the merge pays a few L2 round trips, not one per part
+    constexpr int EPT = (RPC * (D / 4) + kThreads - 1) / kThreads;
+    constexpr int PB = EPT >= 4 ? 2 : 4;
+    float4 acc[EPT];
+    bool live[EPT];
+    size_t eoff[EPT];
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+        const int e = threadIdx.x + i * kThreads;
         const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
-        const int row = u.row_begin + r;
-        if (row >= u.rows_total) continue;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        int k = 0;
-        for (; k + 4 <= n; k += 4) {
-            float4 ov[4];
+        live[i] = e < RPC * (D / 4) && u.row_begin + r < u.rows_total;
+        eoff[i] = (size_t)r * D + d4;
+        acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int k0 = 0; k0 < n; k0 += PB) {
+        float4 ov[EPT][PB];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                ov[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (item_of(k + j) * RPC + r) * D + d4));
+        for (int j = 0; j < PB; ++j) {
+            const size_t base = k0 + j < n ? item_of(k0 + j) * RPC * D : 0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float f = w[(k + j) * RPC + r];
-                acc.x = fmaf(f, ov[j].x, acc.x);
-                acc.y = fmaf(f, ov[j].y, acc.y);
-                acc.z = fmaf(f, ov[j].z, acc.z);
-                acc.w = fmaf(f, ov[j].w, acc.w);
+            for (int i = 0; i < EPT; ++i)
+                ov[i][j] = (live[i] && k0 + j < n) ? __ldcg(reinterpret_cast<const float4*>(p.ws_o + base + eoff[i]))
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < PB; ++j) {
+            if (k0 + j >= n) break;
+#pragma unroll
+            for (int i = 0; i < EPT; ++i) {
+                const int r = (threadIdx.x + i * kThreads) / (D / 4);
+                const float f = live[i] ? w[(k0 + j) * RPC + r] : 0.f;
+                acc[i].x = fmaf(f, ov[i][j].x, acc[i].x);
+                acc[i].y = fmaf(f, ov[i][j].y, acc[i].y);
+                acc[i].z = fmaf(f, ov[i][j].z, acc[i].z);
+                acc[i].w = fmaf(f, ov[i][j].w, acc[i].w);
             }
         }
-        for (; k < n; ++k) {
-            const float4 ov = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (item_of(k) * RPC + r) * D + d4));
-            const float f = w[k * RPC + r];
-            acc.x = fmaf(f, ov.x, acc.x);
-            acc.y = fmaf(f, ov.y, acc.y);
-            acc.z = fmaf(f, ov.z, acc.z);
-            acc.w = fmaf(f, ov.w, acc.w);
-        }
+    }
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+        if (!live[i]) continue;
+        const int e = threadIdx.x + i * kThreads;
+        const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
         if (dst_item < 0) {
             uint2 pk;
-            pk.x = pack_h2(acc.x, acc.y);
-            pk.y = pack_h2(acc.z, acc.w);
-            *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, row, D) + d4) = pk;
+            pk.x = pack_h2(acc[i].x, acc[i].y);
+            pk.y = pack_h2(acc[i].z, acc[i].w);
+            *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, u.row_begin + r, D) + d4) = pk;
         } else {
-            __stcg(reinterpret_cast<float4*>(p.ws_o + ((size_t)dst_item * RPC + r) * D + d4), acc);
+            __stcg(reinterpret_cast<float4*>(p.ws_o + (size_t)dst_item * RPC * D + eoff[i]), acc[i]);
         }
     }
     if (dst_item >= 0)
@@ -640,8 +656,13 @@ __device__ __forceinline__ void arrive_and_merge_2level(const SplitParams& p, co
 
 // ---- schedule 1: persistent, equal contiguous ranges of (unit, tile) ------------------------
 
+// Resident CTAs per SM the register allocation must allow (the wide variants would
+// otherwise take ~200 registers and fit only 2).
+template <int D, int NT>
+constexpr int min_ctas() { return (D == 128 && NT == 1) ? 4 : 3; }
+
 template <int D, int NB, int NT, int TPP, int STAGES>
-__global__ void __launch_bounds__(kThreads) decode_persistent_kernel(const SplitParams p) {
+__global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent_kernel(const SplitParams p) {
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int RPC = 8 * NT;
     constexpr int DP = D + 4;
@@ -834,10 +855,20 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
         const int smem = SMEM + (a.batch + 1) * (int)sizeof(long long);
         const int rc = raise_smem(kern, SMEM + (kPersistentMaxBatch + 1) * (int)sizeof(long long), dev, set_to);
         if (rc) return rc;
-        // every CTA must be resident at once: cap the grid by the occupancy at this batch size
+        // every CTA must be resident at once: cap the grid by the occupancy at this shared-memory
+        // size (cached per device for the last size asked)
+        static int occ_smem[64] = {}, occ_val[64] = {};
         int occ = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
-        if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+        if (dev >= 0 && dev < 64 && occ_smem[dev] == smem) {
+            occ = occ_val[dev];
+        } else {
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
+            if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+            if (dev >= 0 && dev < 64) {
+                occ_smem[dev] = smem;
+                occ_val[dev] = occ;
+            }
+        }
         const int ctas = std::max(1, std::min(plan.persistent_ctas, occ * a.pool->sm_count));
         kern<<<ctas, kThreads, smem, a.stream>>>(p);
         e = cudaGetLastError();
@@ -863,7 +894,10 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
 template <int D, int NB, int NT, int TPP>
 static int launch_st(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
     if (plan.stages == 3) return launch_t<D, NB, NT, TPP, 3>(a, plan, p);
-    return launch_t<D, NB, NT, TPP, (D == 128 ? 4 : 3)>(a, plan, p);
+    if constexpr (D == 128)
+        return launch_t<D, NB, NT, TPP, 4>(a, plan, p);
+    else
+        return launch_t<D, NB, NT, TPP, 2>(a, plan, p);
 }
 
 template <int D, int NB, int NT>

@@ -70,7 +70,7 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     if (tiles > 65535LL * chunk) chunk = (tiles + 65534) / 65535;  // grid z <= 65535
     p.chunk_tiles = chunk;
     p.max_chunks = tiles > 0 ? (tiles + chunk - 1) / chunk : 1;
-    p.stages = pool->desc.head_dim == 128 ? 4 : 3;
+    p.stages = pool->desc.head_dim == 128 ? 4 : 2;
     const char* st = getenv("YF_DECODE_STAGES");  // host-side tuning override
     if (st && atoi(st) == 3) p.stages = 3;
     const char* fc = getenv("YF_FUSED_COMBINE");
