@@ -110,4 +110,9 @@ struct AttnArgs {
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan);
 
+// Tensor-core (tcgen05) causal prefill for query blocks of >= 128 rows per kv head
+// (yf_prefill_tc.cu); needs no workspace.
+bool prefill_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q);
+int launch_prefill_tc(const AttnArgs& a);
+
 }  // namespace yf

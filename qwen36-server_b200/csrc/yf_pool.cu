@@ -357,6 +357,7 @@ static int check_attn(const yf_pool* pool, int32_t layer, const void* q, int32_t
 
 size_t yf_attn_workspace_size(const yf_pool* pool, int32_t hq, int32_t batch, int32_t max_q, int32_t max_k) {
     if (!pool || batch <= 0 || hq < pool->desc.n_kv_heads || hq % pool->desc.n_kv_heads) return 0;
+    if (max_q > 1 && prefill_tc_applies(pool, hq, max_q)) return 0;
     return plan_split(pool, hq, batch, max_q, max_k).ws_bytes;
 }
 
@@ -365,8 +366,9 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
                     int32_t max_k, float scale, void* out, void* ws, size_t ws_bytes, void* stream) {
     const int rc = check_attn(pool, layer, q, hq, cu_k, bt, max_blocks, batch, max_q, max_k, scale, out);
     if (rc || batch == 0) return rc;
+    const bool tc = cu_q && prefill_tc_applies(pool, hq, max_q);
     const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k);
-    if (plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
+    if (!tc && plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
         return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", plan.ws_bytes,
                     ws ? ws_bytes : (size_t)0);
     AttnArgs a;
@@ -386,6 +388,7 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     a.workspace = ws;
     a.workspace_bytes = ws_bytes;
     a.stream = static_cast<cudaStream_t>(stream);
+    if (tc) return launch_prefill_tc(a);
     return launch_splitkv(a, plan);
 }
 
