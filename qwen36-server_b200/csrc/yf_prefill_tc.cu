@@ -6,19 +6,19 @@
 // QK_INT8_PREFILL described at docs/research/2026-09-16-head-to-head-llamacpp-and-phase-profile.md:3627-3634):
 // query row i of an entry sees keys 0 .. Tk - Tq + i.
 //
-// One CTA (128 threads) = one entry, one kv head, 128 query rows = 128/G query positions x
-// the G q heads of the kv head (GQA folded into M, so every key tile is dequantized once for
-// all of them).  Per 64-key tile:
-//   1. lane 0 of warp 0 bulk-copies the four 16-token pool tiles (K+V int8 + scales, one
-//      contiguous block each) into a raw staging buffer, double-buffered one tile ahead;
-//   2. all threads dequantize K into f16 [key][dim] and V into f16 V^T [dim][key], both in
-//      the K-major 128-byte-swizzled shared-memory layout the MMA descriptors describe;
-//   3. one thread issues S = Q K^T (M=128 rows, N=64 keys, K=128 dims: 8 x tcgen05.mma
-//      kind::f16, f32 accumulator in TMEM) and commits to an mbarrier;
-//   4. thread r (TMEM lane r) loads its row of S, applies the scale, the causal mask and
-//      an online base-2 softmax with lazy rescale, and writes its row of P (f16) over K;
-//      when a row's max moved, every thread rescales its TMEM lane of O^T;
-//   5. one thread issues O^T += V^T P^T (M=128 dims, N=128 rows, K=64 keys: 4 MMAs).
+// One CTA = one entry, one kv head, 128 query rows = 128/G query positions x the G q heads
+// of the kv head (GQA folded into M, so every key tile is dequantized once for all of them).
+// The CTA's nine warps are specialised and hand 64-key tiles to each other through
+// mbarriers, double-buffered so that the stages of consecutive tiles overlap:
+//   * control warp (lane 0): bulk-copies the four 16-token pool tiles of a key tile (K+V int8
+//     + scales, one contiguous block each) into a raw staging buffer two tiles ahead, and
+//     issues the MMAs: S = Q K^T (M=128 rows, N=64 keys, K=128 dims: 8 x tcgen05.mma
+//     kind::f16, f32 in TMEM) and O^T += V^T P^T (M=128 dims, N=128 rows, K=64 keys: 4 MMAs);
+//   * 4 dequant warps: int8 K -> f16 [key][dim], int8 V -> f16 V^T [dim][key], both in the
+//     K-major 128-byte-swizzled layout the MMA descriptors describe;
+//   * 4 softmax warps: thread r owns query row r (TMEM lane r of S): scale, causal mask,
+//     online base-2 softmax with lazy rescale, P (f16) to shared memory; when a row's max
+//     moved they rescale O^T in TMEM (thread d owns lane d) before the next PV.
 // At the end thread d reads lane d of O^T (all 128 rows) and writes out[row][d] / l[row].
 #include <cstdint>
 #include <cstdlib>
@@ -29,23 +29,25 @@
 namespace yf {
 namespace {
 
-constexpr int kPfThreads = 128;
 constexpr int kPfRows = 128;     // query rows per CTA (M of S, N of O^T)
 constexpr int kPfKeys = 64;      // keys per tile (N of S, K of O^T)
 constexpr int kPfD = 128;        // head dim (K of S, M of O^T)
-constexpr int kPfTmemCols = 256; // S: cols [0,64), O^T: cols [64,192)
+constexpr int kPfTmemCols = 256; // S[2]: cols [0,128), O^T: cols [128,256)
 constexpr float kPfRescale = 8.0f;  // lazy rescale threshold (base 2), as in the decode kernels
 
-// shared-memory map (bytes from a 1024-aligned base)
-constexpr int kSmQ = 0;                        // Q  [128 rows][128 d] f16, 2 column blocks x 16 KB
-constexpr int kSmKP = kSmQ + 32768;            // K  [64 keys][128 d] f16 (2 x 8 KB); later P [128 rows][64 keys]
-constexpr int kSmVt = kSmKP + 16384;           // V^T [128 d][64 keys] f16
-constexpr int kSmRaw = kSmVt + 16384;          // 2 x 4 raw pool tiles (4352 B each)
-constexpr int kRawTileBytes = 4352;            // D=128, group 32
-constexpr int kRawBytes = 4 * kRawTileBytes;   // one 64-key tile
+// shared-memory map (bytes from a 1024-aligned base); [2] = double buffer
+constexpr int kSmQ = 0;                         // Q   [128 rows][128 d] f16: 2 column blocks x 16 KB
+constexpr int kSmK = kSmQ + 32768;              // K   [2][64 keys][128 d] f16 (2 column blocks x 8 KB)
+constexpr int kSmVt = kSmK + 2 * 16384;         // V^T [2][128 d][64 keys] f16
+constexpr int kSmP = kSmVt + 2 * 16384;         // P   [2][128 rows][64 keys] f16
+constexpr int kSmRaw = kSmP + 2 * 16384;        // raw [2][4 pool tiles x 4352 B]
+constexpr int kRawTileBytes = 4352;             // D=128, group 32
+constexpr int kRawBytes = 4 * kRawTileBytes;    // one 64-key tile
 constexpr int kSmMisc = kSmRaw + 2 * kRawBytes;
-constexpr int kSmBytes = kSmMisc + 2048;       // misc: barriers, tmem address, alpha, 1/l, flags
-constexpr int kSmAlloc = kSmBytes + 1024;      // + alignment slack
+constexpr int kSmBytes = kSmMisc + 2048;        // barriers, tmem address, alpha[2][128], 1/l, flags
+constexpr int kSmAlloc = kSmBytes + 1024;       // + alignment slack
+constexpr int kPfWarps = 9;                     // 4 softmax, 4 dequant, 1 control
+constexpr int kPfBlock = kPfWarps * 32;
 
 struct PrefillParams {
     const uint8_t* layer_base;
@@ -150,19 +152,48 @@ __device__ __forceinline__ uint32_t dq2(uint32_t biased, int sel, uint32_t scale
     return h2mul(h, scale2);
 }
 
-__global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const PrefillParams p) {
+// True for every thread of the 4 softmax warps when any of them passes true.
+__device__ __forceinline__ bool softmax_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Bars {
+    uint64_t raw_full[2], raw_free[2], kv_full[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+};
+
+// Bounded wait for the use-th completion (0-based) of `bar`.  A wait that gives up raises the
+// CTA's abort flag, after which every role skips its remaining waits and drains quickly.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int* abort) {
+    if (*abort) return false;
+    for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+        if (mbar_try_wait(bar, (uint32_t)use & 1u)) return true;
+        if ((i & 255u) == 255u && *abort) return false;
+    }
+    *abort = 1;
+    return false;
+}
+
+__global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t sraw = smem_u32(smem_raw);
     const uint32_t sbase = (sraw + 1023u) & ~1023u;
     uint8_t* base = smem_raw + (sbase - sraw);
-    uint64_t* bar_mma = reinterpret_cast<uint64_t*>(base + kSmMisc);
-    uint64_t* bar_raw = bar_mma + 1;  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kSmMisc + 64);
-    float* s_alpha = reinterpret_cast<float*>(base + kSmMisc + 128);   // [128]
-    float* s_linv = s_alpha + kPfRows;                                    // [128]
-    uint8_t* s_valid = reinterpret_cast<uint8_t*>(s_linv + kPfRows);    // [2][4] pool-tile flags
+    Bars* bars = reinterpret_cast<Bars*>(base + kSmMisc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kSmMisc + 256);
+    float* s_alpha = reinterpret_cast<float*>(base + kSmMisc + 512);     // [2][128]
+    float* s_linv = s_alpha + 2 * kPfRows;                                  // [128]
+    uint8_t* s_valid = reinterpret_cast<uint8_t*>(s_linv + kPfRows);      // [2][4] pool-tile flags
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_valid + 16);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.z, h = blockIdx.y;
     const int ppb = kPfRows / p.G;  // query positions per CTA
 
@@ -181,185 +212,247 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const Prefill
     if (pos0 >= Tq) return;
     const int npos = min(ppb, Tq - pos0);
     const int rows = npos * p.G;
-    const int kv0 = Tk - Tq;                     // keys before the chunk
+    const int kv0 = Tk - Tq;  // keys before the chunk
     const int kv_hi = max(0, min(Tk, kv0 + pos0 + npos));
+    const int kv_lo = max(0, min(Tk, kv0 + pos0 + 1));  // every row sees keys [0, kv_lo)
     const int n_kt = (kv_hi + kPfKeys - 1) / kPfKeys;
-    const int pt_total = (Tk + 15) / 16;         // pool tiles that hold keys
+    const int pt_total = (Tk + 15) / 16;
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
     const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
     const long long page_stride = p.phb * p.H;
 
-    // this thread's softmax row
-    const int my_row = tid;
-    const bool row_live = my_row < rows;
-    const int my_kvlen = row_live ? max(0, min(Tk, kv0 + pos0 + my_row / p.G + 1)) : 0;
-
-    // ---- set-up: barriers, TMEM, Q tile
+    // ---- set-up
     if (tid == 0) {
-        mbar_init(bar_mma, 1);
-        mbar_init(&bar_raw[0], 1);
-        mbar_init(&bar_raw[1], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->raw_full[i], 1);
+            mbar_init(&bars->raw_free[i], 4);
+            mbar_init(&bars->kv_full[i], 4);
+            mbar_init(&bars->s_full[i], 1);
+            mbar_init(&bars->s_free[i], 4);
+            mbar_init(&bars->p_full[i], 4);
+            mbar_init(&bars->pv_done[i], 1);
+        }
+        mbar_init(&bars->drain, 1);
+        *s_abort = 0;
         fence_mbar_init();
     }
-    if (warp == 0) {
+    if (warp == 8) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kPfTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    {
+    if (warp < 4) {
         // Q row `tid` (position pos0 + tid/G, head h*G + tid%G) into the SW128 Q tile
-        uint4 zero = make_uint4(0, 0, 0, 0);
+        const bool live = tid < rows;
+        const uint4 zero = make_uint4(0, 0, 0, 0);
         const uint4* qp = nullptr;
-        if (row_live)
+        if (live)
             qp = reinterpret_cast<const uint4*>(
-                p.q + ((size_t)(qrow0 + pos0 + my_row / p.G) * p.Hq + (size_t)h * p.G + my_row % p.G) * kPfD);
+                p.q + ((size_t)(qrow0 + pos0 + tid / p.G) * p.Hq + (size_t)h * p.G + tid % p.G) * kPfD);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) sts128(sbase + kSmQ + sw128_off(my_row, c, kPfRows), row_live ? __ldg(qp + c) : zero);
+        for (int c = 0; c < 16; ++c) sts128(sbase + kSmQ + sw128_off(tid, c, kPfRows), live ? __ldg(qp + c) : zero);
+        fence_proxy_async_smem();
     }
-
-    // lane 0 of warp 0: copy the four pool tiles of key tile `kt` into raw buffer `buf`
-    auto issue_raw = [&](int kt, int buf) {
-        uint8_t* dst = base + kSmRaw + buf * kRawBytes;
-        uint32_t bytes = 0;
-        const uint8_t* src[4];
-        for (int j = 0; j < 4; ++j) {
-            const int pt = kt * 4 + j;
-            src[j] = nullptr;
-            if (pt < pt_total) {
-                const uint32_t page = __ldg(btrow + pt / p.tpp);
-                if (page < (uint32_t)p.n_pages)
-                    src[j] = head_base + (size_t)page * page_stride + (pt % p.tpp) * kRawTileBytes;
-                else
-                    atomicOr(p.status, YF_DEV_BAD_PAGE);
-            }
-            s_valid[buf * 4 + j] = src[j] != nullptr;
-            bytes += src[j] ? kRawTileBytes : 0;
-        }
-        mbar_arrive_expect_tx(&bar_raw[buf], bytes);
-        for (int j = 0; j < 4; ++j)
-            if (src[j]) bulk_g2s(dst + j * kRawTileBytes, src[j], kRawTileBytes, &bar_raw[buf]);
-    };
-
-    fence_proxy_async_smem();  // Q tile (generic writes) before the MMAs read it
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_S = tmem;
-    const uint32_t tmem_O = tmem + 64;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    if (tid == 0 && n_kt > 0) issue_raw(0, 0);
-
-    constexpr uint32_t IDESC_S = umma_idesc_f16(kPfRows, kPfKeys);
-    constexpr uint32_t IDESC_O = umma_idesc_f16(kPfD, kPfRows);
-    float m_run = -INFINITY, l_run = 0.f;
     bool timed_out = false;
 
-    for (int it = 0; it < n_kt; ++it) {
-        const int buf = it & 1;
-        if (tid == 0 && it + 1 < n_kt) issue_raw(it + 1, buf ^ 1);
-        if (!mbar_wait(&bar_raw[buf], (uint32_t)(it >> 1) & 1u)) timed_out = true;
-        const uint8_t* raw = base + kSmRaw + buf * kRawBytes;
-
-        // ---- 2. dequantize K -> [key][d] and V -> V^T [d][key] (f16, SW128)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            // K: 16-byte word w of the tile = tokens g, g+8 x dims 32cb+8tig .. +7
-            const int w = tid + i * kPfThreads;
-            const int j = w >> 7, cb = (w & 127) >> 5, ln = w & 31, g = ln >> 2, tig = ln & 3;
-            const uint8_t* T = raw + j * kRawTileBytes;
-            uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
-            if (s_valid[buf * 4 + j]) {
-                const uint4 kw = lds128(T + cb * 512 + ln * 16);
-                // K scales [g][half][group]: token g is half 0, token g+8 half 1
-                const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2) * 4 + cb));
-                const uint16_t s1 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2 + 1) * 4 + cb));
-                const uint32_t d0 = (uint32_t)s0 | ((uint32_t)s0 << 16), d1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
-                const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
-                o0 = make_uint4(dq2(x0, 0, d0), dq2(x0, 1, d0), dq2(x1, 0, d0), dq2(x1, 1, d0));
-                o1 = make_uint4(dq2(z0, 0, d1), dq2(z0, 1, d1), dq2(z1, 0, d1), dq2(z1, 1, d1));
-            }
-            const int t0 = j * 16 + g, c = cb * 4 + tig;  // 16-byte chunk = dims 8c .. 8c+7
-            sts128(sbase + kSmKP + sw128_off(t0, c, kPfKeys), o0);
-            sts128(sbase + kSmKP + sw128_off(t0 + 8, c, kPfKeys), o1);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            // V^T row d, keys 16j .. 16j+15: the four lanes (g', tig=0..3) of dim d hold
-            // tokens {2tig, 2tig+8, 2tig+1, 2tig+9} in one 32-bit word each
-            const int item = tid + i * kPfThreads;
-            const int j = item >> 7, d = item & 127;
-            const int m = d >> 4, gp = d & 7, dh = (d >> 3) & 1;
-            const uint8_t* T = raw + j * kRawTileBytes;
-            uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-            if (s_valid[buf * 4 + j]) {
-                const uint8_t* vb = T + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + dh) * 4;
-                uint32_t wv[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) wv[t] = lds32(vb + (gp * 4 + t) * 16);
-                // keys 0..7 = bytes 0,2 of wv[0..3]; keys 8..15 = bytes 1,3
-                const uint32_t k03 = __byte_perm(wv[0], wv[1], 0x6420), k47 = __byte_perm(wv[2], wv[3], 0x6420);
-                const uint32_t k8b = __byte_perm(wv[0], wv[1], 0x7531), kcf = __byte_perm(wv[2], wv[3], 0x7531);
-                // V scales of group s = d/32 for tokens 0..15: [tig][s][j] pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
-                const int s = d >> 5;
-                uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
-                const uint8_t* vs = T + 32 * kPfD + 128 + s * 8;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const uint2 q = lds64(vs + t * 4 * 8);  // .x = (2t, 2t+8), .y = (2t+1, 2t+9)
-                    sp[t] = __byte_perm(q.x, q.y, 0x5410);       // (2t, 2t+1)
-                    sp[4 + t] = __byte_perm(q.x, q.y, 0x7632);   // (2t+8, 2t+9)
+    if (warp == 8) {
+        // ================= control: bulk copies and MMAs =================
+        if (lane == 0) {
+            auto issue_raw = [&](int kt, int buf) {
+                uint8_t* dst = base + kSmRaw + buf * kRawBytes;
+                uint32_t bytes = 0;
+                const uint8_t* src[4];
+                for (int j = 0; j < 4; ++j) {
+                    const int pt = kt * 4 + j;
+                    src[j] = nullptr;
+                    if (pt < pt_total) {
+                        const uint32_t page = __ldg(btrow + pt / p.tpp);
+                        if (page < (uint32_t)p.n_pages)
+                            src[j] = head_base + (size_t)page * page_stride + (pt % p.tpp) * kRawTileBytes;
+                        else
+                            atomicOr(p.status, YF_DEV_BAD_PAGE);
+                    }
+                    s_valid[buf * 4 + j] = src[j] != nullptr;
+                    bytes += src[j] ? kRawTileBytes : 0;
                 }
-                const uint32_t a = bias8(k03), bq = bias8(k47), c8 = bias8(k8b), cf = bias8(kcf);
-                lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
-                hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
+                mbar_arrive_expect_tx(&bars->raw_full[buf], bytes);
+                for (int j = 0; j < 4; ++j)
+                    if (src[j]) bulk_g2s(dst + j * kRawTileBytes, src[j], kRawTileBytes, &bars->raw_full[buf]);
+            };
+            constexpr uint32_t IDESC_S = umma_idesc_f16(kPfRows, kPfKeys);
+            constexpr uint32_t IDESC_O = umma_idesc_f16(kPfD, kPfRows);
+            auto issue_pv = [&](int j) {
+                const int bj = j & 1;
+                if (!wait_phase(&bars->p_full[bj], j >> 1, s_abort)) timed_out = true;
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kPfKeys / 16; ++ks) {
+                    const uint64_t a = umma_desc_sw128(sbase + kSmVt + bj * 16384 + ks * 32);
+                    const uint64_t bd = umma_desc_sw128(sbase + kSmP + bj * 16384 + ks * 32);
+                    umma_f16(tmem + 128, a, bd, IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                umma_commit(&bars->pv_done[bj]);
+            };
+            if (n_kt > 0) issue_raw(0, 0);
+            if (n_kt > 1) issue_raw(1, 1);
+            int issued = 0;  // key tiles whose QK was issued
+            for (int it = 0; it < n_kt && !*s_abort; ++it, ++issued) {
+                const int b2 = it & 1;
+                if (!wait_phase(&bars->kv_full[b2], it >> 1, s_abort)) timed_out = true;
+                if (it >= 2 && !wait_phase(&bars->s_free[b2], (it - 2) >> 1, s_abort)) timed_out = true;
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kPfD / 16; ++ks) {
+                    const uint64_t a = umma_desc_sw128(sbase + kSmQ + (ks >> 2) * (kPfRows * 128) + (ks & 3) * 32);
+                    const uint64_t bd =
+                        umma_desc_sw128(sbase + kSmK + b2 * 16384 + (ks >> 2) * (kPfKeys * 128) + (ks & 3) * 32);
+                    umma_f16(tmem + b2 * 64, a, bd, IDESC_S, ks > 0);
+                }
+                umma_commit(&bars->s_full[b2]);
+                if (it >= 1) issue_pv(it - 1);
+                if (it + 2 < n_kt) {
+                    if (!wait_phase(&bars->raw_free[b2], it >> 1, s_abort)) timed_out = true;
+                    issue_raw(it + 2, b2);
+                }
             }
-            sts128(sbase + kSmVt + sw128_off(d, 2 * j, kPfD), lo);
-            sts128(sbase + kSmVt + sw128_off(d, 2 * j + 1, kPfD), hi);
+            if (issued > 0 && !*s_abort) issue_pv(issued - 1);
+            // every MMA of this CTA has completed before TMEM is released
+            umma_commit(&bars->drain);
+            (void)mbar_wait(&bars->drain, 0u);
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- 3. S = Q K^T
-        if (tid == 0) {
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ================= dequant: raw pool tiles -> f16 K and V^T =================
+        const int t = tid - 128;
+        for (int it = 0; it < n_kt; ++it) {
+            const int b2 = it & 1;
+            if (!wait_phase(&bars->raw_full[b2], it >> 1, s_abort)) timed_out = true;
+            if (it >= 2) {  // K[b2] was read by QK(it-2), V^T[b2] by PV(it-2)
+                if (!wait_phase(&bars->s_full[b2], (it - 2) >> 1, s_abort)) timed_out = true;
+                if (!wait_phase(&bars->pv_done[b2], (it - 2) >> 1, s_abort)) timed_out = true;
+            }
+            const uint8_t* raw = base + kSmRaw + b2 * kRawBytes;
+            const uint32_t kdst = sbase + kSmK + b2 * 16384, vdst = sbase + kSmVt + b2 * 16384;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                // K: 16-byte word w of pool tile j = tokens g, g+8 x dims 32cb+8tig .. +7
+                const int w = t + i * 128;
+                const int j = w >> 7, cb = (w & 127) >> 5, ln = w & 31, g = ln >> 2, tig = ln & 3;
+                const uint8_t* T = raw + j * kRawTileBytes;
+                uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
+                if (s_valid[b2 * 4 + j]) {
+                    const uint4 kw = lds128(T + cb * 512 + ln * 16);
+                    // K scales [g][half][group]: token g is half 0, token g+8 half 1
+                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2) * 4 + cb));
+                    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2 + 1) * 4 + cb));
+                    const uint32_t d0 = (uint32_t)s0 | ((uint32_t)s0 << 16), d1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
+                    const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+                    o0 = make_uint4(dq2(x0, 0, d0), dq2(x0, 1, d0), dq2(x1, 0, d0), dq2(x1, 1, d0));
+                    o1 = make_uint4(dq2(z0, 0, d1), dq2(z0, 1, d1), dq2(z1, 0, d1), dq2(z1, 1, d1));
+                }
+                const int t0 = j * 16 + g, c = cb * 4 + tig;  // 16-byte chunk = dims 8c .. 8c+7
+                sts128(kdst + sw128_off(t0, c, kPfKeys), o0);
+                sts128(kdst + sw128_off(t0 + 8, c, kPfKeys), o1);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                // V^T row d, keys 16j .. 16j+15: the four lanes (g', tig=0..3) of dim d hold
+                // tokens {2tig, 2tig+8, 2tig+1, 2tig+9} in one 32-bit word each
+                const int item = t + i * 128;
+                const int j = item >> 7, d = item & 127;
+                const int m = d >> 4, gp = d & 7, dh = (d >> 3) & 1;
+                const uint8_t* T = raw + j * kRawTileBytes;
+                uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+                if (s_valid[b2 * 4 + j]) {
+                    const uint8_t* vb = T + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + dh) * 4;
+                    uint32_t wv[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) wv[q] = lds32(vb + (gp * 4 + q) * 16);
+                    // keys 0..7 = bytes 0,2 of wv[0..3]; keys 8..15 = bytes 1,3
+                    const uint32_t k03 = __byte_perm(wv[0], wv[1], 0x6420), k47 = __byte_perm(wv[2], wv[3], 0x6420);
+                    const uint32_t k8b = __byte_perm(wv[0], wv[1], 0x7531), kcf = __byte_perm(wv[2], wv[3], 0x7531);
+                    // V scales [tig][group][j]: pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
+                    const int sg = d >> 5;
+                    uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
+                    const uint8_t* vs = T + 32 * kPfD + 128 + sg * 8;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint2 pr = lds64(vs + q * 32);
+                        sp[q] = __byte_perm(pr.x, pr.y, 0x5410);
+                        sp[4 + q] = __byte_perm(pr.x, pr.y, 0x7632);
+                    }
+                    const uint32_t a = bias8(k03), bq = bias8(k47), c8 = bias8(k8b), cf = bias8(kcf);
+                    lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
+                    hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
+                }
+                sts128(vdst + sw128_off(d, 2 * j, kPfD), lo);
+                sts128(vdst + sw128_off(d, 2 * j + 1, kPfD), hi);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&bars->kv_full[b2]);
+                mbar_arrive(&bars->raw_free[b2]);
+            }
+        }
+    } else {
+        // ================= softmax: thread = query row =================
+        const int row = tid;
+        const int kvlen = row < rows ? max(0, min(Tk, kv0 + pos0 + row / p.G + 1)) : 0;
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        float m_run = -INFINITY, l_run = 0.f;
+        for (int it = 0; it < n_kt; ++it) {
+            const int b2 = it & 1;
+            if (!wait_phase(&bars->s_full[b2], it >> 1, s_abort)) timed_out = true;
             tc_fence_after();
-#pragma unroll
-            for (int ks = 0; ks < kPfD / 16; ++ks) {
-                const uint64_t a = umma_desc_sw128(sbase + kSmQ + (ks >> 2) * (kPfRows * 128) + (ks & 3) * 32);
-                const uint64_t bd = umma_desc_sw128(sbase + kSmKP + (ks >> 2) * (kPfKeys * 128) + (ks & 3) * 32);
-                umma_f16(tmem_S, a, bd, IDESC_S, ks > 0);
-            }
-            umma_commit(bar_mma);
-        }
-        if (!mbar_wait(bar_mma, 0u)) timed_out = true;
-        tc_fence_after();
-
-        // ---- 4. softmax of row tid; P over K
-        bool need = false;
-        float alpha = 1.f;
-        {
             float s[64];
-            float* s0 = s;
-            tmem_ld32(tmem_S + lane_off + 0, *reinterpret_cast<float(*)[32]>(s0));
-            tmem_ld32(tmem_S + lane_off + 32, *reinterpret_cast<float(*)[32]>(s0 + 32));
+            tmem_ld32(tmem + b2 * 64 + lane_off, *reinterpret_cast<float(*)[32]>(s));
+            tmem_ld32(tmem + b2 * 64 + 32 + lane_off, *reinterpret_cast<float(*)[32]>(s + 32));
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->s_free[b2]);
+
             const int key0 = it * kPfKeys;
-            float mx = -INFINITY;
+            // pool tiles of this key tile that hold keys (read from the block table: the control
+            // warp already reuses its flags for the tile two ahead)
+            bool pv[4];
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                const int key = key0 + c;
-                const bool ok = key < my_kvlen && s_valid[buf * 4 + (c >> 4)];
-                s[c] = ok ? s[c] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, s[c]);
+            for (int j = 0; j < 4; ++j) {
+                const int pt = it * 4 + j;
+                pv[j] = pt < pt_total && __ldg(btrow + pt / p.tpp) < (uint32_t)p.n_pages;
             }
+            const bool full = key0 + kPfKeys <= kv_lo && pv[0] && pv[1] && pv[2] && pv[3];
+            float mx = -INFINITY;
+            if (full) {
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    s[c] *= p.scale_log2;
+                    mx = fmaxf(mx, s[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    const bool ok = key0 + c < kvlen && pv[c >> 4];
+                    s[c] = ok ? s[c] * p.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, s[c]);
+                }
+            }
+            float alpha = 1.f;
+            bool need = false;
             if (mx > m_run + kPfRescale) {
                 alpha = fast_exp2(m_run - mx);
                 m_run = mx;
                 l_run *= alpha;
-                need = true;
+                need = it > 0;
             }
             const float muse = m_run == -INFINITY ? 0.f : m_run;
+            if (it >= 2 && !wait_phase(&bars->pv_done[b2], (it - 2) >> 1, s_abort)) timed_out = true;  // P[b2] free
+            const uint32_t pdst = sbase + kSmP + b2 * 16384;
             float sum = 0.f;
 #pragma unroll
             for (int c8 = 0; c8 < 8; ++c8) {
@@ -370,69 +463,58 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const Prefill
                     sum += p0 + p1;
                     pk[e] = pack_h2(p0, p1);
                 }
-                sts128(sbase + kSmKP + sw128_off(my_row, c8, kPfRows), make_uint4(pk[0], pk[1], pk[2], pk[3]));
+                sts128(pdst + sw128_off(row, c8, kPfRows), make_uint4(pk[0], pk[1], pk[2], pk[3]));
             }
             l_run += sum;
+            s_alpha[b2 * kPfRows + row] = alpha;
+            if (softmax_any(need)) {
+                // PV(it-1) must have landed before O^T is rescaled; thread d owns lane d
+                if (!wait_phase(&bars->pv_done[(it - 1) & 1], (it - 1) >> 1, s_abort)) timed_out = true;
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < kPfRows; c0 += 32) {
+                    float o[32];
+                    tmem_ld32(tmem + 128 + c0 + lane_off, o);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] *= s_alpha[b2 * kPfRows + c0 + e];
+                    tmem_st32(tmem + 128 + c0 + lane_off, o);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->p_full[b2]);
         }
-        s_alpha[tid] = alpha;
-        const bool any_need = __syncthreads_or(need && it > 0);
-        if (any_need) {
-            // thread d rescales lane d of O^T: column r is query row r
+        // ---- epilogue: thread d writes dim d of every row
+        s_linv[row] = l_run > 0.f ? 1.f / l_run : 0.f;
+        if (n_kt > 0 && !wait_phase(&bars->pv_done[(n_kt - 1) & 1], (n_kt - 1) >> 1, s_abort)) timed_out = true;
+        tc_fence_after();
+        softmax_sync();
+        const int d = tid;
+        if (n_kt > 0) {
 #pragma unroll
             for (int c0 = 0; c0 < kPfRows; c0 += 32) {
                 float o[32];
-                tmem_ld32(tmem_O + lane_off + c0, o);
+                tmem_ld32(tmem + 128 + c0 + lane_off, o);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) o[e] *= s_alpha[c0 + e];
-                tmem_st32(tmem_O + lane_off + c0, o);
-            }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- 5. O^T += V^T P^T
-        if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            for (int ks = 0; ks < kPfKeys / 16; ++ks) {
-                const uint64_t a = umma_desc_sw128(sbase + kSmVt + ks * 32);
-                const uint64_t bd = umma_desc_sw128(sbase + kSmKP + ks * 32);
-                umma_f16(tmem_O, a, bd, IDESC_O, (it > 0 || ks > 0) ? 1u : 0u);
-            }
-            umma_commit(bar_mma);
-        }
-        if (!mbar_wait(bar_mma, 1u)) timed_out = true;
-        tc_fence_after();
-    }
-    if (timed_out) atomicOr(p.status, YF_DEV_TIMEOUT);
-
-    // ---- epilogue: thread d writes dim d of every row
-    s_linv[tid] = l_run > 0.f ? 1.f / l_run : 0.f;
-    __syncthreads();
-    if (n_kt > 0) {
-        const int d = tid;
-#pragma unroll
-        for (int c0 = 0; c0 < kPfRows; c0 += 32) {
-            float o[32];
-            tmem_ld32(tmem_O + lane_off + c0, o);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int r = c0 + e;
-                if (r < rows) {
-                    __half* op = p.out + ((size_t)(qrow0 + pos0 + r / p.G) * p.Hq + (size_t)h * p.G + r % p.G) * kPfD + d;
-                    *op = __float2half_rn(o[e] * s_linv[r]);
+                for (int e = 0; e < 32; ++e) {
+                    const int r = c0 + e;
+                    if (r < rows)
+                        p.out[((size_t)(qrow0 + pos0 + r / p.G) * p.Hq + (size_t)h * p.G + r % p.G) * kPfD + d] =
+                            __float2half_rn(o[e] * s_linv[r]);
                 }
             }
+        } else {
+            for (int r = 0; r < rows; ++r)
+                p.out[((size_t)(qrow0 + pos0 + r / p.G) * p.Hq + (size_t)h * p.G + r % p.G) * kPfD + d] =
+                    __float2half_rn(0.f);
         }
-    } else {
-        for (int r = 0; r < rows; ++r)
-            p.out[((size_t)(qrow0 + pos0 + r / p.G) * p.Hq + (size_t)h * p.G + r % p.G) * kPfD + tid] = __float2half_rn(0.f);
     }
+    if (timed_out) atomicOr(p.status, YF_DEV_TIMEOUT);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 8) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols) : "memory");
     }
@@ -479,7 +561,7 @@ int launch_prefill_tc(const AttnArgs& a) {
     const int ppb = kPfRows / p.G;
     const dim3 grid((a.max_seqlen_q + ppb - 1) / ppb, d.n_kv_heads, a.batch);
     if (grid.x > 0x7fffffffu) return fail(YF_E_UNSUPPORTED, "too many query rows");
-    prefill_tc_kernel<<<grid, kPfThreads, kSmAlloc, a.stream>>>(p);
+    prefill_tc_kernel<<<grid, kPfBlock, kSmAlloc, a.stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? YF_OK : cuda_fail(e, "prefill_tc launch");
 }
