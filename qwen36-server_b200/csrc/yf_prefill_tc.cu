@@ -35,16 +35,18 @@ constexpr int kPfD = 128;        // head dim (K of S, M of O^T)
 constexpr int kPfTmemCols = 256; // S[2]: cols [0,128), O^T: cols [128,256)
 constexpr float kPfRescale = 8.0f;  // lazy rescale threshold (base 2), as in the decode kernels
 
-// shared-memory map (bytes from a 1024-aligned base); [2] = double buffer
+// shared-memory map (bytes from a 1024-aligned base); [n] = ring of n buffers
 constexpr int kSmQ = 0;                         // Q   [128 rows][128 d] f16: 2 column blocks x 16 KB
 constexpr int kSmK = kSmQ + 32768;              // K   [2][64 keys][128 d] f16 (2 column blocks x 8 KB)
-constexpr int kSmVt = kSmK + 2 * 16384;         // V^T [2][128 d][64 keys] f16
-constexpr int kSmP = kSmVt + 2 * 16384;         // P   [2][128 rows][64 keys] f16
-constexpr int kSmRaw = kSmP + 2 * 16384;        // raw [2][4 pool tiles x 4352 B]
+constexpr int kSmVt = kSmK + 2 * 16384;         // V^T [3][128 d][64 keys] f16
+constexpr int kSmP = kSmVt + 3 * 16384;         // P   [2][128 rows][64 keys] f16
+constexpr int kSmRaw = kSmP + 2 * 16384;        // raw [3][4 pool tiles x 4352 B]
 constexpr int kRawTileBytes = 4352;             // D=128, group 32
 constexpr int kRawBytes = 4 * kRawTileBytes;    // one 64-key tile
-constexpr int kSmMisc = kSmRaw + 2 * kRawBytes;
-constexpr int kSmBytes = kSmMisc + 2048;        // barriers, tmem address, alpha[2][128], 1/l, flags
+constexpr int kSmMisc = kSmRaw + 3 * kRawBytes;
+// misc: Bars at +0 (< 256 B), TMEM address at +256, alpha[2][128] at +512, 1/l[128] at +1536,
+// pool-tile flags [3][4] at +2048, abort word at +2064
+constexpr int kSmBytes = kSmMisc + 4096;
 constexpr int kSmAlloc = kSmBytes + 1024;       // + alignment slack
 constexpr int kPfWarps = 9;                     // 4 softmax, 4 dequant, 1 control
 constexpr int kPfBlock = kPfWarps * 32;
@@ -166,8 +168,20 @@ __device__ __forceinline__ bool softmax_any(bool v) {
 __device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct Bars {
-    uint64_t raw_full[2], raw_free[2], kv_full[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+    uint64_t raw_full[3], raw_free[3], vt_free[3], kv_full[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain;
 };
+static_assert(sizeof(Bars) <= 256, "barrier area");
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, int use) {  // non-blocking: use-th completion done?
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"((uint32_t)use & 1u)
+        : "memory");
+    return ok != 0;
+}
 
 // Bounded wait for the use-th completion (0-based) of `bar`.  A wait that gives up raises the
 // CTA's abort flag, after which every role skips its remaining waits and drains quickly.
@@ -190,7 +204,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kSmMisc + 256);
     float* s_alpha = reinterpret_cast<float*>(base + kSmMisc + 512);     // [2][128]
     float* s_linv = s_alpha + 2 * kPfRows;                                  // [128]
-    uint8_t* s_valid = reinterpret_cast<uint8_t*>(s_linv + kPfRows);      // [2][4] pool-tile flags
+    uint8_t* s_valid = reinterpret_cast<uint8_t*>(s_linv + kPfRows);      // [3][4] pool-tile flags
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_valid + 16);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -223,9 +237,12 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
 
     // ---- set-up
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < 3; ++i) {
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_free[i], 4);
+            mbar_init(&bars->vt_free[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->kv_full[i], 4);
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->s_free[i], 4);
@@ -286,41 +303,54 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
             };
             constexpr uint32_t IDESC_S = umma_idesc_f16(kPfRows, kPfKeys);
             constexpr uint32_t IDESC_O = umma_idesc_f16(kPfD, kPfRows);
-            auto issue_pv = [&](int j) {
-                const int bj = j & 1;
-                if (!wait_phase(&bars->p_full[bj], j >> 1, s_abort)) timed_out = true;
-                tc_fence_after();
-#pragma unroll
-                for (int ks = 0; ks < kPfKeys / 16; ++ks) {
-                    const uint64_t a = umma_desc_sw128(sbase + kSmVt + bj * 16384 + ks * 32);
-                    const uint64_t bd = umma_desc_sw128(sbase + kSmP + bj * 16384 + ks * 32);
-                    umma_f16(tmem + 128, a, bd, IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
+            // Polling loop: issue whichever of {next raw copy, next QK, next PV} is ready.
+            // QK runs at most 2 tiles ahead of PV (two S buffers; keeps every parity wait
+            // within one phase of its barrier).
+            int qk = 0, pv = 0, rw = 0;
+            uint32_t idle = 0;
+            while (pv < n_kt && !*s_abort) {
+                bool prog = false;
+                if (rw < n_kt && (rw < 3 || mbar_test(&bars->raw_free[rw % 3], rw / 3 - 1))) {
+                    issue_raw(rw, rw % 3);
+                    ++rw;
+                    prog = true;
                 }
-                umma_commit(&bars->pv_done[bj]);
-            };
-            if (n_kt > 0) issue_raw(0, 0);
-            if (n_kt > 1) issue_raw(1, 1);
-            int issued = 0;  // key tiles whose QK was issued
-            for (int it = 0; it < n_kt && !*s_abort; ++it, ++issued) {
-                const int b2 = it & 1;
-                if (!wait_phase(&bars->kv_full[b2], it >> 1, s_abort)) timed_out = true;
-                if (it >= 2 && !wait_phase(&bars->s_free[b2], (it - 2) >> 1, s_abort)) timed_out = true;
-                tc_fence_after();
+                if (qk < n_kt && qk < pv + 2 && mbar_test(&bars->kv_full[qk & 1], qk >> 1) &&
+                    (qk < 2 || mbar_test(&bars->s_free[qk & 1], (qk - 2) >> 1))) {
+                    const int b2 = qk & 1;
+                    tc_fence_after();
 #pragma unroll
-                for (int ks = 0; ks < kPfD / 16; ++ks) {
-                    const uint64_t a = umma_desc_sw128(sbase + kSmQ + (ks >> 2) * (kPfRows * 128) + (ks & 3) * 32);
-                    const uint64_t bd =
-                        umma_desc_sw128(sbase + kSmK + b2 * 16384 + (ks >> 2) * (kPfKeys * 128) + (ks & 3) * 32);
-                    umma_f16(tmem + b2 * 64, a, bd, IDESC_S, ks > 0);
+                    for (int ks = 0; ks < kPfD / 16; ++ks) {
+                        const uint64_t a = umma_desc_sw128(sbase + kSmQ + (ks >> 2) * (kPfRows * 128) + (ks & 3) * 32);
+                        const uint64_t bd =
+                            umma_desc_sw128(sbase + kSmK + b2 * 16384 + (ks >> 2) * (kPfKeys * 128) + (ks & 3) * 32);
+                        umma_f16(tmem + b2 * 64, a, bd, IDESC_S, ks > 0);
+                    }
+                    umma_commit(&bars->s_full[b2]);
+                    ++qk;
+                    prog = true;
                 }
-                umma_commit(&bars->s_full[b2]);
-                if (it >= 1) issue_pv(it - 1);
-                if (it + 2 < n_kt) {
-                    if (!wait_phase(&bars->raw_free[b2], it >> 1, s_abort)) timed_out = true;
-                    issue_raw(it + 2, b2);
+                if (pv < qk && mbar_test(&bars->p_full[pv & 1], pv >> 1)) {
+                    const int bp = pv & 1, bv = pv % 3;
+                    tc_fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < kPfKeys / 16; ++ks) {
+                        const uint64_t a = umma_desc_sw128(sbase + kSmVt + bv * 16384 + ks * 32);
+                        const uint64_t bd = umma_desc_sw128(sbase + kSmP + bp * 16384 + ks * 32);
+                        umma_f16(tmem + 128, a, bd, IDESC_O, (pv > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&bars->pv_done[bp]);
+                    umma_commit(&bars->vt_free[bv]);
+                    ++pv;
+                    prog = true;
+                }
+                if (prog) {
+                    idle = 0;
+                } else if (++idle > 4u * kMaxWaitIters) {
+                    *s_abort = 1;
+                    timed_out = true;
                 }
             }
-            if (issued > 0 && !*s_abort) issue_pv(issued - 1);
             // every MMA of this CTA has completed before TMEM is released
             umma_commit(&bars->drain);
             (void)mbar_wait(&bars->drain, 0u);
@@ -330,14 +360,13 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
         // ================= dequant: raw pool tiles -> f16 K and V^T =================
         const int t = tid - 128;
         for (int it = 0; it < n_kt; ++it) {
-            const int b2 = it & 1;
-            if (!wait_phase(&bars->raw_full[b2], it >> 1, s_abort)) timed_out = true;
-            if (it >= 2) {  // K[b2] was read by QK(it-2), V^T[b2] by PV(it-2)
-                if (!wait_phase(&bars->s_full[b2], (it - 2) >> 1, s_abort)) timed_out = true;
-                if (!wait_phase(&bars->pv_done[b2], (it - 2) >> 1, s_abort)) timed_out = true;
-            }
-            const uint8_t* raw = base + kSmRaw + b2 * kRawBytes;
-            const uint32_t kdst = sbase + kSmK + b2 * 16384, vdst = sbase + kSmVt + b2 * 16384;
+            const int b2 = it & 1, b3 = it % 3;
+            if (!wait_phase(&bars->raw_full[b3], it / 3, s_abort)) timed_out = true;
+            // K[b2] was read by QK(it-2), V^T[b3] by PV(it-3)
+            if (it >= 2 && !wait_phase(&bars->s_full[b2], (it - 2) >> 1, s_abort)) timed_out = true;
+            if (it >= 3 && !wait_phase(&bars->vt_free[b3], it / 3 - 1, s_abort)) timed_out = true;
+            const uint8_t* raw = base + kSmRaw + b3 * kRawBytes;
+            const uint32_t kdst = sbase + kSmK + b2 * 16384, vdst = sbase + kSmVt + b3 * 16384;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 // K: 16-byte word w of pool tile j = tokens g, g+8 x dims 32cb+8tig .. +7
@@ -345,7 +374,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                 const int j = w >> 7, cb = (w & 127) >> 5, ln = w & 31, g = ln >> 2, tig = ln & 3;
                 const uint8_t* T = raw + j * kRawTileBytes;
                 uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
-                if (s_valid[b2 * 4 + j]) {
+                if (s_valid[b3 * 4 + j]) {
                     const uint4 kw = lds128(T + cb * 512 + ln * 16);
                     // K scales [g][half][group]: token g is half 0, token g+8 half 1
                     const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2) * 4 + cb));
@@ -368,7 +397,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                 const int m = d >> 4, gp = d & 7, dh = (d >> 3) & 1;
                 const uint8_t* T = raw + j * kRawTileBytes;
                 uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-                if (s_valid[b2 * 4 + j]) {
+                if (s_valid[b3 * 4 + j]) {
                     const uint8_t* vb = T + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + dh) * 4;
                     uint32_t wv[4];
 #pragma unroll
@@ -397,7 +426,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&bars->kv_full[b2]);
-                mbar_arrive(&bars->raw_free[b2]);
+                mbar_arrive(&bars->raw_free[b3]);
             }
         }
     } else {
