@@ -73,6 +73,9 @@ extern "C" {
 #define YF_DEV_BAD_POS 4u      /* a KV write position was outside the block table: row skipped */
 #define YF_DEV_BAD_ROWS 8u     /* a query-row count exceeded max_seqlen_q (or its keys): rows clamped */
 #define YF_DEV_TIMEOUT 16u     /* a bounded wait on a page copy gave up: output of that CTA invalid */
+#define YF_DEV_SMEM_ALIGN 32u  /* a kernel found its shared memory misaligned and wrote nothing */
+/* With YF_DEV_TIMEOUT set, bits 16-31 of the status word hold a diagnostic tag of the first
+ * wait that gave up (kernel-specific: role, barrier, awaited completion). */
 
 typedef struct yf_pool yf_pool;
 

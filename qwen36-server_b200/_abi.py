@@ -25,6 +25,7 @@ YF_DEV_LEN_OVERFLOW = 2
 YF_DEV_BAD_POS = 4
 YF_DEV_BAD_ROWS = 8
 YF_DEV_TIMEOUT = 16
+YF_DEV_SMEM_ALIGN = 32
 
 ERROR_NAMES = {
     YF_E_INVALID: "YF_E_INVALID", YF_E_UNSUPPORTED: "YF_E_UNSUPPORTED", YF_E_NOMEM: "YF_E_NOMEM",

@@ -7,9 +7,17 @@
 
 namespace yf {
 
-// Iterations of a bounded mbarrier wait before it gives up (each try_wait
-// itself suspends for a hardware-defined interval), i.e. seconds, not a hang.
+// Bounds of an mbarrier wait: it gives up after kWaitLimitNs of global time or kMaxWaitIters
+// tries, whichever comes first (a try_wait may itself suspend for a hardware-defined interval,
+// so the iteration bound alone could stretch to minutes).
 constexpr uint32_t kMaxWaitIters = 1u << 20;
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,8 +60,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the given phase parity; false if it gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMaxWaitIters; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1; i < kMaxWaitIters; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
     return false;
 }
 

@@ -6,20 +6,25 @@
 // QK_INT8_PREFILL described at docs/research/2026-09-16-head-to-head-llamacpp-and-phase-profile.md:3627-3634):
 // query row i of an entry sees keys 0 .. Tk - Tq + i.
 //
-// One CTA = one entry, one kv head, 128 query rows = 128/G query positions x the G q heads
-// of the kv head (GQA folded into M, so every key tile is dequantized once for all of them).
-// The CTA's nine warps are specialised and hand 64-key tiles to each other through
-// mbarriers, double-buffered so that the stages of consecutive tiles overlap:
-//   * control warp (lane 0): bulk-copies the four 16-token pool tiles of a key tile (K+V int8
-//     + scales, one contiguous block each) into a raw staging buffer two tiles ahead, and
-//     issues the MMAs: S = Q K^T (M=128 rows, N=64 keys, K=128 dims: 8 x tcgen05.mma
-//     kind::f16, f32 in TMEM) and O^T += V^T P^T (M=128 dims, N=128 rows, K=64 keys: 4 MMAs);
-//   * 4 dequant warps: int8 K -> f16 [key][dim], int8 V -> f16 V^T [dim][key], both in the
-//     K-major 128-byte-swizzled layout the MMA descriptors describe;
-//   * 4 softmax warps: thread r owns query row r (TMEM lane r of S): scale, causal mask,
-//     online base-2 softmax with lazy rescale, P (f16) to shared memory; when a row's max
-//     moved they rescale O^T in TMEM (thread d owns lane d) before the next PV.
-// At the end thread d reads lane d of O^T (all 128 rows) and writes out[row][d] / l[row].
+// One CTA = one entry, one kv head and two query tiles of 128 rows (256/G query positions x
+// the G q heads of the kv head: GQA folded into M, so each key tile is dequantized once for
+// 256 rows).  Keys advance in tiles of 128.  Per key tile j and query tile i:
+//   S_i = Q_i K_j^T      tcgen05.mma kind::f16, A = Q_i and B = K_j from shared memory
+//                        (K-major, 128-byte swizzle), M = 128 rows, N = 128 keys, f32 in TMEM;
+//   P_i = softmax part   written back into TMEM as f16 over the upper half of S_i's columns;
+//   O_i += P_i V_j       tcgen05.mma with A = P_i read from TMEM, B = V_j^T from shared
+//                        memory, M = 128 rows, N = 128 dims, f32 accumulator in TMEM.
+// TMEM (512 columns): O_0 [0,128), O_1 [128,256), S_0 [256,384), S_1 [384,512).
+//
+// Warp roles (13 warps), handing buffers to each other through mbarriers:
+//   * warps 0-3 / 4-7, softmax of query tile 0 / 1: thread r owns row r (TMEM lane r):
+//     row max, lazy base-2 rescale of the running max (O_i rescaled in TMEM by the same
+//     thread, only when the max grew by more than 2^8), exponentials, f16 P into TMEM;
+//   * warps 8-11, dequant: int8 pool tiles staged by bulk copies -> f16 K [key][dim] and
+//     V^T [dim][key] in the swizzled layouts the MMA descriptors describe;
+//   * warp 12, control (one lane): the bulk copies of 64-key halves of the pool (K+V int8 and
+//     scales, one 4352-byte block per 16-token tile) and every MMA, polling its barriers.
+// At the end thread r reads row r of O_i and writes out[row] / l[row].
 #include <cstdint>
 #include <cstdlib>
 
@@ -29,27 +34,29 @@
 namespace yf {
 namespace {
 
-constexpr int kPfRows = 128;     // query rows per CTA (M of S, N of O^T)
-constexpr int kPfKeys = 64;      // keys per tile (N of S, K of O^T)
-constexpr int kPfD = 128;        // head dim (K of S, M of O^T)
-constexpr int kPfTmemCols = 256; // S[2]: cols [0,128), O^T: cols [128,256)
+constexpr int kPfRows = 128;      // query rows per query tile (M of both MMAs)
+constexpr int kPfTiles = 2;       // query tiles per CTA
+constexpr int kPfKeys = 128;      // keys per key tile (N of S, K of PV)
+constexpr int kPfD = 128;         // head dim (K of S, N of PV)
+constexpr int kPfTmemCols = 512;
 constexpr float kPfRescale = 8.0f;  // lazy rescale threshold (base 2), as in the decode kernels
 
-// shared-memory map (bytes from a 1024-aligned base); [n] = ring of n buffers
-constexpr int kSmQ = 0;                         // Q   [128 rows][128 d] f16: 2 column blocks x 16 KB
-constexpr int kSmK = kSmQ + 32768;              // K   [2][64 keys][128 d] f16 (2 column blocks x 8 KB)
-constexpr int kSmVt = kSmK + 2 * 16384;         // V^T [3][128 d][64 keys] f16
-constexpr int kSmP = kSmVt + 3 * 16384;         // P   [2][128 rows][64 keys] f16
-constexpr int kSmRaw = kSmP + 2 * 16384;        // raw [3][4 pool tiles x 4352 B]
-constexpr int kRawTileBytes = 4352;             // D=128, group 32
-constexpr int kRawBytes = 4 * kRawTileBytes;    // one 64-key tile
-constexpr int kSmMisc = kSmRaw + 3 * kRawBytes;
-// misc: Bars at +0 (< 256 B), TMEM address at +256, alpha[2][128] at +512, 1/l[128] at +1536,
-// pool-tile flags [3][4] at +2048, abort word at +2064
-constexpr int kSmBytes = kSmMisc + 4096;
-constexpr int kSmAlloc = kSmBytes + 1024;       // + alignment slack
-constexpr int kPfWarps = 9;                     // 4 softmax, 4 dequant, 1 control
+constexpr int kRawTileBytes = 4352;   // one 16-token pool tile, D=128, group 32
+constexpr int kRawPitch = 4368;       // staged tiles 16 B apart modulo 128 B: spreads banks
+constexpr int kRawHalf = 4 * kRawPitch;  // 64 keys
+
+// shared-memory map (bytes from the 1024-aligned dynamic shared memory base)
+constexpr int kSmQ = 0;                         // Q   [2 tiles][2 col blocks of 64 dims][128 rows][128 B] f16
+constexpr int kSmK = kSmQ + kPfTiles * 32768;   // K   [2 stages][2 col blocks of 64 dims][128 keys][128 B]
+constexpr int kSmVt = kSmK + 2 * 32768;         // V^T [2 stages][2 col blocks of 64 keys][128 dims][128 B]
+constexpr int kSmRaw = kSmVt + 2 * 32768;       // raw [2 halves][4 pool tiles, kRawPitch apart]
+constexpr int kSmMisc = kSmRaw + 2 * kRawHalf;
+// misc: Bars at +0, TMEM address at +160, staged-tile flags [2][4] at +168, abort word at +176
+constexpr int kSmAlloc = kSmMisc + 256;
+constexpr int kPfWarps = 13;
 constexpr int kPfBlock = kPfWarps * 32;
+constexpr int kCtlWarp = 12;
+static_assert(kSmAlloc <= 232448, "shared memory");
 
 struct PrefillParams {
     const uint8_t* layer_base;
@@ -88,12 +95,24 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
            | ((uint32_t)(M >> 4) << 24);     // M / 16
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+// D (TMEM) (+)= A (shared memory) * B (shared memory)
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM: lane = row, two f16 of K per 32-bit column) * B (shared memory)
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
         : "memory");
 }
 
@@ -104,35 +123,56 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 32 consecutive TMEM columns of this thread's lane (warp w reads lanes 32w..32w+31).
+// 32 consecutive TMEM columns of this thread's lane (warp w reads lanes 32(w%4) .. +31).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr)
+        : "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+// 64 consecutive TMEM columns of this thread's lane, in one load.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
         "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
-        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
-        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
 
@@ -154,23 +194,89 @@ __device__ __forceinline__ uint32_t dq2(uint32_t biased, int sel, uint32_t scale
     return h2mul(h, scale2);
 }
 
-// True for every thread of the 4 softmax warps when any of them passes true.
-__device__ __forceinline__ bool softmax_any(bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.or.pred po, 1, 128, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v)
-        : "memory");
-    return r != 0;
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
-__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// (a.x*b + c, a.y*b + c) in one packed f32x2 FMA
+__device__ __forceinline__ float2 ffma2(float2 a, float b, float c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%5, %5};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b), "f"(c));
+    return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// Key k (0..127) of the current key tile is visible: causal limit and page validity.
+__device__ __forceinline__ bool key_ok(int k, int lim, uint32_t pm) { return k < lim && ((pm >> (k >> 4)) & 1u); }
+
+// Max of 64 S values (raw dot products); masked keys do not count.
+template <bool kMasked>
+__device__ __forceinline__ float row_max64(const float (&v)[64], int k0, int lim, uint32_t pm) {
+    float a = -INFINITY, b = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 64; c += 4) {
+        float x0 = v[c], x1 = v[c + 1], x2 = v[c + 2], x3 = v[c + 3];
+        if (kMasked) {
+            x0 = key_ok(k0 + c, lim, pm) ? x0 : -INFINITY;
+            x1 = key_ok(k0 + c + 1, lim, pm) ? x1 : -INFINITY;
+            x2 = key_ok(k0 + c + 2, lim, pm) ? x2 : -INFINITY;
+            x3 = key_ok(k0 + c + 3, lim, pm) ? x3 : -INFINITY;
+        }
+        a = max3f(a, x0, x1);
+        b = max3f(b, x2, x3);
+    }
+    return fmaxf(a, b);
+}
+
+// p = 2^(s * scale_log2 - m) for 64 keys, stored as 32 f16x2 TMEM columns; returns sum(p).
+template <bool kMasked>
+__device__ __forceinline__ float exp_store64(const float (&v)[64], int k0, int lim, uint32_t pm, float sl2,
+                                             float nm, uint32_t taddr) {
+    uint32_t pk[32];
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+        float2 x = ffma2(make_float2(v[2 * c], v[2 * c + 1]), sl2, nm);
+        if (kMasked) {
+            x.x = key_ok(k0 + 2 * c, lim, pm) ? x.x : -INFINITY;
+            x.y = key_ok(k0 + 2 * c + 1, lim, pm) ? x.y : -INFINITY;
+        }
+        const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        if (c & 1)
+            acc1 = fadd2(acc1, e);
+        else
+            acc0 = fadd2(acc0, e);
+        pk[c] = pack_h2(e.x, e.y);
+    }
+    tmem_st32(taddr, pk);
+    const float2 s = fadd2(acc0, acc1);
+    return s.x + s.y;
+}
 
 struct Bars {
-    uint64_t raw_full[3], raw_free[3], vt_free[3], kv_full[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+    uint64_t raw_full[2], raw_free[2];  // staged 64-key halves of the pool
+    uint64_t kv_full[2];                // K and V^T stage of a key tile written
+    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its last MMA
+    uint64_t s_full[2], p_full[2];      // per query tile
+    uint64_t o_done[2];                 // per query tile: last PV complete
+    uint64_t drain;
 };
-static_assert(sizeof(Bars) <= 256, "barrier area");
+static_assert(sizeof(Bars) <= 160, "barrier area");
 
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, int use) {  // non-blocking: use-th completion done?
     uint32_t ok;
@@ -183,33 +289,53 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, int use) {  // non-bloc
     return ok != 0;
 }
 
-// Bounded wait for the use-th completion (0-based) of `bar`.  A wait that gives up raises the
-// CTA's abort flag, after which every role skips its remaining waits and drains quickly.
-__device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int* abort) {
-    if (*abort) return false;
-    for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
-        if (mbar_try_wait(bar, (uint32_t)use & 1u)) return true;
-        if ((i & 255u) == 255u && *abort) return false;
-    }
+// Diagnostic tag of a wait that gave up: role (1 control, 2 dequant, 3 softmax) in bits 14-15,
+// barrier in bits 10-13, the awaited completion (low 10 bits) in bits 0-9.
+enum : uint32_t { kBarRawFull, kBarRawFree, kBarKvFull, kBarKFree, kBarVFree, kBarSFull, kBarPFull, kBarODone,
+                  kBarDrain, kBarIdle };
+__host__ __device__ constexpr uint32_t wait_tag(uint32_t role, uint32_t bar, int use) {
+    return (role << 14) | (bar << 10) | ((uint32_t)use & 1023u);
+}
+
+// Raises the CTA's abort flag and, for the first wait of the launch that gives up, records
+// its tag in bits 16-31 of the status word next to YF_DEV_TIMEOUT.
+__device__ __forceinline__ void give_up(volatile int* abort, uint32_t* status, uint32_t tag) {
     *abort = 1;
+    const uint32_t old = atomicOr(status, YF_DEV_TIMEOUT);
+    if (!(old & YF_DEV_TIMEOUT)) atomicOr(status, tag << 16);
+}
+
+// Bounded wait for the use-th completion (0-based) of `bar` (kWaitLimitNs of global time).
+// A wait that gives up raises the CTA's abort flag, after which every role skips its
+// remaining waits and drains quickly.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int* abort, uint32_t* status,
+                                           uint32_t tag) {
+    if (*abort) return false;
+    if (mbar_try_wait(bar, (uint32_t)use & 1u)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, (uint32_t)use & 1u)) return true;
+        if ((i & 7u) == 0) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+    }
+    give_up(abort, status, tag);
     return false;
 }
 
 __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t sraw = smem_u32(smem_raw);
-    const uint32_t sbase = (sraw + 1023u) & ~1023u;
-    uint8_t* base = smem_raw + (sbase - sraw);
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = smem_raw;
+    const uint32_t sbase = smem_u32(smem_raw);
     Bars* bars = reinterpret_cast<Bars*>(base + kSmMisc);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kSmMisc + 256);
-    float* s_alpha = reinterpret_cast<float*>(base + kSmMisc + 512);     // [2][128]
-    float* s_linv = s_alpha + 2 * kPfRows;                                  // [128]
-    uint8_t* s_valid = reinterpret_cast<uint8_t*>(s_linv + kPfRows);      // [3][4] pool-tile flags
-    volatile int* s_abort = reinterpret_cast<volatile int*>(s_valid + 16);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kSmMisc + 160);
+    uint8_t* s_valid = base + kSmMisc + 168;  // [2][4] staged pool-tile flags
+    volatile int* s_abort = reinterpret_cast<volatile int*>(base + kSmMisc + 176);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.z, h = blockIdx.y;
-    const int ppb = kPfRows / p.G;  // query positions per CTA
+    const int ppb = kPfTiles * kPfRows / p.G;  // query positions per CTA
 
     // ---- geometry (same clamps as the split-KV kernels)
     const int cap = p.max_blocks * p.tpp * 16;
@@ -221,184 +347,209 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
         if (tk_u > (uint32_t)cap) atomicOr(p.status, YF_DEV_LEN_OVERFLOW);
         if (tq_u > (uint32_t)p.max_seqlen_q || Tq > Tk) atomicOr(p.status, YF_DEV_BAD_ROWS);
     }
+    // the swizzled operand layouts need a 1024-aligned base (the whole map fits no slack)
+    if (sbase & 1023u) {
+        if (tid == 0) atomicOr(p.status, YF_DEV_SMEM_ALIGN);
+        return;
+    }
     const int qrow0 = (int)p.cu_q[b];
     const int pos0 = blockIdx.x * ppb;
     if (pos0 >= Tq) return;
     const int npos = min(ppb, Tq - pos0);
     const int rows = npos * p.G;
-    const int kv0 = Tk - Tq;  // keys before the chunk
+    const bool act1 = rows > kPfRows;  // query tile 1 holds rows
+    const int kv0 = Tk - Tq;           // keys before the chunk
     const int kv_hi = max(0, min(Tk, kv0 + pos0 + npos));
-    const int kv_lo = max(0, min(Tk, kv0 + pos0 + 1));  // every row sees keys [0, kv_lo)
     const int n_kt = (kv_hi + kPfKeys - 1) / kPfKeys;
     const int pt_total = (Tk + 15) / 16;
+    const int pt_need = (kv_hi + 15) / 16;  // pool tiles this CTA reads
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
     const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
     const long long page_stride = p.phb * p.H;
 
     // ---- set-up
     if (tid == 0) {
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_free[i], 4);
-            mbar_init(&bars->vt_free[i], 1);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars->kv_full[i], 4);
+            mbar_init(&bars->kv_full[i], 8);
+            mbar_init(&bars->k_free[i], 1);
+            mbar_init(&bars->v_free[i], 1);
             mbar_init(&bars->s_full[i], 1);
-            mbar_init(&bars->s_free[i], 4);
             mbar_init(&bars->p_full[i], 4);
-            mbar_init(&bars->pv_done[i], 1);
+            mbar_init(&bars->o_done[i], 1);
         }
         mbar_init(&bars->drain, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
-    if (warp == 8) {
+    if (warp == kCtlWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kPfTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (warp < 4) {
-        // Q row `tid` (position pos0 + tid/G, head h*G + tid%G) into the SW128 Q tile
-        const bool live = tid < rows;
+    int bad = 0;
+    if (warp < 8) {
+        // Q row `row` (position pos0 + row/G, head h*G + row%G) into the SW128 Q tile
+        const int qt = tid >> 7, r = tid & 127, row = tid;
+        const bool live = row < rows;
         const uint4 zero = make_uint4(0, 0, 0, 0);
         const uint4* qp = nullptr;
         if (live)
             qp = reinterpret_cast<const uint4*>(
-                p.q + ((size_t)(qrow0 + pos0 + tid / p.G) * p.Hq + (size_t)h * p.G + tid % p.G) * kPfD);
+                p.q + ((size_t)(qrow0 + pos0 + row / p.G) * p.Hq + (size_t)h * p.G + row % p.G) * kPfD);
+        const uint32_t qdst = sbase + kSmQ + qt * 32768;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) sts128(sbase + kSmQ + sw128_off(tid, c, kPfRows), live ? __ldg(qp + c) : zero);
+        for (int c = 0; c < 16; ++c) sts128(qdst + sw128_off(r, c, kPfRows), live ? __ldg(qp + c) : zero);
         fence_proxy_async_smem();
+        // every page this CTA reads exists (the common case skips per-tile page checks)
+        for (int pt = tid; pt < pt_need; pt += 256)
+            if (__ldg(btrow + pt / p.tpp) >= (uint32_t)p.n_pages) bad = 1;
     }
     tc_fence_before();
-    __syncthreads();
+    const bool pages_ok = __syncthreads_or(bad) == 0;
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    bool timed_out = false;
 
-    if (warp == 8) {
+    if (warp == kCtlWarp) {
         // ================= control: bulk copies and MMAs =================
         if (lane == 0) {
-            auto issue_raw = [&](int kt, int buf) {
-                uint8_t* dst = base + kSmRaw + buf * kRawBytes;
+            auto issue_raw = [&](int hf) {  // pool tiles 4hf .. 4hf+3 into raw slot hf & 1
+                const int slot = hf & 1;
+                uint8_t* dst = base + kSmRaw + slot * kRawHalf;
                 uint32_t bytes = 0;
                 const uint8_t* src[4];
                 for (int j = 0; j < 4; ++j) {
-                    const int pt = kt * 4 + j;
+                    const int pt = hf * 4 + j;
                     src[j] = nullptr;
-                    if (pt < pt_total) {
+                    if (pt < pt_need) {
                         const uint32_t page = __ldg(btrow + pt / p.tpp);
                         if (page < (uint32_t)p.n_pages)
                             src[j] = head_base + (size_t)page * page_stride + (pt % p.tpp) * kRawTileBytes;
                         else
                             atomicOr(p.status, YF_DEV_BAD_PAGE);
                     }
-                    s_valid[buf * 4 + j] = src[j] != nullptr;
+                    s_valid[slot * 4 + j] = src[j] != nullptr;
                     bytes += src[j] ? kRawTileBytes : 0;
                 }
-                mbar_arrive_expect_tx(&bars->raw_full[buf], bytes);
+                mbar_arrive_expect_tx(&bars->raw_full[slot], bytes);
                 for (int j = 0; j < 4; ++j)
-                    if (src[j]) bulk_g2s(dst + j * kRawTileBytes, src[j], kRawTileBytes, &bars->raw_full[buf]);
+                    if (src[j]) bulk_g2s(dst + j * kRawPitch, src[j], kRawTileBytes, &bars->raw_full[slot]);
             };
-            constexpr uint32_t IDESC_S = umma_idesc_f16(kPfRows, kPfKeys);
-            constexpr uint32_t IDESC_O = umma_idesc_f16(kPfD, kPfRows);
-            // Polling loop: issue whichever of {next raw copy, next QK, next PV} is ready.
-            // QK runs at most 2 tiles ahead of PV (two S buffers; keeps every parity wait
-            // within one phase of its barrier).
-            int qk = 0, pv = 0, rw = 0;
+            constexpr uint32_t IDESC = umma_idesc_f16(kPfRows, 128);  // S: N = 128 keys; O: N = 128 dims
+            const int n_half = 2 * n_kt;
+            // Polling loop: issue whichever of {next raw copy, PV_i, QK_i} is ready.  S_i is
+            // single-buffered: QK_i(j) follows PV_i(j-1), which read P_i from the same columns
+            // (tcgen05.mma operations of one thread execute in issue order).
+            int rw = 0, qk[2] = {0, 0}, pv[2] = {0, 0};
             uint32_t idle = 0;
-            while (pv < n_kt && !*s_abort) {
+            uint64_t idle_t0 = 0;
+            while ((pv[0] < n_kt || (act1 && pv[1] < n_kt)) && !*s_abort) {
                 bool prog = false;
-                if (rw < n_kt && (rw < 3 || mbar_test(&bars->raw_free[rw % 3], rw / 3 - 1))) {
-                    issue_raw(rw, rw % 3);
+                if (rw < n_half && (rw < 2 || mbar_test(&bars->raw_free[rw & 1], (rw >> 1) - 1))) {
+                    issue_raw(rw);
                     ++rw;
                     prog = true;
                 }
-                if (qk < n_kt && qk < pv + 2 && mbar_test(&bars->kv_full[qk & 1], qk >> 1) &&
-                    (qk < 2 || mbar_test(&bars->s_free[qk & 1], (qk - 2) >> 1))) {
-                    const int b2 = qk & 1;
-                    tc_fence_after();
 #pragma unroll
-                    for (int ks = 0; ks < kPfD / 16; ++ks) {
-                        const uint64_t a = umma_desc_sw128(sbase + kSmQ + (ks >> 2) * (kPfRows * 128) + (ks & 3) * 32);
-                        const uint64_t bd =
-                            umma_desc_sw128(sbase + kSmK + b2 * 16384 + (ks >> 2) * (kPfKeys * 128) + (ks & 3) * 32);
-                        umma_f16(tmem + b2 * 64, a, bd, IDESC_S, ks > 0);
-                    }
-                    umma_commit(&bars->s_full[b2]);
-                    ++qk;
-                    prog = true;
-                }
-                if (pv < qk && mbar_test(&bars->p_full[pv & 1], pv >> 1)) {
-                    const int bp = pv & 1, bv = pv % 3;
-                    tc_fence_after();
+                for (int i = 0; i < kPfTiles; ++i) {
+                    if (i == 1 && !act1) break;
+                    const uint32_t tS = tmem + 256 + i * 128;
+                    if (pv[i] < qk[i] && mbar_test(&bars->p_full[i], pv[i])) {
+                        const int j = pv[i];
+                        tc_fence_after();
 #pragma unroll
-                    for (int ks = 0; ks < kPfKeys / 16; ++ks) {
-                        const uint64_t a = umma_desc_sw128(sbase + kSmVt + bv * 16384 + ks * 32);
-                        const uint64_t bd = umma_desc_sw128(sbase + kSmP + bp * 16384 + ks * 32);
-                        umma_f16(tmem + 128, a, bd, IDESC_O, (pv > 0 || ks > 0) ? 1u : 0u);
+                        for (int ks = 0; ks < kPfKeys / 16; ++ks) {
+                            const uint64_t bd =
+                                umma_desc_sw128(sbase + kSmVt + (j & 1) * 32768 + (ks >> 2) * 16384 + (ks & 3) * 32);
+                            umma_ts(tmem + i * 128, tS + 64 + ks * 8, bd, IDESC, (j > 0 || ks > 0) ? 1u : 0u);
+                        }
+                        pv[i] = j + 1;
+                        if (!act1 || pv[1 - i] > j) umma_commit(&bars->v_free[j & 1]);  // last reader of V_j
+                        if (j == n_kt - 1) umma_commit(&bars->o_done[i]);
+                        prog = true;
                     }
-                    umma_commit(&bars->pv_done[bp]);
-                    umma_commit(&bars->vt_free[bv]);
-                    ++pv;
-                    prog = true;
+                    if (qk[i] < n_kt && qk[i] == pv[i] && mbar_test(&bars->kv_full[qk[i] & 1], qk[i] >> 1)) {
+                        const int j = qk[i];
+                        tc_fence_after();
+#pragma unroll
+                        for (int ks = 0; ks < kPfD / 16; ++ks) {
+                            const uint64_t a =
+                                umma_desc_sw128(sbase + kSmQ + i * 32768 + (ks >> 2) * 16384 + (ks & 3) * 32);
+                            const uint64_t bd =
+                                umma_desc_sw128(sbase + kSmK + (j & 1) * 32768 + (ks >> 2) * 16384 + (ks & 3) * 32);
+                            umma_ss(tS, a, bd, IDESC, ks > 0);
+                        }
+                        umma_commit(&bars->s_full[i]);
+                        qk[i] = j + 1;
+                        if (!act1 || qk[1 - i] > j) umma_commit(&bars->k_free[j & 1]);  // last reader of K_j
+                        prog = true;
+                    }
                 }
                 if (prog) {
                     idle = 0;
-                } else if (++idle > 4u * kMaxWaitIters) {
-                    *s_abort = 1;
-                    timed_out = true;
+                } else if (++idle == 1) {
+                    idle_t0 = globaltimer_ns();
+                } else if ((idle & 63u) == 0 && globaltimer_ns() - idle_t0 > kWaitLimitNs) {
+                    give_up(s_abort, p.status, wait_tag(1, kBarIdle, (qk[0] & 31) | ((pv[0] & 31) << 5)));
                 }
             }
             // every MMA of this CTA has completed before TMEM is released
             umma_commit(&bars->drain);
-            (void)mbar_wait(&bars->drain, 0u);
+            if (!mbar_wait(&bars->drain, 0u)) give_up(s_abort, p.status, wait_tag(1, kBarDrain, 0));
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else if (warp >= 8) {
         // ================= dequant: raw pool tiles -> f16 K and V^T =================
-        const int t = tid - 128;
-        for (int it = 0; it < n_kt; ++it) {
-            const int b2 = it & 1, b3 = it % 3;
-            if (!wait_phase(&bars->raw_full[b3], it / 3, s_abort)) timed_out = true;
-            // K[b2] was read by QK(it-2), V^T[b3] by PV(it-3)
-            if (it >= 2 && !wait_phase(&bars->s_full[b2], (it - 2) >> 1, s_abort)) timed_out = true;
-            if (it >= 3 && !wait_phase(&bars->vt_free[b3], it / 3 - 1, s_abort)) timed_out = true;
-            const uint8_t* raw = base + kSmRaw + b3 * kRawBytes;
-            const uint32_t kdst = sbase + kSmK + b2 * 16384, vdst = sbase + kSmVt + b3 * 16384;
+        const int t = tid - 256, dw = t >> 5;
+        // K: lane -> (token g, dim octet tig) of a 512-byte block, paired so that each
+        // quarter-warp's loads and swizzled stores hit eight distinct 16-byte bank groups
+        const int qw = lane >> 3, k8 = lane & 7;
+        const int kg = (k8 < 4) ? qw : (qw ^ 5), ktig = k8 & 3;
+        // V: lane -> (dim bits 4, 3, 0; staged tile); warp and step give dim bits 5-6, 1-2
+        const int vm1 = lane >> 4, vdh = (lane >> 3) & 1, vjt = (lane >> 1) & 3, vg1 = lane & 1;
+        const int n_half = 2 * n_kt;
+        for (int hf = 0; hf < n_half; ++hf) {
+            const int j = hf >> 1, e = hf & 1, slot = hf & 1;
+            (void)wait_phase(&bars->raw_full[slot], hf >> 1, s_abort, p.status, wait_tag(2, kBarRawFull, hf >> 1));
+            // stage j&1 was last read by QK(j-2) (K) and PV(j-2) (V^T)
+            if (e == 0 && j >= 2) {
+                (void)wait_phase(&bars->k_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarKFree, j));
+                (void)wait_phase(&bars->v_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarVFree, j));
+            }
+            const uint8_t* raw = base + kSmRaw + slot * kRawHalf;
+            const uint32_t kdst = sbase + kSmK + (j & 1) * 32768, vdst = sbase + kSmVt + (j & 1) * 32768 + e * 16384;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                // K: 16-byte word w of pool tile j = tokens g, g+8 x dims 32cb+8tig .. +7
-                const int w = t + i * 128;
-                const int j = w >> 7, cb = (w & 127) >> 5, ln = w & 31, g = ln >> 2, tig = ln & 3;
-                const uint8_t* T = raw + j * kRawTileBytes;
+            for (int jt = 0; jt < 4; ++jt) {
+                // K: tokens kg, kg+8 x dims 32dw + 8ktig .. +7 of pool tile jt
+                const uint8_t* T = raw + jt * kRawPitch;
                 uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
-                if (s_valid[b3 * 4 + j]) {
-                    const uint4 kw = lds128(T + cb * 512 + ln * 16);
-                    // K scales [g][half][group]: token g is half 0, token g+8 half 1
-                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2) * 4 + cb));
-                    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((g * 2 + 1) * 4 + cb));
+                if (s_valid[slot * 4 + jt]) {
+                    const uint4 kw = lds128(T + dw * 512 + (kg * 4 + ktig) * 16);
+                    // K scales [token%8][token/8][group]
+                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2) * 4 + dw));
+                    const uint16_t s1 =
+                        *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2 + 1) * 4 + dw));
                     const uint32_t d0 = (uint32_t)s0 | ((uint32_t)s0 << 16), d1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
                     const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
                     o0 = make_uint4(dq2(x0, 0, d0), dq2(x0, 1, d0), dq2(x1, 0, d0), dq2(x1, 1, d0));
                     o1 = make_uint4(dq2(z0, 0, d1), dq2(z0, 1, d1), dq2(z1, 0, d1), dq2(z1, 1, d1));
                 }
-                const int t0 = j * 16 + g, c = cb * 4 + tig;  // 16-byte chunk = dims 8c .. 8c+7
-                sts128(kdst + sw128_off(t0, c, kPfKeys), o0);
-                sts128(kdst + sw128_off(t0 + 8, c, kPfKeys), o1);
+                const int key = e * 64 + jt * 16 + kg, c = dw * 4 + ktig;  // chunk c = dims 8c .. 8c+7
+                sts128(kdst + sw128_off(key, c, kPfKeys), o0);
+                sts128(kdst + sw128_off(key + 8, c, kPfKeys), o1);
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                // V^T row d, keys 16j .. 16j+15: the four lanes (g', tig=0..3) of dim d hold
-                // tokens {2tig, 2tig+8, 2tig+1, 2tig+9} in one 32-bit word each
-                const int item = t + i * 128;
-                const int j = item >> 7, d = item & 127;
-                const int m = d >> 4, gp = d & 7, dh = (d >> 3) & 1;
-                const uint8_t* T = raw + j * kRawTileBytes;
+            for (int st = 0; st < 4; ++st) {
+                // V^T row d, keys 16vjt .. +15 of this half: the four (token-pair) words of dim d
+                // hold tokens {2tig, 2tig+8, 2tig+1, 2tig+9} for tig = 0..3
+                const int d = 32 * dw + 16 * vm1 + 8 * vdh + 2 * st + vg1;
+                const int m = d >> 4, gp = d & 7;
+                const uint8_t* T = raw + vjt * kRawPitch;
                 uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-                if (s_valid[b3 * 4 + j]) {
-                    const uint8_t* vb = T + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + dh) * 4;
+                if (s_valid[slot * 4 + vjt]) {
+                    const uint8_t* vb = T + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + vdh) * 4;
                     uint32_t wv[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) wv[q] = lds32(vb + (gp * 4 + q) * 16);
@@ -406,12 +557,11 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                     const uint32_t k03 = __byte_perm(wv[0], wv[1], 0x6420), k47 = __byte_perm(wv[2], wv[3], 0x6420);
                     const uint32_t k8b = __byte_perm(wv[0], wv[1], 0x7531), kcf = __byte_perm(wv[2], wv[3], 0x7531);
                     // V scales [tig][group][j]: pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
-                    const int sg = d >> 5;
                     uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
-                    const uint8_t* vs = T + 32 * kPfD + 128 + sg * 8;
+                    const uint8_t* vsc = T + 32 * kPfD + 128 + (d >> 5) * 8;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const uint2 pr = lds64(vs + q * 32);
+                        const uint2 pr = lds64(vsc + q * 32);
                         sp[q] = __byte_perm(pr.x, pr.y, 0x5410);
                         sp[4 + q] = __byte_perm(pr.x, pr.y, 0x7632);
                     }
@@ -419,131 +569,116 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                     lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
                     hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
                 }
-                sts128(vdst + sw128_off(d, 2 * j, kPfD), lo);
-                sts128(vdst + sw128_off(d, 2 * j + 1, kPfD), hi);
+                sts128(vdst + sw128_off(d, 2 * vjt, kPfD), lo);
+                sts128(vdst + sw128_off(d, 2 * vjt + 1, kPfD), hi);
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&bars->kv_full[b2]);
-                mbar_arrive(&bars->raw_free[b3]);
+                mbar_arrive(&bars->kv_full[j & 1]);
+                mbar_arrive(&bars->raw_free[slot]);
             }
         }
     } else {
-        // ================= softmax: thread = query row =================
-        const int row = tid;
-        const int kvlen = row < rows ? max(0, min(Tk, kv0 + pos0 + row / p.G + 1)) : 0;
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        float m_run = -INFINITY, l_run = 0.f;
-        for (int it = 0; it < n_kt; ++it) {
-            const int b2 = it & 1;
-            if (!wait_phase(&bars->s_full[b2], it >> 1, s_abort)) timed_out = true;
-            tc_fence_after();
-            float s[64];
-            tmem_ld32(tmem + b2 * 64 + lane_off, *reinterpret_cast<float(*)[32]>(s));
-            tmem_ld32(tmem + b2 * 64 + 32 + lane_off, *reinterpret_cast<float(*)[32]>(s + 32));
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->s_free[b2]);
-
-            const int key0 = it * kPfKeys;
-            // pool tiles of this key tile that hold keys (read from the block table: the control
-            // warp already reuses its flags for the tile two ahead)
-            bool pv[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int pt = it * 4 + j;
-                pv[j] = pt < pt_total && __ldg(btrow + pt / p.tpp) < (uint32_t)p.n_pages;
-            }
-            const bool full = key0 + kPfKeys <= kv_lo && pv[0] && pv[1] && pv[2] && pv[3];
-            float mx = -INFINITY;
-            if (full) {
-#pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    s[c] *= p.scale_log2;
-                    mx = fmaxf(mx, s[c]);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const bool ok = key0 + c < kvlen && pv[c >> 4];
-                    s[c] = ok ? s[c] * p.scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, s[c]);
-                }
-            }
-            float alpha = 1.f;
-            bool need = false;
-            if (mx > m_run + kPfRescale) {
-                alpha = fast_exp2(m_run - mx);
-                m_run = mx;
-                l_run *= alpha;
-                need = it > 0;
-            }
-            const float muse = m_run == -INFINITY ? 0.f : m_run;
-            if (it >= 2 && !wait_phase(&bars->pv_done[b2], (it - 2) >> 1, s_abort)) timed_out = true;  // P[b2] free
-            const uint32_t pdst = sbase + kSmP + b2 * 16384;
-            float sum = 0.f;
-#pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {
-                uint32_t pk[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = fast_exp2(s[c8 * 8 + 2 * e] - muse), p1 = fast_exp2(s[c8 * 8 + 2 * e + 1] - muse);
-                    sum += p0 + p1;
-                    pk[e] = pack_h2(p0, p1);
-                }
-                sts128(pdst + sw128_off(row, c8, kPfRows), make_uint4(pk[0], pk[1], pk[2], pk[3]));
-            }
-            l_run += sum;
-            s_alpha[b2 * kPfRows + row] = alpha;
-            if (softmax_any(need)) {
-                // PV(it-1) must have landed before O^T is rescaled; thread d owns lane d
-                if (!wait_phase(&bars->pv_done[(it - 1) & 1], (it - 1) >> 1, s_abort)) timed_out = true;
+        // ================= softmax: thread = query row of tile qt =================
+        const int qt = tid >> 7, row = tid;
+        if (qt == 0 || act1) {
+            const bool live = row < rows;
+            const int kvlen = live ? max(0, min(Tk, kv0 + pos0 + row / p.G + 1)) : 0;
+            const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+            const uint32_t tS = tmem + 256 + qt * 128 + lane_off, tP = tS + 64, tO = tmem + qt * 128 + lane_off;
+            const float sl2 = p.scale_log2;
+            float m_run = -INFINITY, l_run = 0.f;  // running max (scaled, base 2) and sum
+            for (int it = 0; it < n_kt; ++it) {
+                (void)wait_phase(&bars->s_full[qt], it, s_abort, p.status, wait_tag(3, kBarSFull, it));
+                __syncwarp();
                 tc_fence_after();
+                const int key0 = it * kPfKeys, lim = kvlen - key0;
+                uint32_t pm = 0xFFu;
+                if (!pages_ok) {
 #pragma unroll
-                for (int c0 = 0; c0 < kPfRows; c0 += 32) {
-                    float o[32];
-                    tmem_ld32(tmem + 128 + c0 + lane_off, o);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] *= s_alpha[b2 * kPfRows + c0 + e];
-                    tmem_st32(tmem + 128 + c0 + lane_off, o);
+                    for (int jt = 0; jt < 8; ++jt) {
+                        const int pt = key0 / 16 + jt;
+                        if (pt >= pt_total || __ldg(btrow + pt / p.tpp) >= (uint32_t)p.n_pages) pm &= ~(1u << jt);
+                    }
                 }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_full[b2]);
-        }
-        // ---- epilogue: thread d writes dim d of every row
-        s_linv[row] = l_run > 0.f ? 1.f / l_run : 0.f;
-        if (n_kt > 0 && !wait_phase(&bars->pv_done[(n_kt - 1) & 1], (n_kt - 1) >> 1, s_abort)) timed_out = true;
-        tc_fence_after();
-        softmax_sync();
-        const int d = tid;
-        if (n_kt > 0) {
+                // warp-uniform: both paths end in warp-collective TMEM accesses
+                const bool full = __all_sync(0xffffffffu, pm == 0xFFu && lim >= kPfKeys);
+                float v[64];
+                tmem_ld64(tS, v);
+                float mx = full ? row_max64<false>(v, 0, lim, pm) : row_max64<true>(v, 0, lim, pm);
+                tmem_ld64(tS + 64, v);
+                mx = fmaxf(mx, full ? row_max64<false>(v, 64, lim, pm) : row_max64<true>(v, 64, lim, pm));
+                mx *= sl2;
+                float alpha = 1.f;
+                bool need = false;
+                if (mx > m_run + kPfRescale) {
+                    alpha = fast_exp2(m_run - mx);
+                    m_run = mx;
+                    l_run *= alpha;
+                    need = it > 0;
+                }
+                if (__any_sync(0xffffffffu, need)) {
+                    // PV(it-1) completed before QK(it) (committed in issue order): O_i is stable.
+                    // Rare: S is reloaded afterwards rather than kept live across it.
+#pragma unroll 1
+                    for (int c0 = 0; c0 < kPfD; c0 += 32) {
+                        float o[32];
+                        uint32_t ob[32];
+                        tmem_ld32(tO + c0, o);
 #pragma unroll
-            for (int c0 = 0; c0 < kPfRows; c0 += 32) {
+                        for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(o[e] * alpha);
+                        tmem_st32(tO + c0, ob);
+                    }
+                    tmem_ld64(tS + 64, v);
+                }
+                const float nm = m_run == -INFINITY ? 0.f : -m_run;
+                // P over S columns 64..127: keys 64..127 first (their S columns are then free),
+                // then keys 0..63
+                float sum = full ? exp_store64<false>(v, 64, lim, pm, sl2, nm, tP + 32)
+                                 : exp_store64<true>(v, 64, lim, pm, sl2, nm, tP + 32);
+                tmem_ld64(tS, v);
+                sum += full ? exp_store64<false>(v, 0, lim, pm, sl2, nm, tP) : exp_store64<true>(v, 0, lim, pm, sl2, nm, tP);
+                l_run += sum;
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->p_full[qt]);
+            }
+            // ---- epilogue: thread r writes row r of O_i / l
+            if (n_kt > 0) {
+                (void)wait_phase(&bars->o_done[qt], 0, s_abort, p.status, wait_tag(3, kBarODone, 0));
+                __syncwarp();
+                tc_fence_after();
+            }
+            const float linv = l_run > 0.f ? 1.f / l_run : 0.f;
+            uint4* orow = live ? reinterpret_cast<uint4*>(p.out + ((size_t)(qrow0 + pos0 + row / p.G) * p.Hq +
+                                                                   (size_t)h * p.G + row % p.G) *
+                                                                      kPfD)
+                               : nullptr;
+#pragma unroll
+            for (int c0 = 0; c0 < kPfD; c0 += 32) {
                 float o[32];
-                tmem_ld32(tmem + 128 + c0 + lane_off, o);
+                if (n_kt > 0) {
+                    tmem_ld32(tO + c0, o);
+                } else {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int r = c0 + e;
-                    if (r < rows)
-                        p.out[((size_t)(qrow0 + pos0 + r / p.G) * p.Hq + (size_t)h * p.G + r % p.G) * kPfD + d] =
-                            __float2half_rn(o[e] * s_linv[r]);
+                    for (int e = 0; e < 32; ++e) o[e] = 0.f;
+                }
+                if (live) {
+#pragma unroll
+                    for (int v = 0; v < 4; ++v)
+                        orow[c0 / 8 + v] = make_uint4(pack_h2(o[8 * v] * linv, o[8 * v + 1] * linv),
+                                                      pack_h2(o[8 * v + 2] * linv, o[8 * v + 3] * linv),
+                                                      pack_h2(o[8 * v + 4] * linv, o[8 * v + 5] * linv),
+                                                      pack_h2(o[8 * v + 6] * linv, o[8 * v + 7] * linv));
                 }
             }
-        } else {
-            for (int r = 0; r < rows; ++r)
-                p.out[((size_t)(qrow0 + pos0 + r / p.G) * p.Hq + (size_t)h * p.G + r % p.G) * kPfD + d] =
-                    __float2half_rn(0.f);
         }
     }
-    if (timed_out) atomicOr(p.status, YF_DEV_TIMEOUT);
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == kCtlWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols) : "memory");
     }
@@ -587,7 +722,7 @@ int launch_prefill_tc(const AttnArgs& a) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
         if (dev >= 0 && dev < 64) attr_dev[dev] = 1;
     }
-    const int ppb = kPfRows / p.G;
+    const int ppb = kPfTiles * kPfRows / p.G;
     const dim3 grid((a.max_seqlen_q + ppb - 1) / ppb, d.n_kv_heads, a.batch);
     if (grid.x > 0x7fffffffu) return fail(YF_E_UNSUPPORTED, "too many query rows");
     prefill_tc_kernel<<<grid, kPfBlock, kSmAlloc, a.stream>>>(p);
