@@ -44,9 +44,14 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def dominant_kernel(config: str) -> str:
+    """The kernel that dominates one attention call of the workload."""
+    return "prefill_tc_kernel" if config == "prefill_chunk" else "decode_persistent_kernel"
+
+
 def profile_traffic(config: str):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
-    path = os.path.join(REPO, "profiles", f"splitkv_{config}.md")
+    path = os.path.join(REPO, "profiles", f"{dominant_kernel(config).replace('_kernel', '')}_{config}.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -343,7 +348,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = profile_traffic(args.config)
-    roof["kernel"] = "splitkv_kernel + splitkv_combine (one attention call)"
+    roof["kernel"] = dominant_kernel(args.config) + " (one attention call)"
     roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback"
     roof["algorithmic_bytes_per_launch"] = alg_bytes_attn
     roof["launch_ms"] = attn_ms

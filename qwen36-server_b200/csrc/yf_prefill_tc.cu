@@ -16,14 +16,15 @@
 //                        memory, M = 128 rows, N = 128 dims, f32 accumulator in TMEM.
 // TMEM (512 columns): O_0 [0,128), O_1 [128,256), S_0 [256,384), S_1 [384,512).
 //
-// Warp roles (13 warps), handing buffers to each other through mbarriers:
+// Warp roles (14 warps), handing buffers to each other through mbarriers:
 //   * warps 0-3 / 4-7, softmax of query tile 0 / 1: thread r owns row r (TMEM lane r):
 //     row max, lazy base-2 rescale of the running max (O_i rescaled in TMEM by the same
 //     thread, only when the max grew by more than 2^8), exponentials, f16 P into TMEM;
 //   * warps 8-11, dequant: int8 pool tiles staged by bulk copies -> f16 K [key][dim] and
 //     V^T [dim][key] in the swizzled layouts the MMA descriptors describe;
-//   * warp 12, control (one lane): the bulk copies of 64-key halves of the pool (K+V int8 and
-//     scales, one 4352-byte block per 16-token tile) and every MMA, polling its barriers.
+//   * warp 12, control (one lane): every MMA and commit, polling its barriers;
+//   * warp 13, copies (one lane): bulk copies of 64-key halves of the pool (K+V int8 and
+//     scales, one 4352-byte block per 16-token tile), page ids read one half ahead.
 // At the end thread r reads row r of O_i and writes out[row] / l[row].
 #include <cstdint>
 #include <cstdlib>
@@ -53,9 +54,10 @@ constexpr int kSmRaw = kSmVt + 2 * 32768;       // raw [2 halves][4 pool tiles, 
 constexpr int kSmMisc = kSmRaw + 2 * kRawHalf;
 // misc: Bars at +0, TMEM address at +160, staged-tile flags [2][4] at +168, abort word at +176
 constexpr int kSmAlloc = kSmMisc + 256;
-constexpr int kPfWarps = 13;
+constexpr int kPfWarps = 14;
 constexpr int kPfBlock = kPfWarps * 32;
 constexpr int kCtlWarp = 12;
+constexpr int kCopyWarp = 13;
 static_assert(kSmAlloc <= 232448, "shared memory");
 
 struct PrefillParams {
@@ -415,43 +417,15 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
     if (warp == kCtlWarp) {
         // ================= control: bulk copies and MMAs =================
         if (lane == 0) {
-            auto issue_raw = [&](int hf) {  // pool tiles 4hf .. 4hf+3 into raw slot hf & 1
-                const int slot = hf & 1;
-                uint8_t* dst = base + kSmRaw + slot * kRawHalf;
-                uint32_t bytes = 0;
-                const uint8_t* src[4];
-                for (int j = 0; j < 4; ++j) {
-                    const int pt = hf * 4 + j;
-                    src[j] = nullptr;
-                    if (pt < pt_need) {
-                        const uint32_t page = __ldg(btrow + pt / p.tpp);
-                        if (page < (uint32_t)p.n_pages)
-                            src[j] = head_base + (size_t)page * page_stride + (pt % p.tpp) * kRawTileBytes;
-                        else
-                            atomicOr(p.status, YF_DEV_BAD_PAGE);
-                    }
-                    s_valid[slot * 4 + j] = src[j] != nullptr;
-                    bytes += src[j] ? kRawTileBytes : 0;
-                }
-                mbar_arrive_expect_tx(&bars->raw_full[slot], bytes);
-                for (int j = 0; j < 4; ++j)
-                    if (src[j]) bulk_g2s(dst + j * kRawPitch, src[j], kRawTileBytes, &bars->raw_full[slot]);
-            };
             constexpr uint32_t IDESC = umma_idesc_f16(kPfRows, 128);  // S: N = 128 keys; O: N = 128 dims
-            const int n_half = 2 * n_kt;
-            // Polling loop: issue whichever of {next raw copy, PV_i, QK_i} is ready.  S_i is
+            // Polling loop: issue whichever of {PV_i, QK_i} is ready.  S_i is
             // single-buffered: QK_i(j) follows PV_i(j-1), which read P_i from the same columns
             // (tcgen05.mma operations of one thread execute in issue order).
-            int rw = 0, qk[2] = {0, 0}, pv[2] = {0, 0};
+            int qk[2] = {0, 0}, pv[2] = {0, 0};
             uint32_t idle = 0;
             uint64_t idle_t0 = 0;
             while ((pv[0] < n_kt || (act1 && pv[1] < n_kt)) && !*s_abort) {
                 bool prog = false;
-                if (rw < n_half && (rw < 2 || mbar_test(&bars->raw_free[rw & 1], (rw >> 1) - 1))) {
-                    issue_raw(rw);
-                    ++rw;
-                    prog = true;
-                }
 #pragma unroll
                 for (int i = 0; i < kPfTiles; ++i) {
                     if (i == 1 && !act1) break;
@@ -500,6 +474,49 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
             if (!mbar_wait(&bars->drain, 0u)) give_up(s_abort, p.status, wait_tag(1, kBarDrain, 0));
         }
         __syncwarp();
+    } else if (warp == kCopyWarp) {
+        // ================= copies: pool tiles of 64-key halves into the raw ring =================
+        if (lane == 0) {
+            const int n_half = 2 * n_kt;
+            uint32_t page[4];
+            auto fetch_pages = [&](int hf) {  // page ids of pool tiles 4hf .. 4hf+3 (n_pages: skip)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int pt = hf * 4 + j;
+                    page[j] = pt < pt_need ? __ldg(btrow + pt / p.tpp) : (uint32_t)p.n_pages;
+                }
+            };
+            if (n_half > 0) fetch_pages(0);
+            for (int hf = 0; hf < n_half; ++hf) {
+                const int slot = hf & 1;
+                uint32_t cur[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) cur[j] = page[j];
+                if (hf + 1 < n_half) fetch_pages(hf + 1);  // in flight while this half waits
+                if (hf >= 2 &&
+                    !wait_phase(&bars->raw_free[slot], (hf >> 1) - 1, s_abort, p.status, wait_tag(1, kBarRawFree, hf)))
+                    break;
+                uint8_t* dst = base + kSmRaw + slot * kRawHalf;
+                uint32_t bytes = 0;
+                const uint8_t* src[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int pt = hf * 4 + j;
+                    src[j] = nullptr;
+                    if (cur[j] < (uint32_t)p.n_pages)
+                        src[j] = head_base + (size_t)cur[j] * page_stride + (pt % p.tpp) * kRawTileBytes;
+                    else if (pt < pt_need)
+                        atomicOr(p.status, YF_DEV_BAD_PAGE);
+                    s_valid[slot * 4 + j] = src[j] != nullptr;
+                    bytes += src[j] ? kRawTileBytes : 0;
+                }
+                mbar_arrive_expect_tx(&bars->raw_full[slot], bytes);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (src[j]) bulk_g2s(dst + j * kRawPitch, src[j], kRawTileBytes, &bars->raw_full[slot]);
+            }
+        }
+        __syncwarp();
     } else if (warp >= 8) {
         // ================= dequant: raw pool tiles -> f16 K and V^T =================
         const int t = tid - 256, dw = t >> 5;
@@ -540,31 +557,35 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                 sts128(kdst + sw128_off(key, c, kPfKeys), o0);
                 sts128(kdst + sw128_off(key + 8, c, kPfKeys), o1);
             }
+            // V: the thread's four dims share one scale group (dims 32dw .. 32dw+31) of tile vjt
+            const uint8_t* TV = raw + vjt * kRawPitch;
+            const bool vvalid = s_valid[slot * 4 + vjt] != 0;
+            uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
+            if (vvalid) {
+                // V scales [tig][group][j]: pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
+                const uint8_t* vsc = TV + 32 * kPfD + 128 + dw * 8;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint2 pr = lds64(vsc + q * 32);
+                    sp[q] = __byte_perm(pr.x, pr.y, 0x5410);
+                    sp[4 + q] = __byte_perm(pr.x, pr.y, 0x7632);
+                }
+            }
 #pragma unroll
             for (int st = 0; st < 4; ++st) {
                 // V^T row d, keys 16vjt .. +15 of this half: the four (token-pair) words of dim d
                 // hold tokens {2tig, 2tig+8, 2tig+1, 2tig+9} for tig = 0..3
                 const int d = 32 * dw + 16 * vm1 + 8 * vdh + 2 * st + vg1;
                 const int m = d >> 4, gp = d & 7;
-                const uint8_t* T = raw + vjt * kRawPitch;
                 uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-                if (s_valid[slot * 4 + vjt]) {
-                    const uint8_t* vb = T + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + vdh) * 4;
+                if (vvalid) {
+                    const uint8_t* vb = TV + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + vdh) * 4;
                     uint32_t wv[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) wv[q] = lds32(vb + (gp * 4 + q) * 16);
                     // keys 0..7 = bytes 0,2 of wv[0..3]; keys 8..15 = bytes 1,3
                     const uint32_t k03 = __byte_perm(wv[0], wv[1], 0x6420), k47 = __byte_perm(wv[2], wv[3], 0x6420);
                     const uint32_t k8b = __byte_perm(wv[0], wv[1], 0x7531), kcf = __byte_perm(wv[2], wv[3], 0x7531);
-                    // V scales [tig][group][j]: pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
-                    uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
-                    const uint8_t* vsc = T + 32 * kPfD + 128 + (d >> 5) * 8;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint2 pr = lds64(vsc + q * 32);
-                        sp[q] = __byte_perm(pr.x, pr.y, 0x5410);
-                        sp[4 + q] = __byte_perm(pr.x, pr.y, 0x7632);
-                    }
                     const uint32_t a = bias8(k03), bq = bias8(k47), c8 = bias8(k8b), cf = bias8(kcf);
                     lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
                     hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
