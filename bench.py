@@ -248,6 +248,72 @@ class Step:
         return wl.n_layers * (2 + (1 if separate else 0))
 
 
+class ShardedStep:
+    """decode_long on `world` GPUs: this rank's kv head and key range of the one sequence
+    (qwen36_server_b200.sharding), partial decode -> NCCL all-gather -> LSE combine per step.
+    Strong scaling: every rank works on the same token."""
+
+    def __init__(self, wl, device: int, rank: int, world: int):
+        import torch
+
+        yf = graft.load_package()
+        from qwen36_server_b200 import sharding as S
+        from qwen36_server_b200 import workloads as W
+
+        self.torch, self.yf, self.wl = torch, yf, wl
+        self.dev = torch.device("cuda", device)
+        torch.cuda.set_device(self.dev)
+        self.stream = torch.cuda.Stream(self.dev)
+        self.L = yf.lib()
+        self.layers = 1
+        ctx = int(wl.ctx[0])
+        self.shard = sh = S.long_context_plan(world, wl.n_kv_heads, ctx, wl.page_size)[rank]
+        n = sh.k1 - sh.k0
+        pages = max(1, -(-n // wl.page_size))
+        self.sd = S.ShardedLongDecode(sh, wl.n_q_heads, wl.n_kv_heads, wl.head_dim, pages, wl.page_size,
+                                      wl.group_size, batch=1, device=device)
+        self.pool = self.sd.pool
+        gen = torch.Generator(device=self.dev)
+        gen.manual_seed(wl.seed + 7919 * rank)
+        self.bt = torch.arange(pages, dtype=torch.int32, device=self.dev).view(1, pages)
+        self.owner = sh.k0 < ctx <= sh.k1  # holds the newest key: appends it every step
+        hist = n - 1 if self.owner else n
+        for s0 in range(0, hist, 1 << 18):
+            m = min(1 << 18, hist - s0)
+            k = W.kv_rows_torch(gen, m, sh.kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+            v = W.kv_rows_torch(gen, m, sh.kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+            yf.launch_append_multi(self.pool, 0, k, v, [0, m], [s0], self.bt, max_rows=m)
+        self.T = 1
+        self.k_new = W.kv_rows_torch(gen, 1, sh.kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+        self.v_new = W.kv_rows_torch(gen, 1, sh.kv_heads, wl.head_dim, wl.outlier_frac, self.dev)
+        self.q = torch.randn((1, wl.n_q_heads, wl.head_dim), generator=gen, device=self.dev).half()
+        self.q_local = self.sd.q_slice(self.q)
+        self.out = self.sd.out
+        self.start = torch.tensor([n - 1], dtype=torch.int32, device=self.dev)
+        self.cu_k = torch.tensor([0, n], dtype=torch.int32, device=self.dev)
+        self.n = n
+        self.scale = yf.default_scale(wl.head_dim)
+        self.ws_bytes = self.pool.workspace_size(self.sd.hq, 1, 1, max(n, 1))
+        torch.cuda.synchronize()
+        if self.pool.status():
+            raise RuntimeError("device status after building the shard")
+
+    def run(self):
+        if self.owner:
+            self.yf.kv_append_paged(self.pool, 0, self.k_new, self.v_new, self.start, self.bt)
+        h0 = self.shard.kv_head0 * self.sd.G
+        self.q_local.copy_(self.q[:, h0:h0 + self.sd.hq])
+        self.sd.step(self.q_local, self.cu_k, self.bt, self.scale, max(self.n, 1))
+
+    def run_attn(self):
+        self.sd.partial(self.q_local, self.cu_k, self.bt, self.scale, max(self.n, 1))
+
+    def launches_per_step(self) -> int:
+        """KV write (owner only) + partial decode + one combine per head group (the all-gather
+        is NCCL's kernel, the q slice a torch copy)."""
+        return (1 if self.owner else 0) + 1 + self.shard.n_head_groups
+
+
 def make_workload(name: str, rank: int):
     from qwen36_server_b200 import workloads as W
 
@@ -260,15 +326,16 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
 
-    wl = make_workload(args.config, rank)
+    sharded = args.config == "decode_long" and world > 1
+    wl = make_workload(args.config, 0 if sharded else rank)
     layers_resident = wl.n_layers
     if args.config == "mtp_verify":
         free = torch.cuda.mem_get_info(local_rank)[0]
         per_layer = wl.kv_bytes(1)
         layers_resident = max(1, min(wl.n_layers, int(0.8 * free // per_layer)))
-    step = Step(wl, local_rank, layers_resident)
+    step = ShardedStep(wl, local_rank, rank, world) if sharded else Step(wl, local_rank, layers_resident)
     stream = step.stream
-    if args.no_graph:
+    if args.no_graph or sharded:  # the sharded step holds an NCCL call: launched directly
         run_step, run_attn = step.run, step.run_attn
     else:
         step.capture()
@@ -336,10 +403,10 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     ms, e2e_ms, attn_ms = t.tolist()
     status = step.pool.status()
 
-    tokens = step.T * world
-    kv_bytes = wl.kv_bytes()
+    tokens = step.T * (1 if sharded else world)
+    kv_bytes = wl.kv_bytes() // (world if sharded else 1)  # per GPU
     hbm, tflops, peak_kind = peaks()
-    alg_bytes_attn = wl.kv_bytes(1)
+    alg_bytes_attn = wl.kv_bytes(1) // (world if sharded else 1)
     achieved_gbs = alg_bytes_attn / (attn_ms * 1e-3) / 1e9
     if wl.name == "prefill_chunk":
         roof = {"bound": "tensor", "achieved": wl.attn_flops() / wl.n_layers / (attn_ms * 1e-3) / 1e12,
@@ -348,7 +415,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = profile_traffic(args.config)
-    roof["kernel"] = dominant_kernel(args.config) + " (one attention call)"
+    roof["kernel"] = dominant_kernel(args.config) + (" (this rank's partial over its shard)" if sharded
+                                                      else " (one attention call)")
     roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback"
     roof["algorithmic_bytes_per_launch"] = alg_bytes_attn
     roof["launch_ms"] = attn_ms
@@ -362,7 +430,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if sharded else "weak",
         "vs_baseline": None,
         "dtype": "f16 (int8 KV unpacked exactly to f16 for mma, f32 accumulate)",
         "data": "synthetic (seeded N(0,1) K/V, fragmented seeded page tables)",
@@ -376,8 +444,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
             "kv_bytes_per_step_per_gpu": kv_bytes,
             "l2": "inputs larger than L2: the pool read per step exceeds 126 MB" if wl.kv_bytes(1) > 126e6
             else "pool fits in L2 (small workload)",
-            "parallelism": f"slot-sharded x{world} (each rank its own slots, no collective)",
-            "launch": "direct C-ABI calls" if args.no_graph else "CUDA graph replay of the step's C-ABI calls",
+            "parallelism": (f"kv-head x sequence sharded x{world} (partials all-gathered over NCCL, LSE combine)"
+                            if sharded else f"slot-sharded x{world} (each rank its own slots, no collective)"),
+            "launch": "direct C-ABI calls" if (args.no_graph or sharded) else "CUDA graph replay of the step's C-ABI calls",
         },
         "kv_gbs": kv_bytes * world / (ms * 1e-3) / 1e9,
         "hbm_frac_step": kv_bytes / (ms * 1e-3) / 1e9 / hbm,

@@ -209,6 +209,34 @@ YF_API int yf_attn_prefill(yf_pool* pool, int32_t layer, const void* d_q, int32_
                            int32_t max_seqlen_q, int32_t max_seqlen_k, float scale, void* d_out,
                            void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* Sharded decode, first half: yf_attn_decode over the keys this pool holds
+ * (one shard of each sequence and/or a subset of the kv heads), emitting
+ * partials instead of f16 output: d_o_part f32 [B, Hq, D] is O normalised
+ * over the shard's keys and d_lse_part f32 [B, Hq] is the natural-log
+ * log-sum-exp of the shard's scaled logits (-inf, with O = 0, for a shard
+ * without keys).  Replaces the partial (o, lse) output of the reference's
+ * split-KV kernel that flash_fwd_splitkv_combine_kernel consumes
+ * (docs/plans/2026-09-16-prefil-parity-fa2-and-mmq.md:104-107), with the
+ * shards on different GPUs.  d_o_part and d_lse_part 16- and 4-byte aligned. */
+YF_API int yf_attn_decode_partial(yf_pool* pool, int32_t layer, const void* d_q, int32_t n_q_heads,
+                                  const uint32_t* d_cu_seqlens_k, const uint32_t* d_block_table,
+                                  int32_t max_blocks, int32_t batch, int32_t max_seqlen_k, float scale,
+                                  float* d_o_part, float* d_lse_part, void* d_workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* Sharded decode, second half: merges n_parts partials of `rows` rows into
+ * d_out f16 [rows][head_dim].  Part k's O, f32 [rows][head_dim], starts at
+ * d_o_parts + k * o_part_stride and its lse, f32 [rows], at d_lse_parts +
+ * k * lse_part_stride (strides in floats), so partials packed per rank as
+ * one all-gathered buffer are read in place.
+ * out = sum_k exp(lse_k - M) o_k / sum_k exp(lse_k - M), M = max_k lse_k
+ * (zeros where every lse is -inf).  The LSE merge of
+ * flash_fwd_splitkv_combine_kernel (same citation), across GPUs.
+ * head_dim a multiple of 4; every O part 16-byte aligned, d_out 8-byte. */
+YF_API int yf_attn_combine(const float* d_o_parts, int64_t o_part_stride, const float* d_lse_parts,
+                           int64_t lse_part_stride, int32_t n_parts, int32_t rows, int32_t head_dim, void* d_out,
+                           void* stream);
+
 /* ---- prefix snapshot export / restore ----------------------------------------
  * Byte copies of whole pages (all KV heads, one layer) with their scales and
  * no requantization, as StateSnapshot::to_host / to_device do for the int8

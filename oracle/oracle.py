@@ -293,6 +293,36 @@ def np_attn(desc: PoolDesc, pool: np.ndarray, layer: int, q: np.ndarray, cu_q, c
     return out
 
 
+def np_partial_decode(q: np.ndarray, K: np.ndarray, V: np.ndarray, scale: float):
+    """One decode row over one key range, as the split-KV partial the reference's combine
+    consumes: q [hq, D] (f16 values), K/V [n_keys, D] dequantized.  Returns (O [hq, D]
+    normalised over the range, lse [hq] = ln sum exp(q.k * scale)); a range without keys gives
+    (0, -inf).  Float64."""
+    q = np.asarray(q, np.float16).astype(np.float64)
+    hq, D = q.shape
+    if K.shape[0] == 0:
+        return np.zeros((hq, D)), np.full(hq, -np.inf)
+    s = q @ K.astype(np.float64).T * scale
+    m = s.max(axis=1, keepdims=True)
+    p = np.exp(s - m)
+    l = p.sum(axis=1, keepdims=True)
+    return (p @ V.astype(np.float64)) / l, (m + np.log(l))[:, 0]
+
+
+def np_combine(o_parts: np.ndarray, lse_parts: np.ndarray) -> np.ndarray:
+    """LSE merge of partials (flash_fwd_splitkv_combine_kernel's formula,
+    docs/plans/2026-09-16-prefil-parity-fa2-and-mmq.md:104-107): o_parts [n, rows, D],
+    lse_parts [n, rows] -> [rows, D]; rows whose every lse is -inf give zeros."""
+    o = np.asarray(o_parts, np.float64)
+    lse = np.asarray(lse_parts, np.float64)
+    M = lse.max(axis=0)
+    finite = np.isfinite(M)
+    w = np.where(np.isfinite(lse), np.exp(lse - np.where(finite, M, 0.0)), 0.0)
+    L = w.sum(axis=0)
+    out = np.einsum("nr,nrd->rd", w, o)
+    return np.where(L[:, None] > 0, out / np.where(L > 0, L, 1.0)[:, None], 0.0)
+
+
 def error_profile(err: np.ndarray):
     """Per-head and per-row max |error| of an error tensor [1, seq, heads, dim]
     (the helper of src/bin/fa_probe.rs:107-112)."""

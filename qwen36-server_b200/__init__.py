@@ -7,8 +7,10 @@ package is the host-side mirror of the engine's operator surface
 from ._abi import YfError, lib  # noqa: F401
 from .paged_attn import (  # noqa: F401
     PagedKvPool,
+    combine_partials,
     default_scale,
     dispatch_flash_decode_paged,
+    dispatch_flash_decode_partial,
     forward_attn_prefill_paged,
     forward_verify_paged,
     kv_append_paged,

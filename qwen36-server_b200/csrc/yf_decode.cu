@@ -67,6 +67,8 @@ struct SplitParams {
     int max_chunks;
     float scale_log2;
     __half* out;
+    float* part_o;    // partial output (f32 O + natural-log lse) instead of `out`, or null
+    float* part_lse;
     float* ws_o;
     float* ws_lse;
     uint32_t* counters;  // per-unit arrival counters for the merge, or null (separate combine)
@@ -107,6 +109,23 @@ __device__ __forceinline__ bool unit_geom(const SplitParams& p, int b, int rg, U
 __device__ __forceinline__ size_t row_offset(const SplitParams& p, const UnitGeom& u, int h, int row, int D) {
     const int j = row / p.G, gi = row % p.G;
     return ((size_t)(u.qrow0 + j) * p.Hq + (size_t)h * p.G + gi) * D;
+}
+
+// Final output of dims d4 .. d4+3 of `row` (kv head h of unit u): normalised O `v` and the
+// row's base-2 lse `lse2` (-inf without keys).  f16 into out, or with partial output on, f32
+// O into part_o (same layout) and the natural-log lse into part_lse[row][q head].
+__device__ __forceinline__ void store_row4(const SplitParams& p, const UnitGeom& u, int h, int row, int d4, int D,
+                                           float4 v, float lse2) {
+    const size_t off = row_offset(p, u, h, row, D);
+    if (p.part_o) {
+        *reinterpret_cast<float4*>(p.part_o + off + d4) = v;
+        if (d4 == 0) p.part_lse[off / D] = lse2 * 0.6931471805599453f;
+    } else {
+        uint2 pk;
+        pk.x = pack_h2(v.x, v.y);
+        pk.y = pack_h2(v.z, v.w);
+        *reinterpret_cast<uint2*>(p.out + off + d4) = pk;
+    }
 }
 
 // ---- per-warp state and tile math ------------------------------------------------------
@@ -479,10 +498,7 @@ __device__ __forceinline__ void emit_unit(const SplitParams& p, const UnitGeom& 
         acc.z *= inv;
         acc.w *= inv;
         if (direct) {
-            uint2 pk;
-            pk.x = pack_h2(acc.x, acc.y);
-            pk.y = pack_h2(acc.z, acc.w);
-            *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, row, D) + d4) = pk;
+            store_row4(p, u, h, row, d4, D, acc, L > 0.f ? M + __log2f(L) : -INFINITY);
         } else {
             *reinterpret_cast<float4*>(p.ws_o + (item * RPC + r) * D + d4) = acc;
             if (d4 == 0) p.ws_lse[item * RPC + r] = L > 0.f ? M + __log2f(L) : -INFINITY;
@@ -515,10 +531,8 @@ __device__ __forceinline__ void combine_items(const SplitParams& p, const UnitGe
             acc.w = fmaf(f, ov.w, acc.w);
         }
         const float inv = L > 0.f ? 1.f / L : 0.f;
-        uint2 pk;
-        pk.x = pack_h2(acc.x * inv, acc.y * inv);
-        pk.y = pack_h2(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, row, D) + d4) = pk;
+        store_row4(p, u, h, row, d4, D, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv),
+                   L > 0.f ? M + __log2f(L) : -INFINITY);
     }
 }
 
@@ -596,10 +610,7 @@ __device__ __forceinline__ void merge_parts(const SplitParams& p, const UnitGeom
         const int e = threadIdx.x + i * kThreads;
         const int r = e / (D / 4), d4 = (e % (D / 4)) * 4;
         if (dst_item < 0) {
-            uint2 pk;
-            pk.x = pack_h2(acc[i].x, acc[i].y);
-            pk.y = pack_h2(acc[i].z, acc[i].w);
-            *reinterpret_cast<uint2*>(p.out + row_offset(p, u, h, u.row_begin + r, D) + d4) = pk;
+            store_row4(p, u, h, u.row_begin + r, d4, D, acc[i], lse_out[r]);
         } else {
             __stcg(reinterpret_cast<float4*>(p.ws_o + (size_t)dst_item * RPC * D + eoff[i]), acc[i]);
         }
@@ -711,10 +722,10 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
         if (sP[b + 1] != sP[b]) continue;
         UnitGeom u;
         if (!unit_geom<TPP, RPC>(p, b, 0, u, false)) continue;
-        for (int e = threadIdx.x; e < u.rows_total * H * (D / 8); e += kThreads) {
-            const int d8 = (e % (D / 8)) * 8, rh = e / (D / 8);
+        for (int e = threadIdx.x; e < u.rows_total * H * (D / 4); e += kThreads) {
+            const int d4 = (e % (D / 4)) * 4, rh = e / (D / 4);
             const int row = rh % u.rows_total, h = rh / u.rows_total;
-            *reinterpret_cast<uint4*>(p.out + row_offset(p, u, h, row, D) + d8) = make_uint4(0, 0, 0, 0);
+            store_row4(p, u, h, row, d4, D, make_float4(0.f, 0.f, 0.f, 0.f), -INFINITY);
         }
     }
     if (s >= e_end) return;
@@ -927,6 +938,8 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.max_chunks = plan.max_chunks;
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.out = a.out;
+    p.part_o = a.part_o;
+    p.part_lse = a.part_lse;
     p.status = a.pool->d_status;
     const size_t units = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups;
     p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;

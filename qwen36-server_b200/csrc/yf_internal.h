@@ -105,6 +105,10 @@ struct AttnArgs {
     void* workspace;
     size_t workspace_bytes;
     cudaStream_t stream;
+    // partial output instead of `out`: normalised f32 O in out's layout and the natural-log
+    // sum of exp(scaled logits) per (row, q head), for a later yf_attn_combine
+    float* part_o = nullptr;
+    float* part_lse = nullptr;
 };
 
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).

@@ -363,10 +363,13 @@ size_t yf_attn_workspace_size(const yf_pool* pool, int32_t hq, int32_t batch, in
 
 static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,
                     const uint32_t* cu_k, const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_q,
-                    int32_t max_k, float scale, void* out, void* ws, size_t ws_bytes, void* stream) {
-    const int rc = check_attn(pool, layer, q, hq, cu_k, bt, max_blocks, batch, max_q, max_k, scale, out);
+                    int32_t max_k, float scale, void* out, void* ws, size_t ws_bytes, void* stream,
+                    float* part_o = nullptr, float* part_lse = nullptr) {
+    const int rc =
+        check_attn(pool, layer, q, hq, cu_k, bt, max_blocks, batch, max_q, max_k, scale, part_o ? part_o : out);
     if (rc || batch == 0) return rc;
-    const bool tc = cu_q && prefill_tc_applies(pool, hq, max_q);
+    if (part_o && (!part_lse || !aligned(part_lse, 4))) return fail(YF_E_INVALID, "lse output null or misaligned");
+    const bool tc = !part_o && cu_q && prefill_tc_applies(pool, hq, max_q);
     const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k);
     if (!tc && plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
         return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", plan.ws_bytes,
@@ -388,6 +391,8 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     a.workspace = ws;
     a.workspace_bytes = ws_bytes;
     a.stream = static_cast<cudaStream_t>(stream);
+    a.part_o = part_o;
+    a.part_lse = part_lse;
     if (tc) return launch_prefill_tc(a);
     return launch_splitkv(a, plan);
 }
@@ -397,6 +402,14 @@ int yf_attn_decode(yf_pool* pool, int32_t layer, const void* q, int32_t hq, cons
                    void* ws, size_t ws_bytes, void* stream) {
     return run_attn(pool, layer, q, hq, nullptr, cu_k, bt, max_blocks, batch, 1, max_k, scale, out, ws, ws_bytes,
                     stream);
+}
+
+int yf_attn_decode_partial(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_k,
+                           const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_k, float scale,
+                           float* o_part, float* lse_part, void* ws, size_t ws_bytes, void* stream) {
+    if (batch > 0 && !o_part) return fail(YF_E_INVALID, "partial O output is null");
+    return run_attn(pool, layer, q, hq, nullptr, cu_k, bt, max_blocks, batch, 1, max_k, scale, nullptr, ws, ws_bytes,
+                    stream, o_part, lse_part);
 }
 
 int yf_attn_prefill(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,

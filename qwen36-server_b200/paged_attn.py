@@ -247,6 +247,58 @@ def dispatch_flash_decode_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, 
     return out
 
 
+def dispatch_flash_decode_partial(q: torch.Tensor, pool: PagedKvPool, layer: int, lens, table, scale: float,
+                                  max_seqlen_k: Optional[int] = None, o_part: Optional[torch.Tensor] = None,
+                                  lse_part: Optional[torch.Tensor] = None,
+                                  workspace: Optional[torch.Tensor] = None):
+    """Decode over the keys this pool holds (one shard), as partials: returns (o f32 [B, Hq, D]
+    normalised over the shard, lse f32 [B, Hq] natural-log log-sum-exp of the scaled logits)."""
+    B, Hq, D = q.shape
+    if q.dtype != torch.float16 or D != pool.head_dim or not q.is_contiguous():
+        raise YfError(_abi.YF_E_INVALID, "dispatch_flash_decode_partial", "q must be contiguous f16 [B, Hq, D]")
+    if max_seqlen_k is None:
+        max_seqlen_k = _max_len(lens)
+    lens = _i32(lens, pool.device)
+    table = _i32(table, pool.device)
+    if o_part is None:
+        o_part = torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
+    if lse_part is None:
+        lse_part = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    ws, ws_bytes = _ws_args(pool, workspace, pool.workspace_size(Hq, B, 1, max_seqlen_k))
+    call("yf_attn_decode_partial", pool.handle, layer, _ptr(q), Hq, _ptr(lens), _ptr(table), table.shape[1], B,
+         max_seqlen_k, ctypes.c_float(scale), _ptr(o_part), _ptr(lse_part), ws, ws_bytes, _stream(pool.device))
+    return o_part, lse_part
+
+
+def combine_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+                     n_parts: Optional[int] = None, rows: Optional[int] = None, head_dim: Optional[int] = None,
+                     o_part_stride: Optional[int] = None, lse_part_stride: Optional[int] = None):
+    """LSE merge of n partials into f16 [rows, D] (or ``out``).  By default o_parts is f32
+    [n, rows, D] and lse_parts f32 [n, rows]; with explicit counts and strides (in floats) both
+    may be views into one buffer that packs each part's O and lse together."""
+    if n_parts is None:
+        n_parts = int(o_parts.shape[0])
+    if head_dim is None:
+        head_dim = int(o_parts.shape[-1])
+    if rows is None:
+        rows = int(lse_parts[0].numel())
+    if o_part_stride is None:
+        o_part_stride = rows * head_dim
+    if lse_part_stride is None:
+        lse_part_stride = rows
+    if o_parts.dtype != torch.float32 or lse_parts.dtype != torch.float32:
+        raise YfError(_abi.YF_E_INVALID, "combine_partials", "partials must be f32")
+    need_o = (n_parts - 1) * o_part_stride + rows * head_dim
+    need_l = (n_parts - 1) * lse_part_stride + rows
+    if o_parts.numel() < need_o or lse_parts.numel() < need_l:
+        raise YfError(_abi.YF_E_INVALID, "combine_partials", "partials smaller than n_parts x strides")
+    if out is None:
+        out = torch.empty((rows, head_dim), dtype=torch.float16, device=o_parts.device)
+    call("yf_attn_combine", _ptr(o_parts), int(o_part_stride), _ptr(lse_parts), int(lse_part_stride), n_parts,
+         rows, head_dim, _ptr(out), _stream(o_parts.device))
+    return out
+
+
 def forward_attn_prefill_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, cu_seqlens_q, cu_seqlens_k, table,
                                scale: float, max_seqlen_q: Optional[int] = None,
                                max_seqlen_k: Optional[int] = None, out: Optional[torch.Tensor] = None,

@@ -1,0 +1,147 @@
+"""Long-context decode split across GPUs: kv heads first, then contiguous key ranges.
+
+A sequence too long for one GPU to read quickly (the 131072-key, 2-kv-head decode) is
+split into world = n_head_groups x n_seq shards.  Rank r owns kv-head group r % n_head_groups
+and key range r // n_head_groups of the sequence, holds only those pages in its own pool,
+and runs yf_attn_decode_partial over them.  Every rank's packed partial
+([O f32 B*hq*D | lse f32 B*hq]) reaches every rank through one all-gather (NCCL over
+NVLink), and yf_attn_combine merges the key ranges of each head group in place in the
+gathered buffer.  This replaces the reference's single-GPU split-KV + combine
+(flash_fwd_splitkv_combine_kernel, docs/plans/2026-09-16-prefil-parity-fa2-and-mmq.md:104-107)
+for a sequence spread over GPUs; partitions with independent slots need no such exchange.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List
+
+import torch
+
+from . import paged_attn as pa
+
+
+@dataclass(frozen=True)
+class LongShard:
+    """What rank `rank` of `world` holds."""
+    rank: int
+    world: int
+    n_head_groups: int
+    head_group: int
+    kv_head0: int       # first kv head of the group
+    kv_heads: int       # kv heads per group
+    n_seq: int
+    seq: int
+    k0: int             # first key of the range
+    k1: int             # one past the last key
+
+
+def long_context_plan(world: int, n_kv_heads: int, ctx: int, page_size: int = 16) -> List[LongShard]:
+    """Shards of one sequence of `ctx` keys: world divides n_kv_heads (heads split, whole
+    sequence per rank) or n_kv_heads divides world (one head group of one kv head, and
+    world / n_kv_heads page-aligned key ranges).  Rank order is seq-major:
+    rank = seq * n_head_groups + head_group."""
+    if world < 1 or n_kv_heads < 1:
+        raise ValueError("world and n_kv_heads must be >= 1")
+    if world <= n_kv_heads:
+        if n_kv_heads % world:
+            raise ValueError(f"world {world} does not divide n_kv_heads {n_kv_heads}")
+        n_hg, n_seq = world, 1
+    else:
+        if world % n_kv_heads:
+            raise ValueError(f"n_kv_heads {n_kv_heads} does not divide world {world}")
+        n_hg, n_seq = n_kv_heads, world // n_kv_heads
+    hpg = n_kv_heads // n_hg
+    per = -(-(-(-ctx // n_seq)) // page_size) * page_size
+    out = []
+    for r in range(world):
+        hg, s = r % n_hg, r // n_hg
+        out.append(LongShard(r, world, n_hg, hg, hg * hpg, hpg, n_seq, s, min(ctx, s * per), min(ctx, (s + 1) * per)))
+    return out
+
+
+def packed_floats(batch: int, q_heads: int, head_dim: int) -> int:
+    """Floats of one rank's packed partial: O [batch, q_heads, head_dim] then lse [batch, q_heads],
+    padded so that every rank's O starts 16-byte aligned in the gathered buffer."""
+    n = batch * q_heads * (head_dim + 1)
+    return -(-n // 4) * 4
+
+
+def combine_views(shard: LongShard, batch: int, q_heads: int, head_dim: int):
+    """For each head group g: (o_offset, lse_offset, part_stride, n_parts, rows) of its parts
+    in the gathered buffer [world][packed_floats], in floats."""
+    blk = packed_floats(batch, q_heads, head_dim)
+    rows = batch * q_heads
+    return [(g * blk, g * blk + rows * head_dim, shard.n_head_groups * blk, shard.n_seq, rows)
+            for g in range(shard.n_head_groups)]
+
+
+def gather_packed(local: torch.Tensor, gathered: torch.Tensor, world: int, group=None) -> None:
+    """Every rank's packed partial into `gathered` [world * len(local)], in rank order."""
+    if world > 1:
+        torch.distributed.all_gather_into_tensor(gathered, local, group=group)
+    else:
+        gathered.copy_(local)
+
+
+class ShardedLongDecode:
+    """One rank's share of a sharded decode (batch entries, all of one length split alike).
+
+    ``pool`` holds this rank's kv heads and key range; the caller writes the shard's keys into
+    it (positions k - k0) and passes the shard's cu_seqlens_k / block table to step()."""
+
+    def __init__(self, shard: LongShard, n_q_heads: int, n_kv_heads: int, head_dim: int, n_pages: int,
+                 page_size: int = 16, group_size: int = 32, batch: int = 1, device: int = 0,
+                 process_group=None):
+        if n_q_heads % n_kv_heads:
+            raise ValueError("n_q_heads must be a multiple of n_kv_heads")
+        self.shard, self.batch, self.D = shard, batch, head_dim
+        self.G = n_q_heads // n_kv_heads
+        self.hq = shard.kv_heads * self.G  # q heads of this rank
+        self.Hq = n_q_heads
+        self.group = process_group
+        self.dev = torch.device("cuda", device)
+        self.pool = pa.PagedKvPool(1, n_pages, shard.kv_heads, head_dim, page_size, group_size, device=device)
+        blk = packed_floats(batch, self.hq, head_dim)
+        self.local = torch.zeros(blk, dtype=torch.float32, device=self.dev)
+        self.gathered = torch.zeros(shard.world * blk, dtype=torch.float32, device=self.dev)
+        n_o = batch * self.hq * head_dim
+        self.o_part = self.local[:n_o].view(batch, self.hq, head_dim)
+        self.lse_part = self.local[n_o:n_o + batch * self.hq].view(batch, self.hq)
+        self.out = torch.empty((batch, n_q_heads, head_dim), dtype=torch.float16, device=self.dev)
+        self._grp_out = None if batch == 1 or shard.n_head_groups == 1 else torch.empty(
+            (shard.n_head_groups, batch * self.hq, head_dim), dtype=torch.float16, device=self.dev)
+        self.ws = None
+
+    def q_slice(self, q: torch.Tensor) -> torch.Tensor:
+        """This rank's q heads of a full q [B, Hq, D]."""
+        h0 = self.shard.kv_head0 * self.G
+        return q[:, h0:h0 + self.hq].contiguous()
+
+    def partial(self, q_local: torch.Tensor, cu_k, table, scale: float, max_seqlen_k: int):
+        if self.ws is None:
+            n = self.pool.workspace_size(self.hq, self.batch, 1, max_seqlen_k)
+            self.ws = torch.empty(max(n, 16), dtype=torch.uint8, device=self.dev)
+        pa.dispatch_flash_decode_partial(q_local, self.pool, 0, cu_k, table, scale, max_seqlen_k=max_seqlen_k,
+                                         o_part=self.o_part, lse_part=self.lse_part, workspace=self.ws)
+
+    def exchange(self):
+        gather_packed(self.local, self.gathered, self.shard.world, self.group)
+
+    def combine(self) -> torch.Tensor:
+        flat = self.out.view(self.batch * self.Hq, self.D)
+        for g, (oo, lo, stride, n_parts, rows) in enumerate(combine_views(self.shard, self.batch, self.hq, self.D)):
+            # one head group: its rows are contiguous in the output when B == 1 or there is one group
+            dst = self._grp_out[g] if self._grp_out is not None else flat[g * rows:(g + 1) * rows]
+            pa.combine_partials(self.gathered[oo:], self.gathered[lo:], out=dst, n_parts=n_parts, rows=rows,
+                                head_dim=self.D, o_part_stride=stride, lse_part_stride=stride)
+        if self._grp_out is not None:
+            self.out.view(self.batch, self.shard.n_head_groups, self.hq, self.D).copy_(
+                self._grp_out.view(self.shard.n_head_groups, self.batch, self.hq, self.D).transpose(0, 1))
+        return self.out
+
+    def step(self, q_local: torch.Tensor, cu_k, table, scale: float, max_seqlen_k: int) -> torch.Tensor:
+        """Partial over this shard, all-gather, combine: the full f16 output [B, Hq, D] on every rank."""
+        self.partial(q_local, cu_k, table, scale, max_seqlen_k)
+        self.exchange()
+        return self.combine()
+
