@@ -11,7 +11,7 @@
 // N dimension so every K/V byte is read once per unit.  The unit's keys are
 // 16-token tiles, each one contiguous block of the pool (K int8 + scales +
 // V int8 + scales).  Each of a CTA's 4 warps streams its own tiles: lane 0
-// issues a 1-D bulk copy (cp.async.bulk, no multicast) of the whole tile into
+// issues a 1-D bulk copy (cp.async.bulk into this CTA only) of the whole tile into
 // a per-warp ring of shared-memory stages, completing on an mbarrier, and
 // loads the next tile's page id one tile ahead.  The tile bytes are laid out
 // so that each lane's 16-byte shared load is exactly its mma.sync fragment:

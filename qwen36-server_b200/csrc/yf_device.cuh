@@ -1,5 +1,5 @@
 // Device-side helpers: shared-memory addressing, mbarriers, 1-D bulk copies
-// (TMA, no multicast), warp MMA, and int8 -> f16 unpacking.
+// (TMA into this CTA only), warp MMA, and int8 -> f16 unpacking.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
-// Both addresses 16-byte aligned, bytes a multiple of 16.  No multicast.
+// Both addresses 16-byte aligned, bytes a multiple of 16.  This CTA is the only destination.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     uint64_t g;
     asm volatile("cvta.to.global.u64 %0, %1;" : "=l"(g) : "l"(src));
