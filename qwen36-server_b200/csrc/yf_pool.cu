@@ -74,12 +74,21 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     const char* st = getenv("YF_DECODE_STAGES");  // host-side tuning override
     if (st && atoi(st) == 3) p.stages = 3;
     const char* fc = getenv("YF_FUSED_COMBINE");
-    p.fused_combine = !(fc && atoi(fc) == 0);
+    const bool fused_env = !(fc && atoi(fc) == 0);
+    // the in-kernel merge of the chunked schedule keeps (chunks + 1) x rows floats of weights
+    // in the CTA's stage area (4 warps x stages x tile bytes); the persistent schedule merges
+    // at most 16 or kMaxGroupCounters / 2 / 16 parts at a time
+    {
+        const int D = pool->desc.head_dim, NB = D / pool->desc.group_size;
+        const long long area_floats = 4LL * p.stages * (32 * D + 64 * NB) / 4;
+        p.fused_combine = fused_env && (long long)(p.max_chunks + 1) * p.rows_per_cta <= area_floats;
+    }
     // Persistent schedule: one row group per entry (decode, small verify blocks), a batch whose
     // tile prefix fits in shared memory, and the merge counters available.
     const char* ps = getenv("YF_PERSISTENT");
     p.persistent = !(ps && atoi(ps) == 0) && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
-                   units <= kMaxCombineUnits && p.fused_combine;
+                   units <= kMaxCombineUnits && fused_env;
+    if (p.persistent) p.fused_combine = true;
     const size_t row_bytes = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
     if (p.persistent) {
         // at least 16 tiles (4 per warp) per CTA, at most kMaxCtasPerSm CTAs per SM
