@@ -640,29 +640,165 @@ __device__ __forceinline__ void arrive_and_merge(const SplitParams& p, const Uni
     if (threadIdx.x == 0) p.counters[unit] = 0;  // ready for the next call on this pool
 }
 
-// Two-level merge of the persistent schedule: pieces form groups of kMergeGroup; the last
-// arrival of a group merges it into the group's first slot, and the last group merges the
-// group results into the output.
-constexpr int kMergeGroup = 16;
+// ---- cooperative merge of the persistent schedule ------------------------------------------
+// Every CTA of a split unit arrives on the unit's counter (low 16 bits); the CTAs whose range
+// ends inside the unit then wait for all of the unit's parts and merge one slice each of the
+// unit's output columns (all of a slice's loads in flight at once), and count their
+// departure (high 16 bits); the last to leave resets the counter for the next call.  A CTA
+// that goes on to the next unit only arrives.  The grid is a single resident wave, so the
+// waits end; each is bounded by kWaitLimitNs and flags YF_DEV_TIMEOUT if it gives up.
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* ptr) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+// Online merge of one (base-2 lse, normalised O) part into (m, l, o).
+__device__ __forceinline__ void merge_in(float lv, float4 ov, float& m, float& l, float4& o) {
+    if (lv == -INFINITY) return;
+    if (lv > m) {
+        const float f = m == -INFINITY ? 0.f : fast_exp2(m - lv);
+        l *= f;
+        o.x *= f;
+        o.y *= f;
+        o.z *= f;
+        o.w *= f;
+        m = lv;
+    }
+    const float w = fast_exp2(lv - m);
+    l += w;
+    o.x = fmaf(w, ov.x, o.x);
+    o.y = fmaf(w, ov.y, o.y);
+    o.z = fmaf(w, ov.z, o.z);
+    o.w = fmaf(w, ov.w, o.w);
+}
+
+// Slice `slice` of `n_slices` of the unit's RPC x D/4 output columns (float4), merged over the
+// n parts whose workspace items are items[0..n-1].
+template <int D, int RPC>
+__device__ __forceinline__ void merge_slice(const SplitParams& p, const UnitGeom& u, int h, int n,
+                                            const uint32_t* items, int slice, int n_slices) {
+    constexpr int COLS = RPC * (D / 4);
+    constexpr int PB = 8;  // parts per lane (or thread) loaded together
+    const int c0 = (int)((long long)slice * COLS / n_slices), c1 = (int)((long long)(slice + 1) * COLS / n_slices);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n >= 32) {
+        // a warp per column, its lanes over the parts, then the lanes' states merged
+        for (int col = c0 + warp; col < c1; col += kWarps) {
+            const int r = col / (D / 4), d4 = (col % (D / 4)) * 4;
+            if (u.row_begin + r >= u.rows_total) continue;
+            float m = -INFINITY, l = 0.f;
+            float4 o = zero;
+            for (int k0 = lane; k0 < n; k0 += 32 * PB) {
+                float lv[PB];
+                float4 ov[PB];
+#pragma unroll
+                for (int j = 0; j < PB; ++j) {
+                    const int k = k0 + 32 * j;
+                    lv[j] = -INFINITY;
+                    ov[j] = zero;
+                    if (k < n) {
+                        const size_t it = items[k];
+                        lv[j] = __ldcg(p.ws_lse + it * RPC + r);
+                        ov[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (it * RPC + r) * D + d4));
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < PB; ++j) merge_in(lv[j], ov[j], m, l, o);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+                const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
+                float4 o2;
+                o2.x = __shfl_xor_sync(0xffffffffu, o.x, off);
+                o2.y = __shfl_xor_sync(0xffffffffu, o.y, off);
+                o2.z = __shfl_xor_sync(0xffffffffu, o.z, off);
+                o2.w = __shfl_xor_sync(0xffffffffu, o.w, off);
+                const float M = fmaxf(m, m2);
+                if (M != -INFINITY) {
+                    const float f1 = m == -INFINITY ? 0.f : fast_exp2(m - M);
+                    const float f2 = m2 == -INFINITY ? 0.f : fast_exp2(m2 - M);
+                    l = l * f1 + l2 * f2;
+                    o.x = o.x * f1 + o2.x * f2;
+                    o.y = o.y * f1 + o2.y * f2;
+                    o.z = o.z * f1 + o2.z * f2;
+                    o.w = o.w * f1 + o2.w * f2;
+                    m = M;
+                }
+            }
+            if (lane == 0) {
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                store_row4(p, u, h, u.row_begin + r, d4, D, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
+                           l > 0.f ? m + __log2f(l) : -INFINITY);
+            }
+        }
+    } else {
+        // a thread per column, over every part
+        for (int col = c0 + threadIdx.x; col < c1; col += kThreads) {
+            const int r = col / (D / 4), d4 = (col % (D / 4)) * 4;
+            if (u.row_begin + r >= u.rows_total) continue;
+            float m = -INFINITY, l = 0.f;
+            float4 o = zero;
+            for (int k0 = 0; k0 < n; k0 += PB) {
+                float lv[PB];
+                float4 ov[PB];
+#pragma unroll
+                for (int j = 0; j < PB; ++j) {
+                    lv[j] = -INFINITY;
+                    ov[j] = zero;
+                    if (k0 + j < n) {
+                        const size_t it = items[k0 + j];
+                        lv[j] = __ldcg(p.ws_lse + it * RPC + r);
+                        ov[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (it * RPC + r) * D + d4));
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < PB; ++j) merge_in(lv[j], ov[j], m, l, o);
+            }
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            store_row4(p, u, h, u.row_begin + r, d4, D, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
+                       l > 0.f ? m + __log2f(l) : -INFINITY);
+        }
+    }
+}
 
 template <int D, int RPC, typename ItemOf>
-__device__ __forceinline__ void arrive_and_merge_2level(const SplitParams& p, const UnitGeom& u, int h, size_t unit,
-                                                        int n_parts, int k_self, ItemOf item_of, float* wsm,
-                                                        int* s_flag) {
-    if (n_parts <= kMergeGroup) {
-        arrive_and_merge<D, RPC>(p, u, h, unit, n_parts, item_of, wsm, s_flag);
-        return;
+__device__ __forceinline__ void cooperative_merge(const SplitParams& p, const UnitGeom& u, int h, size_t unit,
+                                                  int n_parts, ItemOf item_of, bool merger, int slice, int n_slices,
+                                                  uint32_t* s_items, int* s_flag) {
+    uint32_t* ctr = &p.counters[unit];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(ctr, 1u);
+    if (!merger) return;
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        if ((ld_acquire_u32(ctr) & 0xFFFFu) < (uint32_t)n_parts) {
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t i = 0;; ++i) {
+                if ((ld_acquire_u32(ctr) & 0xFFFFu) >= (uint32_t)n_parts) break;
+                if ((i & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        if (!ok) atomicOr(p.status, YF_DEV_TIMEOUT);
+        *s_flag = ok;
     }
-    const int g0 = k_self / kMergeGroup * kMergeGroup;
-    const int gn = min(kMergeGroup, n_parts - g0);
-    const size_t first = item_of(g0);
-    uint32_t* gctr = p.counters + kMaxCombineUnits + first;
-    if (!arrive_last(gctr, gn, s_flag)) return;
-    merge_parts<D, RPC>(p, u, h, gn, [&](int k) { return item_of(g0 + k); }, wsm, (long long)first);
-    if (threadIdx.x == 0) *gctr = 0;
-    const int n_groups = (n_parts + kMergeGroup - 1) / kMergeGroup;
-    arrive_and_merge<D, RPC>(p, u, h, unit, n_groups, [&](int k) { return item_of(k * kMergeGroup); }, wsm,
-                             s_flag);
+    for (int k = threadIdx.x; k < n_parts; k += kThreads) s_items[k] = (uint32_t)item_of(k);
+    __syncthreads();
+    __threadfence();
+    if (*s_flag) merge_slice<D, RPC>(p, u, h, n_parts, s_items, slice, n_slices);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t old = atomicAdd(ctr, 0x10000u);
+        if ((old >> 16) == (uint32_t)n_slices - 1) atomicExch(ctr, 0u);  // the last merger leaves
+    }
 }
 
 // ---- schedule 1: persistent, equal contiguous ranges of (unit, tile) ------------------------
@@ -771,9 +907,12 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
                 const long long c = c_lo + k;
                 return (size_t)c * 2 + (start_of(c) < Us ? 1 : 0);
             };
-            arrive_and_merge_2level<D, RPC>(p, u, h, (size_t)b * H + h, (int)(c_hi - c_lo + 1),
-                                            (int)(blockIdx.x - c_lo), item_of, reinterpret_cast<float*>(stages),
-                                            &s_last);
+            // mergers: the unit's CTAs whose range ends inside it (all but c_hi, and c_hi too when
+            // its range ends exactly at the unit's end)
+            const long long p_hi = start_of(c_hi + 1) == Ue ? c_hi : c_hi - 1;
+            cooperative_merge<D, RPC>(p, u, h, (size_t)b * H + h, (int)(c_hi - c_lo + 1), item_of, e_end <= Ue,
+                                      (int)(blockIdx.x - c_lo), (int)(p_hi - c_lo + 1),
+                                      reinterpret_cast<uint32_t*>(stages), &s_last);
         }
         // the merge area is the next unit's stage area: order its generic accesses before the
         // bulk copies that will overwrite it

@@ -77,7 +77,7 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     const bool fused_env = !(fc && atoi(fc) == 0);
     // the in-kernel merge of the chunked schedule keeps (chunks + 1) x rows floats of weights
     // in the CTA's stage area (4 warps x stages x tile bytes); the persistent schedule merges
-    // at most 16 or kMaxGroupCounters / 2 / 16 parts at a time
+    // its CTAs (at most kMaxGroupCounters / 2) in one cooperative pass
     {
         const int D = pool->desc.head_dim, NB = D / pool->desc.group_size;
         const long long area_floats = 4LL * p.stages * (32 * D + 64 * NB) / 4;
