@@ -903,10 +903,10 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
         emit_unit<D, NT>(p, u, h, stages, whole, item);
         if (!whole) {
             const long long c_lo = cta_of(Us), c_hi = cta_of(Ue - 1);
-            auto item_of = [&](int k) -> size_t {
-                const long long c = c_lo + k;
-                return (size_t)c * 2 + (start_of(c) < Us ? 1 : 0);
-            };
+            // partial slot of part k (CTA c_lo + k): only the unit's first CTA can have begun
+            // inside an earlier unit (slot 1)
+            const size_t item0 = (size_t)c_lo * 2 + (start_of(c_lo) < Us ? 1 : 0);
+            auto item_of = [&](int k) -> size_t { return k == 0 ? item0 : (size_t)(c_lo + k) * 2; };
             // mergers: the unit's CTAs whose range ends inside it (all but c_hi, and c_hi too when
             // its range ends exactly at the unit's end)
             const long long p_hi = start_of(c_hi + 1) == Ue ? c_hi : c_hi - 1;
