@@ -7,8 +7,11 @@
 // query row i of an entry sees keys 0 .. Tk - Tq + i.
 //
 // One CTA = one entry, one kv head and two query tiles of 128 rows (256/G query positions x
-// the G q heads of the kv head: GQA folded into M, so each key tile is dequantized once for
-// 256 rows).  Keys advance in tiles of 128.  Per key tile j and query tile i:
+// the G q heads of the kv head: GQA folded into M).  CTAs come in clusters of two covering
+// adjacent row blocks of the same (entry, kv head): each CTA of the pair copies and
+// dequantizes one 64-key half of every key tile and writes the f16 result into both CTAs'
+// shared memory (distributed shared memory), so each pool byte is copied and dequantized once
+// for 512 rows.  Keys advance in tiles of 128.  Per key tile j and query tile i:
 //   S_i = Q_i K_j^T      tcgen05.mma kind::f16, A = Q_i and B = K_j from shared memory
 //                        (K-major, 128-byte swizzle), M = 128 rows, N = 128 keys, f32 in TMEM;
 //   P_i = softmax part   written back into TMEM as f16 over the upper half of S_i's columns;
@@ -20,11 +23,13 @@
 //   * warps 0-3 / 4-7, softmax of query tile 0 / 1: thread r owns row r (TMEM lane r):
 //     row max, lazy base-2 rescale of the running max (O_i rescaled in TMEM by the same
 //     thread, only when the max grew by more than 2^8), exponentials, f16 P into TMEM;
-//   * warps 8-11, dequant: int8 pool tiles staged by bulk copies -> f16 K [key][dim] and
-//     V^T [dim][key] in the swizzled layouts the MMA descriptors describe;
-//   * warp 12, control (one lane): every MMA and commit, polling its barriers;
-//   * warp 13, copies (one lane): bulk copies of 64-key halves of the pool (K+V int8 and
-//     scales, one 4352-byte block per 16-token tile), page ids read one half ahead.
+//   * warps 8-11, dequant: this CTA's half of each key tile, int8 pool tiles staged by bulk
+//     copies -> f16 K [key][dim] and V^T [dim][key] in the swizzled layouts the MMA descriptors
+//     describe, stored locally and into the peer CTA;
+//   * warp 12, control (one lane): every MMA and commit, polling its barriers, and the report
+//     to the peer that a K/V^T stage is no longer read here;
+//   * warp 13, copies (one lane): bulk copies of this CTA's 64-key half of each key tile (K+V
+//     int8 and scales, one 4352-byte block per 16-token tile), page ids read one half ahead.
 // At the end thread r reads row r of O_i and writes out[row] / l[row].
 #include <cstdint>
 #include <cstdlib>
@@ -178,6 +183,24 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void sts128_cluster(uint32_t caddr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(caddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+// Arrival on an mbarrier of another CTA of the cluster, ordering this thread's earlier writes.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void sts128(uint32_t saddr, uint4 v) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(saddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
@@ -271,9 +294,10 @@ __device__ __forceinline__ float exp_store64(const float (&v)[64], int k0, int l
 }
 
 struct Bars {
-    uint64_t raw_full[2], raw_free[2];  // staged 64-key halves of the pool
-    uint64_t kv_full[2];                // K and V^T stage of a key tile written
-    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its last MMA
+    uint64_t raw_full[2], raw_free[2];  // staged 64-key halves of the pool (this CTA's halves)
+    uint64_t kv_full[2];                // K and V^T stage of a key tile written (both halves)
+    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its last MMA here
+    uint64_t peer_free[2];              // ... and by its last MMA in the peer CTA
     uint64_t s_full[2], p_full[2];      // per query tile
     uint64_t o_done[2];                 // per query tile: last PV complete
     uint64_t drain;
@@ -294,7 +318,7 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, int use) {  // non-bloc
 // Diagnostic tag of a wait that gave up: role (1 control, 2 dequant, 3 softmax) in bits 14-15,
 // barrier in bits 10-13, the awaited completion (low 10 bits) in bits 0-9.
 enum : uint32_t { kBarRawFull, kBarRawFree, kBarKvFull, kBarKFree, kBarVFree, kBarSFull, kBarPFull, kBarODone,
-                  kBarDrain, kBarIdle };
+                  kBarDrain, kBarIdle, kBarPeerFree };
 __host__ __device__ constexpr uint32_t wait_tag(uint32_t role, uint32_t bar, int use) {
     return (role << 14) | (bar << 10) | ((uint32_t)use & 1023u);
 }
@@ -326,7 +350,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int*
     return false;
 }
 
-__global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = smem_raw;
     const uint32_t sbase = smem_u32(smem_raw);
@@ -355,16 +379,19 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
         return;
     }
     const int qrow0 = (int)p.cu_q[b];
-    const int pos0 = blockIdx.x * ppb;
-    if (pos0 >= Tq) return;
-    const int npos = min(ppb, Tq - pos0);
+    const int rank = (int)(blockIdx.x & 1);  // rank in the cluster pair (x-adjacent CTAs)
+    const uint32_t peer = (uint32_t)(rank ^ 1);
+    const int pos0 = blockIdx.x * ppb, pair_pos0 = (blockIdx.x & ~1u) * ppb;
+    if (pair_pos0 >= Tq) return;  // both CTAs of the pair: no rows
+    const int npos = max(0, min(ppb, Tq - pos0));  // a pair's second CTA may have none
     const int rows = npos * p.G;
-    const bool act1 = rows > kPfRows;  // query tile 1 holds rows
+    const bool act1 = rows > kPfRows;  // query tile 1 holds rows (tile 0 always runs)
     const int kv0 = Tk - Tq;           // keys before the chunk
-    const int kv_hi = max(0, min(Tk, kv0 + pos0 + npos));
+    // both CTAs stream the key tiles of the pair's last row
+    const int kv_hi = max(0, min(Tk, kv0 + pair_pos0 + min(2 * ppb, Tq - pair_pos0)));
     const int n_kt = (kv_hi + kPfKeys - 1) / kPfKeys;
     const int pt_total = (Tk + 15) / 16;
-    const int pt_need = (kv_hi + 15) / 16;  // pool tiles this CTA reads
+    const int pt_need = (kv_hi + 15) / 16;  // pool tiles the pair reads
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
     const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
     const long long page_stride = p.phb * p.H;
@@ -377,6 +404,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
             mbar_init(&bars->kv_full[i], 8);
             mbar_init(&bars->k_free[i], 1);
             mbar_init(&bars->v_free[i], 1);
+            mbar_init(&bars->peer_free[i], 1);
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->p_full[i], 4);
             mbar_init(&bars->o_done[i], 1);
@@ -412,6 +440,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
     tc_fence_before();
     const bool pages_ok = __syncthreads_or(bad) == 0;
     tc_fence_after();
+    cluster_sync();  // the peer's barriers are initialised before any remote arrival
     const uint32_t tmem = *tmem_slot;
 
     if (warp == kCtlWarp) {
@@ -422,10 +451,20 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
             // single-buffered: QK_i(j) follows PV_i(j-1), which read P_i from the same columns
             // (tcgen05.mma operations of one thread execute in issue order).
             int qk[2] = {0, 0}, pv[2] = {0, 0};
+            int sig = 0;  // next key tile whose K/V^T stage release is reported to the peer
+            const uint32_t peer_free0 = peer_addr(smem_u32(&bars->peer_free[0]), peer);
+            const uint32_t peer_free1 = peer_addr(smem_u32(&bars->peer_free[1]), peer);
             uint32_t idle = 0;
             uint64_t idle_t0 = 0;
-            while ((pv[0] < n_kt || (act1 && pv[1] < n_kt)) && !*s_abort) {
+            while ((pv[0] < n_kt || (act1 && pv[1] < n_kt) || sig + 2 < n_kt) && !*s_abort) {
                 bool prog = false;
+                // the peer rewrites stage (sig & 1) with tile sig + 2 only after this report
+                if (sig + 2 < n_kt && sig < pv[0] && (!act1 || sig < pv[1]) &&
+                    mbar_test(&bars->k_free[sig & 1], sig >> 1) && mbar_test(&bars->v_free[sig & 1], sig >> 1)) {
+                    mbar_arrive_cluster((sig & 1) ? peer_free1 : peer_free0);
+                    ++sig;
+                    prog = true;
+                }
 #pragma unroll
                 for (int i = 0; i < kPfTiles; ++i) {
                     if (i == 1 && !act1) break;
@@ -477,7 +516,6 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
     } else if (warp == kCopyWarp) {
         // ================= copies: pool tiles of 64-key halves into the raw ring =================
         if (lane == 0) {
-            const int n_half = 2 * n_kt;
             uint32_t page[4];
             auto fetch_pages = [&](int hf) {  // page ids of pool tiles 4hf .. 4hf+3 (n_pages: skip)
 #pragma unroll
@@ -486,15 +524,15 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                     page[j] = pt < pt_need ? __ldg(btrow + pt / p.tpp) : (uint32_t)p.n_pages;
                 }
             };
-            if (n_half > 0) fetch_pages(0);
-            for (int hf = 0; hf < n_half; ++hf) {
-                const int slot = hf & 1;
+            if (n_kt > 0) fetch_pages(rank);
+            for (int kt = 0; kt < n_kt; ++kt) {
+                const int hf = 2 * kt + rank, slot = kt & 1;  // this CTA's half of key tile kt
                 uint32_t cur[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) cur[j] = page[j];
-                if (hf + 1 < n_half) fetch_pages(hf + 1);  // in flight while this half waits
-                if (hf >= 2 &&
-                    !wait_phase(&bars->raw_free[slot], (hf >> 1) - 1, s_abort, p.status, wait_tag(1, kBarRawFree, hf)))
+                if (kt + 1 < n_kt) fetch_pages(hf + 2);  // in flight while this half waits
+                if (kt >= 2 &&
+                    !wait_phase(&bars->raw_free[slot], (kt >> 1) - 1, s_abort, p.status, wait_tag(1, kBarRawFree, kt)))
                     break;
                 uint8_t* dst = base + kSmRaw + slot * kRawHalf;
                 uint32_t bytes = 0;
@@ -526,17 +564,22 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
         const int kg = (k8 < 4) ? qw : (qw ^ 5), ktig = k8 & 3;
         // V: lane -> (dim bits 4, 3, 0; staged tile); warp and step give dim bits 5-6, 1-2
         const int vm1 = lane >> 4, vdh = (lane >> 3) & 1, vjt = (lane >> 1) & 3, vg1 = lane & 1;
-        const int n_half = 2 * n_kt;
-        for (int hf = 0; hf < n_half; ++hf) {
-            const int j = hf >> 1, e = hf & 1, slot = hf & 1;
-            (void)wait_phase(&bars->raw_full[slot], hf >> 1, s_abort, p.status, wait_tag(2, kBarRawFull, hf >> 1));
-            // stage j&1 was last read by QK(j-2) (K) and PV(j-2) (V^T)
-            if (e == 0 && j >= 2) {
+        const uint32_t peer_sbase = peer_addr(sbase, peer);
+        const uint32_t peer_kv_full0 = peer_addr(smem_u32(&bars->kv_full[0]), peer);
+        const uint32_t peer_kv_full1 = peer_addr(smem_u32(&bars->kv_full[1]), peer);
+        for (int j = 0; j < n_kt; ++j) {
+            const int e = rank, slot = j & 1;  // half e of key tile j
+            (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, wait_tag(2, kBarRawFull, j));
+            // stage j&1 was last read by QK(j-2) (K) and PV(j-2) (V^T), here and in the peer
+            if (j >= 2) {
                 (void)wait_phase(&bars->k_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarKFree, j));
                 (void)wait_phase(&bars->v_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarVFree, j));
+                (void)wait_phase(&bars->peer_free[j & 1], (j >> 1) - 1, s_abort, p.status,
+                                 wait_tag(2, kBarPeerFree, j));
             }
             const uint8_t* raw = base + kSmRaw + slot * kRawHalf;
             const uint32_t kdst = sbase + kSmK + (j & 1) * 32768, vdst = sbase + kSmVt + (j & 1) * 32768 + e * 16384;
+            const uint32_t pkdst = peer_sbase + (kdst - sbase), pvdst = peer_sbase + (vdst - sbase);
 #pragma unroll
             for (int jt = 0; jt < 4; ++jt) {
                 // K: tokens kg, kg+8 x dims 32dw + 8ktig .. +7 of pool tile jt
@@ -554,8 +597,11 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                     o1 = make_uint4(dq2(z0, 0, d1), dq2(z0, 1, d1), dq2(z1, 0, d1), dq2(z1, 1, d1));
                 }
                 const int key = e * 64 + jt * 16 + kg, c = dw * 4 + ktig;  // chunk c = dims 8c .. 8c+7
-                sts128(kdst + sw128_off(key, c, kPfKeys), o0);
-                sts128(kdst + sw128_off(key + 8, c, kPfKeys), o1);
+                const uint32_t k0off = sw128_off(key, c, kPfKeys), k1off = sw128_off(key + 8, c, kPfKeys);
+                sts128(kdst + k0off, o0);
+                sts128(kdst + k1off, o1);
+                sts128_cluster(pkdst + k0off, o0);
+                sts128_cluster(pkdst + k1off, o1);
             }
             // V: the thread's four dims share one scale group (dims 32dw .. 32dw+31) of tile vjt
             const uint8_t* TV = raw + vjt * kRawPitch;
@@ -590,13 +636,18 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
                     lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
                     hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
                 }
-                sts128(vdst + sw128_off(d, 2 * vjt, kPfD), lo);
-                sts128(vdst + sw128_off(d, 2 * vjt + 1, kPfD), hi);
+                const uint32_t v0off = sw128_off(d, 2 * vjt, kPfD), v1off = sw128_off(d, 2 * vjt + 1, kPfD);
+                sts128(vdst + v0off, lo);
+                sts128(vdst + v1off, hi);
+                sts128_cluster(pvdst + v0off, lo);
+                sts128_cluster(pvdst + v1off, hi);
             }
             fence_proxy_async_smem();
+            asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&bars->kv_full[j & 1]);
+                mbar_arrive_cluster((j & 1) ? peer_kv_full1 : peer_kv_full0);
                 mbar_arrive(&bars->raw_free[slot]);
             }
         }
@@ -703,6 +754,7 @@ __global__ void __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillPa
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols) : "memory");
     }
+    cluster_sync();  // no CTA leaves while its peer may still address its shared memory
 }
 
 }  // namespace
@@ -744,7 +796,8 @@ int launch_prefill_tc(const AttnArgs& a) {
         if (dev >= 0 && dev < 64) attr_dev[dev] = 1;
     }
     const int ppb = kPfTiles * kPfRows / p.G;
-    const dim3 grid((a.max_seqlen_q + ppb - 1) / ppb, d.n_kv_heads, a.batch);
+    const long long blocks = (a.max_seqlen_q + ppb - 1) / ppb;
+    const dim3 grid((unsigned)((blocks + 1) / 2 * 2), d.n_kv_heads, a.batch);  // clusters of 2 along x
     if (grid.x > 0x7fffffffu) return fail(YF_E_UNSUPPORTED, "too many query rows");
     prefill_tc_kernel<<<grid, kPfBlock, kSmAlloc, a.stream>>>(p);
     const cudaError_t e = cudaGetLastError();
