@@ -127,6 +127,15 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+// Completion of this thread's MMAs arrives on `bar` in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    const uint16_t both = 3;
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(both)
+        : "memory");
+}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -189,13 +198,13 @@ __device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ void sts128_cluster(uint32_t caddr, uint4 v) {
-    asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(caddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+// Bulk copy of this CTA's shared memory into another CTA's, completing bytes on that CTA's
+// mbarrier (cluster addresses for dst and bar; 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_s2peer(uint32_t dst_c, uint32_t src, uint32_t bytes, uint32_t bar_c) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst_c),
+                 "r"(src), "r"(bytes), "r"(bar_c)
                  : "memory");
-}
-// Arrival on an mbarrier of another CTA of the cluster, ordering this thread's earlier writes.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -295,9 +304,8 @@ __device__ __forceinline__ float exp_store64(const float (&v)[64], int k0, int l
 
 struct Bars {
     uint64_t raw_full[2], raw_free[2];  // staged 64-key halves of the pool (this CTA's halves)
-    uint64_t kv_full[2];                // K and V^T stage of a key tile written (both halves)
-    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its last MMA here
-    uint64_t peer_free[2];              // ... and by its last MMA in the peer CTA
+    uint64_t kv_full[2];                // K and V^T stage of a key tile written (own half + the peer's copy)
+    uint64_t stage_free[2];             // K/V^T stage read by its last MMA, here and in the peer
     uint64_t s_full[2], p_full[2];      // per query tile
     uint64_t o_done[2];                 // per query tile: last PV complete
     uint64_t drain;
@@ -317,8 +325,8 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, int use) {  // non-bloc
 
 // Diagnostic tag of a wait that gave up: role (1 control, 2 dequant, 3 softmax) in bits 14-15,
 // barrier in bits 10-13, the awaited completion (low 10 bits) in bits 0-9.
-enum : uint32_t { kBarRawFull, kBarRawFree, kBarKvFull, kBarKFree, kBarVFree, kBarSFull, kBarPFull, kBarODone,
-                  kBarDrain, kBarIdle, kBarPeerFree };
+enum : uint32_t { kBarRawFull, kBarRawFree, kBarKvFull, kBarStageFree, kBarSFull, kBarPFull, kBarODone,
+                  kBarDrain, kBarIdle };
 __host__ __device__ constexpr uint32_t wait_tag(uint32_t role, uint32_t bar, int use) {
     return (role << 14) | (bar << 10) | ((uint32_t)use & 1023u);
 }
@@ -401,10 +409,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_free[i], 4);
-            mbar_init(&bars->kv_full[i], 8);
-            mbar_init(&bars->k_free[i], 1);
-            mbar_init(&bars->v_free[i], 1);
-            mbar_init(&bars->peer_free[i], 1);
+            mbar_init(&bars->kv_full[i], 4);     // the dequant warps; the peer's half comes as bytes
+            mbar_init(&bars->stage_free[i], 2);  // this CTA's and the peer's last PV of the tile
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->p_full[i], 4);
             mbar_init(&bars->o_done[i], 1);
@@ -451,20 +457,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
             // single-buffered: QK_i(j) follows PV_i(j-1), which read P_i from the same columns
             // (tcgen05.mma operations of one thread execute in issue order).
             int qk[2] = {0, 0}, pv[2] = {0, 0};
-            int sig = 0;  // next key tile whose K/V^T stage release is reported to the peer
-            const uint32_t peer_free0 = peer_addr(smem_u32(&bars->peer_free[0]), peer);
-            const uint32_t peer_free1 = peer_addr(smem_u32(&bars->peer_free[1]), peer);
             uint32_t idle = 0;
             uint64_t idle_t0 = 0;
-            while ((pv[0] < n_kt || (act1 && pv[1] < n_kt) || sig + 2 < n_kt) && !*s_abort) {
+            while ((pv[0] < n_kt || (act1 && pv[1] < n_kt)) && !*s_abort) {
                 bool prog = false;
-                // the peer rewrites stage (sig & 1) with tile sig + 2 only after this report
-                if (sig + 2 < n_kt && sig < pv[0] && (!act1 || sig < pv[1]) &&
-                    mbar_test(&bars->k_free[sig & 1], sig >> 1) && mbar_test(&bars->v_free[sig & 1], sig >> 1)) {
-                    mbar_arrive_cluster((sig & 1) ? peer_free1 : peer_free0);
-                    ++sig;
-                    prog = true;
-                }
 #pragma unroll
                 for (int i = 0; i < kPfTiles; ++i) {
                     if (i == 1 && !act1) break;
@@ -479,7 +475,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                             umma_ts(tmem + i * 128, tS + 64 + ks * 8, bd, IDESC, (j > 0 || ks > 0) ? 1u : 0u);
                         }
                         pv[i] = j + 1;
-                        if (!act1 || pv[1 - i] > j) umma_commit(&bars->v_free[j & 1]);  // last reader of V_j
+                        // the tile's last MMA here: its stage may be rewritten once the peer's is done too
+                        if (!act1 || pv[1 - i] > j) umma_commit_pair(&bars->stage_free[j & 1]);
                         if (j == n_kt - 1) umma_commit(&bars->o_done[i]);
                         prog = true;
                     }
@@ -496,7 +493,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                         }
                         umma_commit(&bars->s_full[i]);
                         qk[i] = j + 1;
-                        if (!act1 || qk[1 - i] > j) umma_commit(&bars->k_free[j & 1]);  // last reader of K_j
                         prog = true;
                     }
                 }
@@ -567,19 +563,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
         const uint32_t peer_sbase = peer_addr(sbase, peer);
         const uint32_t peer_kv_full0 = peer_addr(smem_u32(&bars->kv_full[0]), peer);
         const uint32_t peer_kv_full1 = peer_addr(smem_u32(&bars->kv_full[1]), peer);
+        constexpr uint32_t kHalfBytes = 2 * 8192 + 16384;  // K rows of 64 keys (2 col blocks) + V^T block
         for (int j = 0; j < n_kt; ++j) {
             const int e = rank, slot = j & 1;  // half e of key tile j
             (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, wait_tag(2, kBarRawFull, j));
             // stage j&1 was last read by QK(j-2) (K) and PV(j-2) (V^T), here and in the peer
-            if (j >= 2) {
-                (void)wait_phase(&bars->k_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarKFree, j));
-                (void)wait_phase(&bars->v_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarVFree, j));
-                (void)wait_phase(&bars->peer_free[j & 1], (j >> 1) - 1, s_abort, p.status,
-                                 wait_tag(2, kBarPeerFree, j));
-            }
+            if (j >= 2)
+                (void)wait_phase(&bars->stage_free[j & 1], (j >> 1) - 1, s_abort, p.status,
+                                 wait_tag(2, kBarStageFree, j));
             const uint8_t* raw = base + kSmRaw + slot * kRawHalf;
             const uint32_t kdst = sbase + kSmK + (j & 1) * 32768, vdst = sbase + kSmVt + (j & 1) * 32768 + e * 16384;
-            const uint32_t pkdst = peer_sbase + (kdst - sbase), pvdst = peer_sbase + (vdst - sbase);
 #pragma unroll
             for (int jt = 0; jt < 4; ++jt) {
                 // K: tokens kg, kg+8 x dims 32dw + 8ktig .. +7 of pool tile jt
@@ -597,11 +590,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                     o1 = make_uint4(dq2(z0, 0, d1), dq2(z0, 1, d1), dq2(z1, 0, d1), dq2(z1, 1, d1));
                 }
                 const int key = e * 64 + jt * 16 + kg, c = dw * 4 + ktig;  // chunk c = dims 8c .. 8c+7
-                const uint32_t k0off = sw128_off(key, c, kPfKeys), k1off = sw128_off(key + 8, c, kPfKeys);
-                sts128(kdst + k0off, o0);
-                sts128(kdst + k1off, o1);
-                sts128_cluster(pkdst + k0off, o0);
-                sts128_cluster(pkdst + k1off, o1);
+                sts128(kdst + sw128_off(key, c, kPfKeys), o0);
+                sts128(kdst + sw128_off(key + 8, c, kPfKeys), o1);
             }
             // V: the thread's four dims share one scale group (dims 32dw .. 32dw+31) of tile vjt
             const uint8_t* TV = raw + vjt * kRawPitch;
@@ -636,18 +626,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                     lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
                     hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
                 }
-                const uint32_t v0off = sw128_off(d, 2 * vjt, kPfD), v1off = sw128_off(d, 2 * vjt + 1, kPfD);
-                sts128(vdst + v0off, lo);
-                sts128(vdst + v1off, hi);
-                sts128_cluster(pvdst + v0off, lo);
-                sts128_cluster(pvdst + v1off, hi);
+                sts128(vdst + sw128_off(d, 2 * vjt, kPfD), lo);
+                sts128(vdst + sw128_off(d, 2 * vjt + 1, kPfD), hi);
             }
             fence_proxy_async_smem();
-            asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
+            // all four dequant warps' writes of this half precede its copy into the peer
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (t == 0) {
+                // this half (K rows 64e..64e+63 of both column blocks, V^T column block e) into the
+                // peer's stage; its bytes complete the peer's kv_full, whose expected count this
+                // CTA's arrival below mirrors for the peer's copy into this CTA
+                const uint32_t pbar = (j & 1) ? peer_kv_full1 : peer_kv_full0;
+                const uint32_t k0 = kdst + e * 64 * 128, k1 = kdst + 16384 + e * 64 * 128;
+                bulk_s2peer(peer_sbase + (k0 - sbase), k0, 8192, pbar);
+                bulk_s2peer(peer_sbase + (k1 - sbase), k1, 8192, pbar);
+                bulk_s2peer(peer_sbase + (vdst - sbase), vdst, 16384, pbar);
+                mbar_arrive_expect_tx(&bars->kv_full[j & 1], kHalfBytes);
+                mbar_arrive(&bars->raw_free[slot]);
+            } else if (lane == 0) {
                 mbar_arrive(&bars->kv_full[j & 1]);
-                mbar_arrive_cluster((j & 1) ? peer_kv_full1 : peer_kv_full0);
                 mbar_arrive(&bars->raw_free[slot]);
             }
         }
