@@ -304,8 +304,8 @@ __device__ __forceinline__ float exp_store64(const float (&v)[64], int k0, int l
 
 struct Bars {
     uint64_t raw_full[2], raw_free[2];  // staged 64-key halves of the pool (this CTA's halves)
-    uint64_t kv_full[2];                // K and V^T stage of a key tile written (own half + the peer's copy)
-    uint64_t stage_free[2];             // K/V^T stage read by its last MMA, here and in the peer
+    uint64_t k_full[2], v_full[2];      // K / V^T stage of a key tile written (own half + the peer's copy)
+    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its last MMA, here and in the peer
     uint64_t s_full[2], p_full[2];      // per query tile
     uint64_t o_done[2];                 // per query tile: last PV complete
     uint64_t drain;
@@ -325,8 +325,8 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, int use) {  // non-bloc
 
 // Diagnostic tag of a wait that gave up: role (1 control, 2 dequant, 3 softmax) in bits 14-15,
 // barrier in bits 10-13, the awaited completion (low 10 bits) in bits 0-9.
-enum : uint32_t { kBarRawFull, kBarRawFree, kBarKvFull, kBarStageFree, kBarSFull, kBarPFull, kBarODone,
-                  kBarDrain, kBarIdle };
+enum : uint32_t { kBarRawFull, kBarRawFree, kBarKFull, kBarVFull, kBarKFree, kBarVFree, kBarSFull, kBarPFull,
+                  kBarODone, kBarDrain, kBarIdle };
 __host__ __device__ constexpr uint32_t wait_tag(uint32_t role, uint32_t bar, int use) {
     return (role << 14) | (bar << 10) | ((uint32_t)use & 1023u);
 }
@@ -409,8 +409,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_free[i], 4);
-            mbar_init(&bars->kv_full[i], 4);     // the dequant warps; the peer's half comes as bytes
-            mbar_init(&bars->stage_free[i], 2);  // this CTA's and the peer's last PV of the tile
+            mbar_init(&bars->k_full[i], 4);  // the dequant warps; the peer's half comes as bytes
+            mbar_init(&bars->v_full[i], 4);
+            mbar_init(&bars->k_free[i], 2);  // this CTA's and the peer's last QK / PV of the tile
+            mbar_init(&bars->v_free[i], 2);
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->p_full[i], 4);
             mbar_init(&bars->o_done[i], 1);
@@ -465,7 +467,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                 for (int i = 0; i < kPfTiles; ++i) {
                     if (i == 1 && !act1) break;
                     const uint32_t tS = tmem + 256 + i * 128;
-                    if (pv[i] < qk[i] && mbar_test(&bars->p_full[i], pv[i])) {
+                    if (pv[i] < qk[i] && mbar_test(&bars->p_full[i], pv[i]) &&
+                        mbar_test(&bars->v_full[pv[i] & 1], pv[i] >> 1)) {
                         const int j = pv[i];
                         tc_fence_after();
 #pragma unroll
@@ -475,12 +478,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                             umma_ts(tmem + i * 128, tS + 64 + ks * 8, bd, IDESC, (j > 0 || ks > 0) ? 1u : 0u);
                         }
                         pv[i] = j + 1;
-                        // the tile's last MMA here: its stage may be rewritten once the peer's is done too
-                        if (!act1 || pv[1 - i] > j) umma_commit_pair(&bars->stage_free[j & 1]);
+                        // the tile's last PV here: V^T may be rewritten once the peer's is done too
+                        if (!act1 || pv[1 - i] > j) umma_commit_pair(&bars->v_free[j & 1]);
                         if (j == n_kt - 1) umma_commit(&bars->o_done[i]);
                         prog = true;
                     }
-                    if (qk[i] < n_kt && qk[i] == pv[i] && mbar_test(&bars->kv_full[qk[i] & 1], qk[i] >> 1)) {
+                    if (qk[i] < n_kt && qk[i] == pv[i] && mbar_test(&bars->k_full[qk[i] & 1], qk[i] >> 1)) {
                         const int j = qk[i];
                         tc_fence_after();
 #pragma unroll
@@ -493,6 +496,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                         }
                         umma_commit(&bars->s_full[i]);
                         qk[i] = j + 1;
+                        if (!act1 || qk[1 - i] > j) umma_commit_pair(&bars->k_free[j & 1]);  // last QK here
                         prog = true;
                     }
                 }
@@ -561,16 +565,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
         // V: lane -> (dim bits 4, 3, 0; staged tile); warp and step give dim bits 5-6, 1-2
         const int vm1 = lane >> 4, vdh = (lane >> 3) & 1, vjt = (lane >> 1) & 3, vg1 = lane & 1;
         const uint32_t peer_sbase = peer_addr(sbase, peer);
-        const uint32_t peer_kv_full0 = peer_addr(smem_u32(&bars->kv_full[0]), peer);
-        const uint32_t peer_kv_full1 = peer_addr(smem_u32(&bars->kv_full[1]), peer);
-        constexpr uint32_t kHalfBytes = 2 * 8192 + 16384;  // K rows of 64 keys (2 col blocks) + V^T block
+        const uint32_t peer_k_full0 = peer_addr(smem_u32(&bars->k_full[0]), peer);
+        const uint32_t peer_k_full1 = peer_addr(smem_u32(&bars->k_full[1]), peer);
+        const uint32_t peer_v_full0 = peer_addr(smem_u32(&bars->v_full[0]), peer);
+        const uint32_t peer_v_full1 = peer_addr(smem_u32(&bars->v_full[1]), peer);
         for (int j = 0; j < n_kt; ++j) {
             const int e = rank, slot = j & 1;  // half e of key tile j
             (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, wait_tag(2, kBarRawFull, j));
             // stage j&1 was last read by QK(j-2) (K) and PV(j-2) (V^T), here and in the peer
+            // K stage j&1 was last read by QK(j-2) here and in the peer
             if (j >= 2)
-                (void)wait_phase(&bars->stage_free[j & 1], (j >> 1) - 1, s_abort, p.status,
-                                 wait_tag(2, kBarStageFree, j));
+                (void)wait_phase(&bars->k_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarKFree, j));
             const uint8_t* raw = base + kSmRaw + slot * kRawHalf;
             const uint32_t kdst = sbase + kSmK + (j & 1) * 32768, vdst = sbase + kSmVt + (j & 1) * 32768 + e * 16384;
 #pragma unroll
@@ -593,6 +598,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                 sts128(kdst + sw128_off(key, c, kPfKeys), o0);
                 sts128(kdst + sw128_off(key + 8, c, kPfKeys), o1);
             }
+            fence_proxy_async_smem();
+            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' K rows precede the copy
+            if (t == 0) {
+                // this half's K rows (64e .. 64e+63 of both column blocks) into the peer; its bytes
+                // complete the peer's k_full, as the peer's do this CTA's (armed here)
+                const uint32_t k0 = kdst + e * 64 * 128, k1 = kdst + 16384 + e * 64 * 128;
+                const uint32_t pbar = (j & 1) ? peer_k_full1 : peer_k_full0;
+                bulk_s2peer(peer_sbase + (k0 - sbase), k0, 8192, pbar);
+                bulk_s2peer(peer_sbase + (k1 - sbase), k1, 8192, pbar);
+                mbar_arrive_expect_tx(&bars->k_full[j & 1], 16384);
+            } else if (lane == 0) {
+                mbar_arrive(&bars->k_full[j & 1]);
+            }
+            // V^T stage j&1 was last read by PV(j-2) here and in the peer
+            if (j >= 2)
+                (void)wait_phase(&bars->v_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarVFree, j));
             // V: the thread's four dims share one scale group (dims 32dw .. 32dw+31) of tile vjt
             const uint8_t* TV = raw + vjt * kRawPitch;
             const bool vvalid = s_valid[slot * 4 + vjt] != 0;
@@ -630,21 +651,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                 sts128(vdst + sw128_off(d, 2 * vjt + 1, kPfD), hi);
             }
             fence_proxy_async_smem();
-            // all four dequant warps' writes of this half precede its copy into the peer
-            asm volatile("bar.sync 2, 128;" ::: "memory");
+            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' V^T columns precede the copy
             if (t == 0) {
-                // this half (K rows 64e..64e+63 of both column blocks, V^T column block e) into the
-                // peer's stage; its bytes complete the peer's kv_full, whose expected count this
-                // CTA's arrival below mirrors for the peer's copy into this CTA
-                const uint32_t pbar = (j & 1) ? peer_kv_full1 : peer_kv_full0;
-                const uint32_t k0 = kdst + e * 64 * 128, k1 = kdst + 16384 + e * 64 * 128;
-                bulk_s2peer(peer_sbase + (k0 - sbase), k0, 8192, pbar);
-                bulk_s2peer(peer_sbase + (k1 - sbase), k1, 8192, pbar);
-                bulk_s2peer(peer_sbase + (vdst - sbase), vdst, 16384, pbar);
-                mbar_arrive_expect_tx(&bars->kv_full[j & 1], kHalfBytes);
+                bulk_s2peer(peer_sbase + (vdst - sbase), vdst, 16384, (j & 1) ? peer_v_full1 : peer_v_full0);
+                mbar_arrive_expect_tx(&bars->v_full[j & 1], 16384);
                 mbar_arrive(&bars->raw_free[slot]);
             } else if (lane == 0) {
-                mbar_arrive(&bars->kv_full[j & 1]);
+                mbar_arrive(&bars->v_full[j & 1]);
                 mbar_arrive(&bars->raw_free[slot]);
             }
         }
