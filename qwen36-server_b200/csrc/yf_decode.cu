@@ -155,8 +155,9 @@ struct WarpAcc {
 // and the key count each of the lane's softmax rows (2tig, 2tig+1 of each n-tile) sees.
 template <int D, int NT>
 __device__ __forceinline__ void load_unit_q(const SplitParams& p, const UnitGeom& u, int h, int lane,
-                                            uint4 (&qf)[NT][D / 32], int (&kvlen)[NT][2]) {
+                                            uint4 (&qf)[NT][D / 32], int (&kvlen)[NT][2], int& kv_min) {
     const int g = lane >> 2, tig = lane & 3;
+    int km = 0x7fffffff;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         const int r = u.row_begin + nt * 8 + g;
@@ -173,15 +174,17 @@ __device__ __forceinline__ void load_unit_q(const SplitParams& p, const UnitGeom
             const int rr = u.row_begin + nt * 8 + 2 * tig + col;
             const int kl = u.Tk - u.Tq + rr / p.G + 1;
             kvlen[nt][col] = rr < u.rows_total ? max(0, min(kl, u.Tk)) : 0;
+            if (rr < u.rows_total) km = min(km, kvlen[nt][col]);
         }
     }
+    kv_min = __reduce_min_sync(0xffffffffu, km);
 }
 
 // One 16-token tile (already in shared memory at T) into the warp's running softmax state.
 template <int D, int NB, int NT>
 __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 (&qf)[NT][D / 32],
-                                          const int (&kvlen)[NT][2], float scale_log2, WarpAcc<D, NT>& a,
-                                          int lane) {
+                                          const int (&kvlen)[NT][2], int kv_min, float scale_log2,
+                                          WarpAcc<D, NT>& a, int lane) {
     constexpr int KS_OFF = 16 * D;
     constexpr int V_OFF = 16 * D + 32 * NB;
     constexpr int VS_OFF = 32 * D + 32 * NB;
@@ -250,38 +253,49 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
             sacc[nt][3] = fmaf(ks1[s], acc[nt][3], sacc[nt][3]);
         }
     }
-    // ---- online softmax (base 2) on rows 2tig, 2tig+1 of each n-tile
+    // ---- online softmax (base 2) on rows 2tig, 2tig+1 of each n-tile.  The running max m of a
+    // row only moves when the tile's max exceeds it by kRescaleThresh, so the exact row max
+    // (shuffles across the row's 8 lanes) and the O rescale are needed only when some lane's
+    // own values cross that bound: one vote per tile decides.
     const int tok0 = kt * kTileTokens + g, tok1 = tok0 + 8;
-    uint32_t pb01[NT], pb23[NT];
+    float v[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        float pr[2][2];
-        float alpha[2];
-        bool need = false;
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int col = 0; col < 2; ++col) {
-            float v0 = sacc[nt][col] * scale_log2;
-            float v1 = sacc[nt][2 + col] * scale_log2;
-            if (tok0 >= kvlen[nt][col]) v0 = -INFINITY;
-            if (tok1 >= kvlen[nt][col]) v1 = -INFINITY;
-            float mx = fmaxf(v0, v1);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            alpha[col] = 1.f;
-            if (mx > a.m[nt][col] + kRescaleThresh) {
-                // a.m == -inf gives alpha = exp2(-inf) = 0: nothing accumulated yet
-                alpha[col] = fast_exp2(a.m[nt][col] - mx);
-                a.m[nt][col] = mx;
-                a.l[nt][col] *= alpha[col];
-                need = true;
+        for (int e = 0; e < 4; ++e) v[nt][e] = sacc[nt][e] * scale_log2;
+    if (kt * kTileTokens + kTileTokens > kv_min) {  // some row ends inside this tile (warp-uniform)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int col = 0; col < 2; ++col) {
+                if (tok0 >= kvlen[nt][col]) v[nt][col] = -INFINITY;
+                if (tok1 >= kvlen[nt][col]) v[nt][2 + col] = -INFINITY;
             }
-            const float muse = a.m[nt][col] == -INFINITY ? 0.f : a.m[nt][col];
-            pr[col][0] = fast_exp2(v0 - muse);
-            pr[col][1] = fast_exp2(v1 - muse);
-            a.l[nt][col] += pr[col][0] + pr[col][1];
-        }
-        if (__any_sync(0xffffffffu, need)) {
+    }
+    bool need = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int col = 0; col < 2; ++col)
+            need |= fmaxf(v[nt][col], v[nt][2 + col]) > a.m[nt][col] + kRescaleThresh;
+    if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            float alpha[2];
+#pragma unroll
+            for (int col = 0; col < 2; ++col) {
+                float mx = fmaxf(v[nt][col], v[nt][2 + col]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                alpha[col] = 1.f;
+                if (mx > a.m[nt][col] + kRescaleThresh) {
+                    // a.m == -inf gives alpha = exp2(-inf) = 0: nothing accumulated yet
+                    alpha[col] = fast_exp2(a.m[nt][col] - mx);
+                    a.m[nt][col] = mx;
+                    a.l[nt][col] *= alpha[col];
+                }
+            }
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
                 a.o[mt][nt][0] *= alpha[0];
@@ -289,6 +303,18 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
                 a.o[mt][nt][1] *= alpha[1];
                 a.o[mt][nt][3] *= alpha[1];
             }
+        }
+    }
+    uint32_t pb01[NT], pb23[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        float pr[2][2];
+#pragma unroll
+        for (int col = 0; col < 2; ++col) {
+            const float muse = a.m[nt][col] == -INFINITY ? 0.f : a.m[nt][col];
+            pr[col][0] = fast_exp2(v[nt][col] - muse);
+            pr[col][1] = fast_exp2(v[nt][2 + col] - muse);
+            a.l[nt][col] += pr[col][0] + pr[col][1];
         }
         // P^T B-fragment: lane (g, tig) needs P[tok 2tig, 2tig+8][row g] and
         // P[tok 2tig+1, 2tig+9][row g]; lane (g', tig') holds tokens g', g'+8 of
@@ -375,7 +401,8 @@ struct TileRing {
 template <int D, int NB, int NT, int TPP, int STAGES>
 __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * D + 64 * NB, STAGES>& ring, int b,
                                             int h, int t0, int n_seg, const uint4 (&qf)[NT][D / 32],
-                                            const int (&kvlen)[NT][2], WarpAcc<D, NT>& a, int warp, int lane) {
+                                            const int (&kvlen)[NT][2], int kv_min, WarpAcc<D, NT>& a, int warp,
+                                            int lane) {
     constexpr int TB = 32 * D + 64 * NB;
     const int my_n = n_seg > warp ? (n_seg - warp + kWarps - 1) / kWarps : 0;
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
@@ -404,7 +431,7 @@ __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * 
         }
         done = i + 1;
         if (ring.flag[slot])
-            tile_math<D, NB, NT>(ring.stage + slot * TB, tile_of(i), qf, kvlen, p.scale_log2, a, lane);
+            tile_math<D, NB, NT>(ring.stage + slot * TB, tile_of(i), qf, kvlen, kv_min, p.scale_log2, a, lane);
         __syncwarp();
         if (lane == 0 && i + STAGES < my_n) {
             ring.issue(i + STAGES, src_of(tile_of(i + STAGES), next_page), p.status);
@@ -870,7 +897,7 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
     ring.init(smem, stages, warp, lane);
     WarpAcc<D, NT> acc;
     uint4 qf[NT][D / 32];
-    int kvlen[NT][2];
+    int kvlen[NT][2], kv_min;
 
     long long x = s;
     while (x < e_end) {
@@ -893,9 +920,9 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
         const long long seg_e = e_end < Ue ? e_end : Ue;
         UnitGeom u;
         unit_geom<TPP, RPC>(p, b, 0, u, false);
-        load_unit_q<D, NT>(p, u, h, lane, qf, kvlen);
+        load_unit_q<D, NT>(p, u, h, lane, qf, kvlen, kv_min);
         acc.reset();
-        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, acc, warp, lane);
+        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, kv_min, acc, warp, lane);
         stash_warp<D, NT>(stages, acc, warp, lane);
         const bool whole = x == Us && seg_e == Ue;
         // partial slots: 2 per CTA; slot 1 when the CTA began inside an earlier unit
@@ -946,13 +973,13 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     const int tile_end = min(tile_begin + p.chunk_tiles, u.n_tiles);
 
     uint4 qf[NT][D / 32];
-    int kvlen[NT][2];
-    load_unit_q<D, NT>(p, u, h, lane, qf, kvlen);
+    int kvlen[NT][2], kv_min;
+    load_unit_q<D, NT>(p, u, h, lane, qf, kvlen, kv_min);
     TileRing<TB, STAGES> ring;
     ring.init(smem, stages, warp, lane);
     WarpAcc<D, NT> acc;
     acc.reset();
-    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, acc, warp, lane);
+    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, kv_min, acc, warp, lane);
     stash_warp<D, NT>(stages, acc, warp, lane);
 
     const bool direct = u.n_chunks == 1;
