@@ -43,6 +43,17 @@ namespace yf {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kHdrBytes = 256;  // mbarriers + per-stage page-valid flags
+// 16-row units (two n-tiles) are bound by instruction issue rather than by HBM: their QK feeds
+// K as the f16 values 1152 + k and starts each scale group's accumulator at -1152 x (the row's q
+// summed over the group), read per warp from shared memory: [group][tig][n-tile][4] floats.
+template <int NT>
+constexpr bool kbias_in_acc() { return NT == 2; }
+template <int NB, int NT>
+constexpr int hdr_bytes() { return kHdrBytes + (kbias_in_acc<NT>() ? kWarps * NB * 4 * NT * 16 : 0); }
+template <int NB, int NT>
+__device__ __forceinline__ float* kbias_area(uint8_t* smem, int warp) {
+    return reinterpret_cast<float*>(smem + kHdrBytes) + warp * NB * 4 * NT * 4;
+}
 // Lazy softmax rescale: the running max only moves when a tile's max exceeds it by
 // more than 8 (base 2), so most tiles skip the O rescale and p stays <= 256.
 constexpr float kRescaleThresh = 8.0f;
@@ -128,6 +139,25 @@ __device__ __forceinline__ void store_row4(const SplitParams& p, const UnitGeom&
     }
 }
 
+// mma.sync m16n8k16 f16 x f16 -> f32, D = A B + C (C may differ from D).
+__device__ __forceinline__ void mma_acc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_init(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1, const uint4 c) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(__uint_as_float(c.x)),
+          "f"(__uint_as_float(c.y)), "f"(__uint_as_float(c.z)), "f"(__uint_as_float(c.w)));
+}
+// bytes 0,1 / 2,3 of a biased word -> f16x2 of 1152 + x (the magic value before its subtraction)
+__device__ __forceinline__ uint32_t s8lo_to_h2_biased(uint32_t wb) { return __byte_perm(wb, 0x64646464u, 0x4140); }
+__device__ __forceinline__ uint32_t s8hi_to_h2_biased(uint32_t wb) { return __byte_perm(wb, 0x64646464u, 0x4342); }
+
 // ---- per-warp state and tile math ------------------------------------------------------
 
 template <int D, int NT>
@@ -153,9 +183,10 @@ struct WarpAcc {
 
 // Q^T fragments of a unit: lane holds Q[row nt*8+g][32cb + 8tig .. +7] for every chunk cb;
 // and the key count each of the lane's softmax rows (2tig, 2tig+1 of each n-tile) sees.
-template <int D, int NT>
+template <int D, int NT, int NBG>
 __device__ __forceinline__ void load_unit_q(const SplitParams& p, const UnitGeom& u, int h, int lane,
-                                            uint4 (&qf)[NT][D / 32], int (&kvlen)[NT][2], int& kv_min) {
+                                            uint4 (&qf)[NT][D / 32], int (&kvlen)[NT][2], int& kv_min,
+                                            float* cw) {
     const int g = lane >> 2, tig = lane & 3;
     int km = 0x7fffffff;
 #pragma unroll
@@ -178,13 +209,40 @@ __device__ __forceinline__ void load_unit_q(const SplitParams& p, const UnitGeom
         }
     }
     kv_min = __reduce_min_sync(0xffffffffu, km);
+    if constexpr (!kbias_in_acc<NT>()) return;
+    // lane (g, tig) reads {c(2tig), c(2tig+1), c(2tig), c(2tig+1)} per n-tile and group
+    __syncwarp();
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int s = 0; s < NBG; ++s) {
+            float sum = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < D / 32 / NBG; ++cc) {
+                const uint4 w = qf[nt][s * (D / 32 / NBG) + cc];
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ww[k]));
+                    sum += f.x + f.y;
+                }
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            if (tig == 0) {
+                float* c = cw + ((s * 4 + (g >> 1)) * NT + nt) * 4;
+                c[g & 1] = -1152.f * sum;
+                c[2 + (g & 1)] = -1152.f * sum;
+            }
+        }
+    __syncwarp();
 }
 
 // One 16-token tile (already in shared memory at T) into the warp's running softmax state.
 template <int D, int NB, int NT>
 __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 (&qf)[NT][D / 32],
-                                          const int (&kvlen)[NT][2], int kv_min, float scale_log2,
-                                          WarpAcc<D, NT>& a, int lane) {
+                                          const int (&kvlen)[NT][2], int kv_min, const float* cw,
+                                          float scale_log2, WarpAcc<D, NT>& a, int lane) {
     constexpr int KS_OFF = 16 * D;
     constexpr int V_OFF = 16 * D + 32 * NB;
     constexpr int VS_OFF = 32 * D + 32 * NB;
@@ -226,24 +284,51 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
 #pragma unroll
     for (int s = 0; s < NB; ++s) {
         float acc[NT][4];
+        if constexpr (kbias_in_acc<NT>()) {
+            uint4 cst[NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+            for (int nt = 0; nt < NT; ++nt) cst[nt] = lds128(cw + ((s * 4 + tig) * NT + nt) * 4);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+            for (int cc = 0; cc < CPG; ++cc) {
+                const int cb = s * CPG + cc;
+                const uint4 kw = lds128(T + cb * 512 + lane * 16);
+                const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+                uint32_t a0 = s8lo_to_h2_biased(x0), a1 = s8lo_to_h2_biased(z0), a2 = s8hi_to_h2_biased(x0),
+                         a3 = s8hi_to_h2_biased(z0);
 #pragma unroll
-        for (int cc = 0; cc < CPG; ++cc) {
-            const int cb = s * CPG + cc;
-            const uint4 kw = lds128(T + cb * 512 + lane * 16);
-            const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
-            uint32_t a0 = s8lo_to_h2(x0), a1 = s8lo_to_h2(z0), a2 = s8hi_to_h2(x0), a3 = s8hi_to_h2(z0);
+                for (int nt = 0; nt < NT; ++nt) {
+                    if (cc == 0)
+                        mma_init(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y, cst[nt]);
+                    else
+                        mma_acc(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y);
+                }
+                a0 = s8lo_to_h2_biased(x1);
+                a1 = s8lo_to_h2_biased(z1);
+                a2 = s8hi_to_h2_biased(x1);
+                a3 = s8hi_to_h2_biased(z1);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y);
-            a0 = s8lo_to_h2(x1);
-            a1 = s8lo_to_h2(z1);
-            a2 = s8hi_to_h2(x1);
-            a3 = s8hi_to_h2(z1);
+                for (int nt = 0; nt < NT; ++nt) mma_acc(acc[nt], a0, a1, a2, a3, qf[nt][cb].z, qf[nt][cb].w);
+            }
+        } else {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].z, qf[nt][cb].w);
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < CPG; ++cc) {
+                const int cb = s * CPG + cc;
+                const uint4 kw = lds128(T + cb * 512 + lane * 16);
+                const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+                uint32_t a0 = s8lo_to_h2(x0), a1 = s8lo_to_h2(z0), a2 = s8hi_to_h2(x0), a3 = s8hi_to_h2(z0);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y);
+                a0 = s8lo_to_h2(x1);
+                a1 = s8lo_to_h2(z1);
+                a2 = s8hi_to_h2(x1);
+                a3 = s8hi_to_h2(z1);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].z, qf[nt][cb].w);
+            }
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -401,8 +486,8 @@ struct TileRing {
 template <int D, int NB, int NT, int TPP, int STAGES>
 __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * D + 64 * NB, STAGES>& ring, int b,
                                             int h, int t0, int n_seg, const uint4 (&qf)[NT][D / 32],
-                                            const int (&kvlen)[NT][2], int kv_min, WarpAcc<D, NT>& a, int warp,
-                                            int lane) {
+                                            const int (&kvlen)[NT][2], int kv_min, const float* cw,
+                                            WarpAcc<D, NT>& a, int warp, int lane) {
     constexpr int TB = 32 * D + 64 * NB;
     const int my_n = n_seg > warp ? (n_seg - warp + kWarps - 1) / kWarps : 0;
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
@@ -431,7 +516,7 @@ __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * 
         }
         done = i + 1;
         if (ring.flag[slot])
-            tile_math<D, NB, NT>(ring.stage + slot * TB, tile_of(i), qf, kvlen, kv_min, p.scale_log2, a, lane);
+            tile_math<D, NB, NT>(ring.stage + slot * TB, tile_of(i), qf, kvlen, kv_min, cw, p.scale_log2, a, lane);
         __syncwarp();
         if (lane == 0 && i + STAGES < my_n) {
             ring.issue(i + STAGES, src_of(tile_of(i + STAGES), next_page), p.status);
@@ -843,7 +928,7 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
     static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
     static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* stages = smem + kHdrBytes;
+    uint8_t* stages = smem + hdr_bytes<NB, NT>();
     long long* sP = reinterpret_cast<long long*>(stages + kWarps * STAGES * TB);  // [B+1] tile prefix
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -920,9 +1005,9 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
         const long long seg_e = e_end < Ue ? e_end : Ue;
         UnitGeom u;
         unit_geom<TPP, RPC>(p, b, 0, u, false);
-        load_unit_q<D, NT>(p, u, h, lane, qf, kvlen, kv_min);
+        load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp));
         acc.reset();
-        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, kv_min, acc, warp, lane);
+        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp), acc, warp, lane);
         stash_warp<D, NT>(stages, acc, warp, lane);
         const bool whole = x == Us && seg_e == Ue;
         // partial slots: 2 per CTA; slot 1 when the CTA began inside an earlier unit
@@ -959,7 +1044,7 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
     static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* stages = smem + kHdrBytes;
+    uint8_t* stages = smem + hdr_bytes<NB, NT>();
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // chunk index is the slowest grid dimension: every unit's first chunks are dispatched first
@@ -974,12 +1059,12 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
 
     uint4 qf[NT][D / 32];
     int kvlen[NT][2], kv_min;
-    load_unit_q<D, NT>(p, u, h, lane, qf, kvlen, kv_min);
+    load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp));
     TileRing<TB, STAGES> ring;
     ring.init(smem, stages, warp, lane);
     WarpAcc<D, NT> acc;
     acc.reset();
-    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, kv_min, acc, warp, lane);
+    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp), acc, warp, lane);
     stash_warp<D, NT>(stages, acc, warp, lane);
 
     const bool direct = u.n_chunks == 1;
@@ -1023,7 +1108,7 @@ static int raise_smem(K kern, int smem, int dev, int* set_to) {
 template <int D, int NB, int NT, int TPP, int STAGES>
 static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
     constexpr int TB = 32 * D + 64 * NB;
-    constexpr int SMEM = kHdrBytes + kWarps * STAGES * TB;
+    constexpr int SMEM = hdr_bytes<NB, NT>() + kWarps * STAGES * TB;
     const int dev = a.pool->desc.device;
     cudaError_t e;
     if (plan.persistent) {
