@@ -32,6 +32,8 @@
  *    Q8_0, or head_dim = the engine's own one-scale-per-row int8 pool) is
  *    stored as int8 q and one f16 scale d, value = q * d.  Quantization is
  *    GGML's Q8_0 rule: d = amax/127, q = roundf(x * (1/d)), d stored as f16.
+ *    Each q is held as the excess-128 byte q + 128 (its top bit flipped), the
+ *    form the kernels turn into f16 with one byte permute.
  *  - Within a layer plane, page p / kv head h is one contiguous block of
  *    page_size/16 "tiles" of 16 tokens.  A tile is
  *        [K int8 16*D][K scales f16 16*(D/G)][V int8 16*D][V scales f16 16*(D/G)]
@@ -103,7 +105,7 @@ YF_API int yf_abi_version(void);
 /* Bytes of one (page, kv head) block and of the whole pool. */
 YF_API size_t yf_pool_page_head_bytes(const yf_pool_desc* desc);
 YF_API size_t yf_pool_bytes(const yf_pool_desc* desc);
-/* Byte offset inside a 16-token tile of the int8 value of (token t in 0..15,
+/* Byte offset inside a 16-token tile of the value byte (q + 128) of (token t in 0..15,
  * dim d) for K (is_v=0) or V (is_v=1); the f16 scale offset of (t, group) is
  * returned by yf_pool_scale_offset.  Pure functions of the format. */
 YF_API int64_t yf_pool_tile_offset(const yf_pool_desc* desc, int is_v, int t, int d);

@@ -193,6 +193,16 @@ def np_quantize_q8(x: np.ndarray, group: int):
     return q.reshape(shp), d.astype(np.float16).reshape(shp[:-1] + (D // group,))
 
 
+def excess128(q: np.ndarray) -> np.ndarray:
+    """Pool bytes of Q8_0 values: q + 128 (the top bit of the two's-complement byte flipped)."""
+    return q.view(np.uint8) ^ np.uint8(0x80)
+
+
+def from_excess128(b: np.ndarray) -> np.ndarray:
+    """Q8_0 values of pool bytes."""
+    return (b ^ np.uint8(0x80)).view(np.int8)
+
+
 def layout_maps(desc: PoolDesc):
     """Offset tables of the 16-token tile: K/V value offsets [16, D] and scale offsets [16, NB]."""
     D, NB = desc.head_dim, desc.n_groups
@@ -235,8 +245,8 @@ def np_kv_write_rows(desc: PoolDesc, pool: np.ndarray, layer: int, k: np.ndarray
     t = row_pos[idx] % 16
     for h in range(H):
         base = np_tile_base(desc, layer, page[idx], np.full(idx.size, h), row_pos[idx] % P)
-        pool[base[:, None] + koff[t]] = kq[:, h, :].view(np.uint8)
-        pool[base[:, None] + voff[t]] = vq[:, h, :].view(np.uint8)
+        pool[base[:, None] + koff[t]] = excess128(kq[:, h, :])
+        pool[base[:, None] + voff[t]] = excess128(vq[:, h, :])
         kdb = np.ascontiguousarray(kd[:, h, :]).view(np.uint8).reshape(-1, NB, 2)
         vdb = np.ascontiguousarray(vd[:, h, :]).view(np.uint8).reshape(-1, NB, 2)
         for byte in range(2):
@@ -254,8 +264,8 @@ def np_dequant_entry(desc: PoolDesc, pool: np.ndarray, layer: int, block_row: np
     base = np_tile_base(desc, layer, page, np.full(n_tokens, head), pos % P)
     koff, voff, ksoff, vsoff = layout_maps(desc)
     t = pos % 16
-    kq = pool[base[:, None] + koff[t]].view(np.int8).astype(np.float32)
-    vq = pool[base[:, None] + voff[t]].view(np.int8).astype(np.float32)
+    kq = from_excess128(pool[base[:, None] + koff[t]]).astype(np.float32)
+    vq = from_excess128(pool[base[:, None] + voff[t]]).astype(np.float32)
 
     def scales(off):
         lo = pool[base[:, None] + off[t]].astype(np.uint16)

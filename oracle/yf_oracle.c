@@ -115,7 +115,8 @@ size_t yfo_pool_bytes(const yfo_desc* d) {
     return (size_t)d->n_layers * d->n_pages * d->n_kv_heads * yfo_page_head_bytes(d);
 }
 
-/* Offset of the int8 value (t, dim) inside a tile.  K: lane (g = t%8, tig)
+/* Offset of the value byte (t, dim) inside a tile; the byte holds the Q8_0 value q as the
+ * excess-128 byte q + 128.  K: lane (g = t%8, tig)
  * holds dims 32b+8tig..+7 of tokens g and g+8 in one 16-byte word.  V: lane
  * (g = dim%8, tig = (t%8)/2) holds tokens {2tig, 2tig+8, 2tig+1, 2tig+9} of
  * dims 16m+g and 16m+g+8 for two adjacent 16-dim tiles m. */
@@ -191,7 +192,8 @@ int yfo_kv_write_rows(const yfo_desc* d, uint8_t* pool, int layer, const uint16_
             for (int kv = 0; kv < 2; ++kv) {
                 const uint16_t* src = (kv ? v : k) + ((size_t)r * H + h) * D;
                 yfo_quantize_row(src, D, G, q, sc);
-                for (int dim = 0; dim < D; ++dim) tile[yfo_tile_offset(d, kv, t, dim)] = (uint8_t)q[dim];
+                for (int dim = 0; dim < D; ++dim)
+                    tile[yfo_tile_offset(d, kv, t, dim)] = (uint8_t)((uint8_t)q[dim] ^ 0x80u);
                 for (int s = 0; s < NB; ++s) memcpy(tile + yfo_scale_offset(d, kv, t, s), &sc[s], 2);
             }
         }
@@ -212,7 +214,7 @@ void yfo_read_kv(const yfo_desc* d, const uint8_t* pool, int layer, int page, in
         for (int dim = 0; dim < D; ++dim) {
             uint16_t sb;
             memcpy(&sb, tile + yfo_scale_offset(d, kv, t, dim / G), 2);
-            int8_t qv = (int8_t)tile[yfo_tile_offset(d, kv, t, dim)];
+            int8_t qv = (int8_t)(tile[yfo_tile_offset(d, kv, t, dim)] ^ 0x80u);
             o[dim] = (float)qv * yfo_f16_to_f32(sb);
         }
     }

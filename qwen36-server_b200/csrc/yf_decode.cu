@@ -154,7 +154,7 @@ __device__ __forceinline__ void mma_init(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(__uint_as_float(c.x)),
           "f"(__uint_as_float(c.y)), "f"(__uint_as_float(c.z)), "f"(__uint_as_float(c.w)));
 }
-// bytes 0,1 / 2,3 of a biased word -> f16x2 of 1152 + x (the magic value before its subtraction)
+// bytes 0,1 / 2,3 of a pool word -> f16x2 of 1152 + x (the magic value before its subtraction)
 __device__ __forceinline__ uint32_t s8lo_to_h2_biased(uint32_t wb) { return __byte_perm(wb, 0x64646464u, 0x4140); }
 __device__ __forceinline__ uint32_t s8hi_to_h2_biased(uint32_t wb) { return __byte_perm(wb, 0x64646464u, 0x4342); }
 
@@ -292,7 +292,7 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
             for (int cc = 0; cc < CPG; ++cc) {
                 const int cb = s * CPG + cc;
                 const uint4 kw = lds128(T + cb * 512 + lane * 16);
-                const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+                const uint32_t x0 = kw.x, x1 = kw.y, z0 = kw.z, z1 = kw.w;
                 uint32_t a0 = s8lo_to_h2_biased(x0), a1 = s8lo_to_h2_biased(z0), a2 = s8hi_to_h2_biased(x0),
                          a3 = s8hi_to_h2_biased(z0);
 #pragma unroll
@@ -318,7 +318,7 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
             for (int cc = 0; cc < CPG; ++cc) {
                 const int cb = s * CPG + cc;
                 const uint4 kw = lds128(T + cb * 512 + lane * 16);
-                const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+                const uint32_t x0 = kw.x, x1 = kw.y, z0 = kw.z, z1 = kw.w;
                 uint32_t a0 = s8lo_to_h2(x0), a1 = s8lo_to_h2(z0), a2 = s8hi_to_h2(x0), a3 = s8hi_to_h2(z0);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a0, a1, a2, a3, qf[nt][cb].x, qf[nt][cb].y);
@@ -428,12 +428,12 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
         for (int mp = 0; mp < MPG / 2; ++mp) {
             const int mt0 = s * MPG + 2 * mp;
             const uint4 vw = lds128(T + V_OFF + (mt0 / 2) * 512 + lane * 16);
-            uint32_t w0 = bias8(vw.x), w1 = bias8(vw.y);
+            uint32_t w0 = vw.x, w1 = vw.y;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
                 mma16816(a.o[mt0][nt], s8lo_to_h2(w0), s8lo_to_h2(w1), s8hi_to_h2(w0), s8hi_to_h2(w1), b0[nt], b1[nt]);
-            w0 = bias8(vw.z);
-            w1 = bias8(vw.w);
+            w0 = vw.z;
+            w1 = vw.w;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
                 mma16816(a.o[mt0 + 1][nt], s8lo_to_h2(w0), s8lo_to_h2(w1), s8hi_to_h2(w0), s8hi_to_h2(w1), b0[nt],

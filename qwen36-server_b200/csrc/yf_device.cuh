@@ -111,24 +111,24 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Signed int8 bytes -> exact f16 pairs.  The byte x is biased to x+128,
-// placed as the low mantissa byte of the f16 0x6400 (= 1024), which gives
-// exactly 1024 + x + 128; subtracting 1152 leaves x.
+// Pool bytes -> exact f16 pairs.  The pool stores a Q8_0 value x in [-128, 127] as the excess-128
+// byte x + 128; placed as the low mantissa byte of the f16 0x6400 (= 1024) it gives exactly
+// 1024 + x + 128, and subtracting 1152 leaves x.
+__device__ __forceinline__ uint8_t excess128(int8_t x) { return (uint8_t)((uint8_t)x ^ 0x80u); }
 __device__ __forceinline__ uint32_t h2_sub_1152(uint32_t v) {
     uint32_t r;
     const uint32_t k = 0x64806480u;  // (1152, 1152) in f16
     asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(k));
     return r;
 }
-// bytes 0,1 of a biased word -> f16x2 (lo = byte 0)
+// bytes 0,1 of a pool word -> f16x2 (lo = byte 0)
 __device__ __forceinline__ uint32_t s8lo_to_h2(uint32_t wb) {
     return h2_sub_1152(__byte_perm(wb, 0x64646464u, 0x4140));
 }
-// bytes 2,3 of a biased word -> f16x2 (lo = byte 2)
+// bytes 2,3 of a pool word -> f16x2 (lo = byte 2)
 __device__ __forceinline__ uint32_t s8hi_to_h2(uint32_t wb) {
     return h2_sub_1152(__byte_perm(wb, 0x64646464u, 0x4342));
 }
-__device__ __forceinline__ uint32_t bias8(uint32_t w) { return w ^ 0x80808080u; }
 
 __device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
     uint32_t r;

@@ -116,14 +116,14 @@ __global__ void __launch_bounds__(kWriteWarps * 32) kv_write_kernel(const WriteP
             if constexpr (E == 4) {
                 uint32_t w = 0;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) w |= (uint32_t)(uint8_t)qv[e] << (8 * e);
+                for (int e = 0; e < 4; ++e) w |= (uint32_t)excess128(qv[e]) << (8 * e);
                 *reinterpret_cast<uint32_t*>(dst) = w;
             } else {
                 uint2 w = make_uint2(0, 0);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    w.x |= (uint32_t)(uint8_t)qv[e] << (8 * e);
-                    w.y |= (uint32_t)(uint8_t)qv[4 + e] << (8 * e);
+                    w.x |= (uint32_t)excess128(qv[e]) << (8 * e);
+                    w.y |= (uint32_t)excess128(qv[4 + e]) << (8 * e);
                 }
                 *reinterpret_cast<uint2*>(dst) = w;
             }
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kWriteWarps * 32) kv_write_kernel(const WriteP
             for (int e = 0; e < E; ++e) {
                 const int dim = d0 + e, m = dim / 16, ii = dim % 16;
                 tile[V_OFF + (m / 2) * 512 + ((ii % 8) * 4 + tig) * 16 + (m % 2) * 8 + (ii / 8) * 4 + j] =
-                    (uint8_t)qv[e];
+                    excess128(qv[e]);
             }
             if (lane % LPG == 0) {
                 const int off = VS_OFF + 2 * ((tig * NB + grp) * 4 + j);

@@ -222,9 +222,9 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c, int rows) {
     return (uint32_t)(kb * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + ((cc ^ (r & 7)) << 4));
 }
 
-// f16x2 of bytes (lo, hi) of a biased word, times an f16x2 scale pair.
-__device__ __forceinline__ uint32_t dq2(uint32_t biased, int sel, uint32_t scale2) {
-    const uint32_t h = sel ? s8hi_to_h2(biased) : s8lo_to_h2(biased);
+// f16x2 of bytes (lo, hi) of a pool word, times an f16x2 scale pair.
+__device__ __forceinline__ uint32_t dq2(uint32_t w, int sel, uint32_t scale2) {
+    const uint32_t h = sel ? s8hi_to_h2(w) : s8lo_to_h2(w);
     return h2mul(h, scale2);
 }
 
@@ -590,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                     const uint16_t s1 =
                         *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2 + 1) * 4 + dw));
                     const uint32_t d0 = (uint32_t)s0 | ((uint32_t)s0 << 16), d1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
-                    const uint32_t x0 = bias8(kw.x), x1 = bias8(kw.y), z0 = bias8(kw.z), z1 = bias8(kw.w);
+                    const uint32_t x0 = kw.x, x1 = kw.y, z0 = kw.z, z1 = kw.w;
                     o0 = make_uint4(dq2(x0, 0, d0), dq2(x0, 1, d0), dq2(x1, 0, d0), dq2(x1, 1, d0));
                     o1 = make_uint4(dq2(z0, 0, d1), dq2(z0, 1, d1), dq2(z1, 0, d1), dq2(z1, 1, d1));
                 }
@@ -643,7 +643,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                     // keys 0..7 = bytes 0,2 of wv[0..3]; keys 8..15 = bytes 1,3
                     const uint32_t k03 = __byte_perm(wv[0], wv[1], 0x6420), k47 = __byte_perm(wv[2], wv[3], 0x6420);
                     const uint32_t k8b = __byte_perm(wv[0], wv[1], 0x7531), kcf = __byte_perm(wv[2], wv[3], 0x7531);
-                    const uint32_t a = bias8(k03), bq = bias8(k47), c8 = bias8(k8b), cf = bias8(kcf);
+                    const uint32_t a = k03, bq = k47, c8 = k8b, cf = kcf;
                     lo = make_uint4(dq2(a, 0, sp[0]), dq2(a, 1, sp[1]), dq2(bq, 0, sp[2]), dq2(bq, 1, sp[3]));
                     hi = make_uint4(dq2(c8, 0, sp[4]), dq2(c8, 1, sp[5]), dq2(cf, 0, sp[6]), dq2(cf, 1, sp[7]));
                 }

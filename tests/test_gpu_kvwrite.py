@@ -61,7 +61,7 @@ def test_gpu_quantizer_matches_gguf_golden(yf, oracle, cuda):
         for r in range(n):
             base = oracle.np_tile_base(desc, 0, wl.block_table[0, r // 16:r // 16 + 1], np.zeros(1), np.array([r % 16]))[0]
             off = (voff if kv else koff)[r % 16]
-            got_q[r] = img[base + off].view(np.int8)
+            got_q[r] = oracle.from_excess128(img[base + off])
             so = (vsoff if kv else ksoff)[r % 16]
             got_d[r] = img[base + so] | (img[base + so + 1].astype(np.uint16) << 8)
         assert np.array_equal(got_q.reshape(-1, 32), qs[: 4 * n])
