@@ -314,11 +314,13 @@ class ShardedStep:
         return (1 if self.owner else 0) + 1 + self.shard.n_head_groups
 
 
-def make_workload(name: str, rank: int):
+def make_workload(name: str, rank: int, layers: int = 0):
     from qwen36_server_b200 import workloads as W
 
     fn = W.CONFIGS[name]
     base_seed = fn.__defaults__[0]
+    if layers and name == "mtp_verify":
+        return fn(seed=base_seed + 1000 * rank, n_layers=layers)
     return fn(seed=base_seed + 1000 * rank)
 
 
@@ -327,7 +329,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     import torch.distributed as dist
 
     sharded = args.config == "decode_long" and world > 1
-    wl = make_workload(args.config, 0 if sharded else rank)
+    wl = make_workload(args.config, 0 if sharded else rank, args.layers)
     layers_resident = wl.n_layers
     if args.config == "mtp_verify":
         free = torch.cuda.mem_get_info(local_rank)[0]
@@ -573,6 +575,9 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-tokens", type=float, default=1.2e5)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="mtp_verify only: stack this many layers instead of 36 (one launch per layer keeps "
+                         "its shape; for profiling a launch with a few GB resident, not a bench line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
