@@ -174,7 +174,8 @@ class Step:
         self.cu_k = i32(wl.cu_k)
         self.cu_q = i32(wl.cu_q)
         self.start = i32(wl.prefix)
-        self.decode = bool((wl.q_rows == 1).all())
+        self.trie = None if wl.trie is None else i32(wl.trie)
+        self.decode = bool((wl.q_rows == 1).all()) and self.trie is None
         self.max_q = int(wl.q_rows.max())
         self.max_k = int(wl.ctx.max())
         ws = self.pool.workspace_size(wl.n_q_heads, wl.batch, self.max_q if not self.decode else 1, self.max_k)
@@ -208,6 +209,10 @@ class Step:
                 a = (L.yf_attn_prefill, (h, pl, ptr(self.q), wl.n_q_heads, ptr(self.cu_q), ptr(self.cu_k),
                                          ptr(self.bt), wl.max_blocks, wl.batch, self.max_q, self.max_k, scale,
                                          ptr(self.out), ptr(self.ws), self.ws_bytes, s))
+                if self.trie is not None:  # tree speculative verify: the trie mask instead of causal rows
+                    a = (L.yf_attn_verify_tree, (h, pl, ptr(self.q), wl.n_q_heads, ptr(self.cu_q), ptr(self.cu_k),
+                                                 ptr(self.bt), wl.max_blocks, wl.batch, self.max_q, self.max_k, scale,
+                                                 ptr(self.trie), ptr(self.out), ptr(self.ws), self.ws_bytes, s))
             self.calls.append((w, a))
 
     def run(self):
@@ -319,7 +324,7 @@ def make_workload(name: str, rank: int, layers: int = 0):
 
     fn = W.CONFIGS[name]
     base_seed = fn.__defaults__[0]
-    if layers and name == "mtp_verify":
+    if layers and name in ("mtp_verify", "tree_verify"):
         return fn(seed=base_seed + 1000 * rank, n_layers=layers)
     return fn(seed=base_seed + 1000 * rank)
 
@@ -331,7 +336,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     sharded = args.config == "decode_long" and world > 1
     wl = make_workload(args.config, 0 if sharded else rank, args.layers)
     layers_resident = wl.n_layers
-    if args.config == "mtp_verify":
+    if args.config in ("mtp_verify", "tree_verify"):
         free = torch.cuda.mem_get_info(local_rank)[0]
         per_layer = wl.kv_bytes(1)
         layers_resident = max(1, min(wl.n_layers, int(0.8 * free // per_layer)))
@@ -537,7 +542,8 @@ def cpu_baseline(wl, seconds: float):
     return {"value": samp.tokens / dt, "unit": "tokens/s", "cores": samp.threads, "kind": "port",
             "sample": f"{samp.sub.batch} of {wl.batch} entries ({int(samp.sub.ctx.sum())} keys, "
                       f"{samp.n_layers} layer(s)), {n} steps; oracle/yf_oracle.c double-precision attention "
-                      f"+ Q8_0 scatter"}
+                      f"+ Q8_0 scatter" + ("; causal rows stand in for the trie mask (same keys but the "
+                                           "skipped branch nodes)" if wl.trie is not None else "")}
 
 
 def reference_arm(args):
@@ -569,7 +575,8 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="decode_batch",
-                    choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify"])
+                    choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify",
+                             "tree_verify"])
     ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")

@@ -211,6 +211,24 @@ YF_API int yf_attn_prefill(yf_pool* pool, int32_t layer, const void* d_q, int32_
                            int32_t max_seqlen_q, int32_t max_seqlen_k, float scale, void* d_out,
                            void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* Tree speculative verify: replaces forward_verify_tree_graphed with its
+ * trie_ranges mask (docs/plans/2026-10-09-tree-speculative-decoding.md:26-38).
+ * As yf_attn_prefill, but an entry's Tq_b <= 64 draft rows are the nodes of a
+ * token trie in depth-first order: d_trie_ranges (int32 [total_q][2], 8-byte
+ * aligned) holds for draft row j of an entry the inclusive range [start_j,
+ * end_j] of its subtree, as node indices 0 .. Tq_b-1 of that entry.  Row i
+ * sees the committed keys 0 .. Tk_b - Tq_b - 1 and draft key Tk_b - Tq_b + j
+ * when j <= i and start_j <= i <= end_j (j is i or an ancestor of i).  A chain
+ * (start_j = j, end_j = Tq_b - 1) gives yf_attn_prefill's causal rows.  A
+ * range outside 0 .. Tq_b-1 is clamped and flags YF_DEV_BAD_ROWS.  Workspace:
+ * yf_attn_workspace_size with the same arguments. */
+YF_API int yf_attn_verify_tree(yf_pool* pool, int32_t layer, const void* d_q, int32_t n_q_heads,
+                               const uint32_t* d_cu_seqlens_q, const uint32_t* d_cu_seqlens_k,
+                               const uint32_t* d_block_table, int32_t max_blocks, int32_t batch,
+                               int32_t max_seqlen_q, int32_t max_seqlen_k, float scale,
+                               const int32_t* d_trie_ranges, void* d_out, void* d_workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Sharded decode, first half: yf_attn_decode over the keys this pool holds
  * (one shard of each sequence and/or a subset of the kv heads), emitting
  * partials instead of f16 output: d_o_part f32 [B, Hq, D] is O normalised

@@ -303,6 +303,42 @@ def np_attn(desc: PoolDesc, pool: np.ndarray, layer: int, q: np.ndarray, cu_q, c
     return out
 
 
+def tree_visible(ranges: np.ndarray, i: int) -> np.ndarray:
+    """Draft nodes row i of a trie verify sees: node j with j <= i and start_j <= i <= end_j,
+    ranges int [Tq, 2] of inclusive depth-first subtree ranges (the reference's trie mask
+    "committed prefix plus the current node's subtree ranges",
+    docs/plans/2026-10-09-tree-speculative-decoding.md:26-38)."""
+    j = np.arange(len(ranges))
+    return (j <= i) & (ranges[:, 0] <= i) & (i <= ranges[:, 1])
+
+
+def np_attn_tree(desc: PoolDesc, pool: np.ndarray, layer: int, q: np.ndarray, cu_q, cu_k, block_table,
+                 scale: float, trie_ranges: np.ndarray) -> np.ndarray:
+    """Tree speculative verify over the dequantized pool (float64 softmax): entry b's draft rows
+    are trie nodes at keys Tk-Tq .. Tk-1; row i sees keys 0 .. Tk-Tq-1 and the draft keys of the
+    nodes tree_visible(ranges of b, i).  trie_ranges int [total_q, 2]."""
+    q = np.asarray(q, np.float16).astype(np.float64)
+    Hq = q.shape[1]
+    H = desc.n_kv_heads
+    grp = Hq // H
+    out = np.zeros(q.shape, np.float32)
+    for b in range(len(cu_q) - 1):
+        q0, Tq = int(cu_q[b]), int(cu_q[b + 1] - cu_q[b])
+        Tk = int(cu_k[b + 1] - cu_k[b])
+        kv0 = Tk - Tq
+        rng = np.asarray(trie_ranges[q0:q0 + Tq], np.int64)
+        for h in range(H):
+            K, V = np_dequant_entry(desc, pool, layer, block_table[b], Tk, h)
+            for i in range(Tq):
+                keys = np.concatenate([np.arange(kv0), kv0 + np.nonzero(tree_visible(rng, i))[0]])
+                qs = q[q0 + i, h * grp:(h + 1) * grp]
+                s = qs @ K[keys].astype(np.float64).T * scale
+                s -= s.max(axis=1, keepdims=True)
+                p = np.exp(s)
+                out[q0 + i, h * grp:(h + 1) * grp] = (p @ V[keys].astype(np.float64)) / p.sum(axis=1, keepdims=True)
+    return out
+
+
 def np_partial_decode(q: np.ndarray, K: np.ndarray, V: np.ndarray, scale: float):
     """One decode row over one key range, as the split-KV partial the reference's combine
     consumes: q [hq, D] (f16 values), K/V [n_keys, D] dequantized.  Returns (O [hq, D]

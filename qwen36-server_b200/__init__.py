@@ -13,6 +13,7 @@ from .paged_attn import (  # noqa: F401
     dispatch_flash_decode_partial,
     forward_attn_prefill_paged,
     forward_verify_paged,
+    forward_verify_tree_paged,
     kv_append_paged,
     launch_append_multi,
 )

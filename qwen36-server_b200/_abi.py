@@ -78,6 +78,8 @@ SIGNATURES = {
     "yf_attn_decode_noalloc": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),
     "yf_attn_prefill": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
                               _vp]),
+    "yf_attn_verify_tree": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp,
+                                  _sz, _vp]),
     "yf_attn_decode_partial": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _sz,
                                      _vp]),
     "yf_attn_combine": (_ci, [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _i32, _i32, _i32, _vp, _vp]),

@@ -43,13 +43,16 @@ namespace yf {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kHdrBytes = 256;  // mbarriers + per-stage page-valid flags
+constexpr int kMaxTreeRows = 64;  // draft rows per entry of a tree verify (one 64-bit mask each)
 // 16-row units (two n-tiles) are bound by instruction issue rather than by HBM: their QK feeds
 // K as the f16 values 1152 + k and starts each scale group's accumulator at -1152 x (the row's q
 // summed over the group), read per warp from shared memory: [group][tig][n-tile][4] floats.
 template <int NT>
 constexpr bool kbias_in_acc() { return NT == 2; }
-template <int NB, int NT>
-constexpr int hdr_bytes() { return kHdrBytes + (kbias_in_acc<NT>() ? kWarps * NB * 4 * NT * 16 : 0); }
+template <int NB, int NT, bool TREE = false>
+constexpr int hdr_bytes() {
+    return kHdrBytes + (kbias_in_acc<NT>() ? kWarps * NB * 4 * NT * 16 : 0) + (TREE ? kMaxTreeRows * 8 : 0);
+}
 template <int NB, int NT>
 __device__ __forceinline__ float* kbias_area(uint8_t* smem, int warp) {
     return reinterpret_cast<float*>(smem + kHdrBytes) + warp * NB * 4 * NT * 4;
@@ -84,6 +87,17 @@ struct SplitParams {
     float* ws_lse;
     uint32_t* counters;  // per-unit arrival counters for the merge, or null (separate combine)
     uint32_t* status;
+    const int2* trie;    // tree verify: inclusive subtree range of every draft row, or null
+};
+
+// Tree verify: the draft rows of an entry are the nodes of a token trie in depth-first order;
+// row i sees the committed keys and draft key j when j <= i and i lies in node j's subtree
+// range (j is i or an ancestor).  anc[i] has bit j set for those j.
+struct TreeCtx {
+    const unsigned long long* anc;  // [Tq] in shared memory
+    int kv0;                        // first draft key (Tk - Tq)
+    int row0;                       // first row of the unit
+    int G;
 };
 
 // Geometry of one unit, computed identically everywhere.
@@ -239,10 +253,10 @@ __device__ __forceinline__ void load_unit_q(const SplitParams& p, const UnitGeom
 }
 
 // One 16-token tile (already in shared memory at T) into the warp's running softmax state.
-template <int D, int NB, int NT>
+template <int D, int NB, int NT, bool TREE = false>
 __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 (&qf)[NT][D / 32],
                                           const int (&kvlen)[NT][2], int kv_min, const float* cw,
-                                          float scale_log2, WarpAcc<D, NT>& a, int lane) {
+                                          float scale_log2, WarpAcc<D, NT>& a, int lane, const TreeCtx& tc) {
     constexpr int KS_OFF = 16 * D;
     constexpr int V_OFF = 16 * D + 32 * NB;
     constexpr int VS_OFF = 32 * D + 32 * NB;
@@ -355,6 +369,16 @@ __device__ __forceinline__ void tile_math(const uint8_t* T, int kt, const uint4 
             for (int col = 0; col < 2; ++col) {
                 if (tok0 >= kvlen[nt][col]) v[nt][col] = -INFINITY;
                 if (tok1 >= kvlen[nt][col]) v[nt][2 + col] = -INFINITY;
+                if constexpr (TREE) {
+                    // kvlen[] > 0 only for real rows; draft keys j = tok - kv0 < kvlen - kv0 <= 64
+                    if (kvlen[nt][col] > 0) {
+                        const unsigned long long anc = tc.anc[(tc.row0 + nt * 8 + 2 * tig + col) / tc.G];
+                        if (tok0 >= tc.kv0 && tok0 < kvlen[nt][col] && !((anc >> (tok0 - tc.kv0)) & 1ull))
+                            v[nt][col] = -INFINITY;
+                        if (tok1 >= tc.kv0 && tok1 < kvlen[nt][col] && !((anc >> (tok1 - tc.kv0)) & 1ull))
+                            v[nt][2 + col] = -INFINITY;
+                    }
+                }
             }
     }
     bool need = false;
@@ -483,11 +507,11 @@ struct TileRing {
 
 // Streams tiles t0 + warp + 4i (i < this warp's share of n_seg tiles) of unit (b, h) through
 // the warp's ring into `a`.  A bounded wait that gives up flags YF_DEV_TIMEOUT.
-template <int D, int NB, int NT, int TPP, int STAGES>
+template <int D, int NB, int NT, int TPP, int STAGES, bool TREE = false>
 __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * D + 64 * NB, STAGES>& ring, int b,
                                             int h, int t0, int n_seg, const uint4 (&qf)[NT][D / 32],
                                             const int (&kvlen)[NT][2], int kv_min, const float* cw,
-                                            WarpAcc<D, NT>& a, int warp, int lane) {
+                                            WarpAcc<D, NT>& a, int warp, int lane, const TreeCtx& tc) {
     constexpr int TB = 32 * D + 64 * NB;
     const int my_n = n_seg > warp ? (n_seg - warp + kWarps - 1) / kWarps : 0;
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
@@ -516,7 +540,8 @@ __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * 
         }
         done = i + 1;
         if (ring.flag[slot])
-            tile_math<D, NB, NT>(ring.stage + slot * TB, tile_of(i), qf, kvlen, kv_min, cw, p.scale_log2, a, lane);
+            tile_math<D, NB, NT, TREE>(ring.stage + slot * TB, tile_of(i), qf, kvlen, kv_min, cw, p.scale_log2, a,
+                                       lane, tc);
         __syncwarp();
         if (lane == 0 && i + STAGES < my_n) {
             ring.issue(i + STAGES, src_of(tile_of(i + STAGES), next_page), p.status);
@@ -1007,7 +1032,8 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
         unit_geom<TPP, RPC>(p, b, 0, u, false);
         load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp));
         acc.reset();
-        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp), acc, warp, lane);
+        stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, (int)(seg_e - x), qf, kvlen, kv_min,
+                                            kbias_area<NB, NT>(smem, warp), acc, warp, lane, TreeCtx{});
         stash_warp<D, NT>(stages, acc, warp, lane);
         const bool whole = x == Us && seg_e == Ue;
         // partial slots: 2 per CTA; slot 1 when the CTA began inside an earlier unit
@@ -1036,7 +1062,7 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
 
 // ---- schedule 2: a 3-D grid of (unit, chunk of tiles) ----------------------------------------
 
-template <int D, int NB, int NT, int TPP, int STAGES>
+template <int D, int NB, int NT, int TPP, int STAGES, bool TREE = false>
 __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) {
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int RPC = 8 * NT;
@@ -1044,7 +1070,7 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     static_assert(kHdrBytes >= kWarps * STAGES * 9, "header area too small");
     static_assert(kWarps * STAGES * TB >= 2 * kWarps * RPC * 4 + kWarps * RPC * DP * 4, "merge area too small");
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* stages = smem + hdr_bytes<NB, NT>();
+    uint8_t* stages = smem + hdr_bytes<NB, NT, TREE>();
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // chunk index is the slowest grid dimension: every unit's first chunks are dispatched first
@@ -1060,11 +1086,29 @@ __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) 
     uint4 qf[NT][D / 32];
     int kvlen[NT][2], kv_min;
     load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp));
+    TreeCtx tc{};
+    if constexpr (TREE) {
+        // ancestor masks of the entry's draft rows from the subtree ranges (clamped to the block;
+        // a range outside it flags YF_DEV_BAD_ROWS)
+        unsigned long long* anc = reinterpret_cast<unsigned long long*>(smem + hdr_bytes<NB, NT>());
+        for (int i = threadIdx.x; i < kMaxTreeRows; i += kThreads) anc[i] = 0ull;
+        __syncthreads();
+        for (int j = threadIdx.x; j < u.Tq; j += kThreads) {
+            const int2 r = p.trie[u.qrow0 + j];
+            if (r.x < 0 || r.y >= u.Tq || r.x > r.y) atomicOr(p.status, YF_DEV_BAD_ROWS);
+            const int lo = max(max(r.x, j), 0), hi = min(r.y, u.Tq - 1);
+            for (int i = lo; i <= hi; ++i) atomicOr(&anc[i], 1ull << j);
+        }
+        __syncthreads();
+        tc = TreeCtx{anc, u.Tk - u.Tq, u.row_begin, p.G};
+        kv_min = min(kv_min, u.Tk - u.Tq);  // every tile holding a draft key takes the mask
+    }
     TileRing<TB, STAGES> ring;
     ring.init(smem, stages, warp, lane);
     WarpAcc<D, NT> acc;
     acc.reset();
-    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp), acc, warp, lane);
+    stream_unit<D, NB, NT, TPP, STAGES, TREE>(p, ring, b, h, tile_begin, tile_end - tile_begin, qf, kvlen, kv_min,
+                                              kbias_area<NB, NT>(smem, warp), acc, warp, lane, tc);
     stash_warp<D, NT>(stages, acc, warp, lane);
 
     const bool direct = u.n_chunks == 1;
@@ -1105,13 +1149,13 @@ static int raise_smem(K kern, int smem, int dev, int* set_to) {
     return YF_OK;
 }
 
-template <int D, int NB, int NT, int TPP, int STAGES>
+template <int D, int NB, int NT, int TPP, int STAGES, bool TREE = false>
 static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
     constexpr int TB = 32 * D + 64 * NB;
-    constexpr int SMEM = hdr_bytes<NB, NT>() + kWarps * STAGES * TB;
+    constexpr int SMEM = hdr_bytes<NB, NT, TREE>() + kWarps * STAGES * TB;
     const int dev = a.pool->desc.device;
     cudaError_t e;
-    if (plan.persistent) {
+    if (!TREE && plan.persistent) {
         auto kern = decode_persistent_kernel<D, NB, NT, TPP, STAGES>;
         static int set_to[64] = {};
         const int smem = SMEM + (a.batch + 1) * (int)sizeof(long long);
@@ -1136,7 +1180,7 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
         e = cudaGetLastError();
         return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_persistent launch");
     }
-    auto kern = splitkv_kernel<D, NB, NT, TPP, STAGES>;
+    auto kern = splitkv_kernel<D, NB, NT, TPP, STAGES, TREE>;
     static int set_to2[64] = {};
     const int rc = raise_smem(kern, SMEM, dev, set_to2);
     if (rc) return rc;
@@ -1155,6 +1199,12 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
 
 template <int D, int NB, int NT, int TPP>
 static int launch_st(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
+    if (p.trie) {  // tree verify: the chunked schedule at the default depth
+        if constexpr (D == 128)
+            return launch_t<D, NB, NT, TPP, 4, true>(a, plan, p);
+        else
+            return launch_t<D, NB, NT, TPP, 2, true>(a, plan, p);
+    }
     if (plan.stages == 3) return launch_t<D, NB, NT, TPP, 3>(a, plan, p);
     if constexpr (D == 128)
         return launch_t<D, NB, NT, TPP, 4>(a, plan, p);
@@ -1192,6 +1242,8 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.part_o = a.part_o;
     p.part_lse = a.part_lse;
     p.status = a.pool->d_status;
+    p.trie = reinterpret_cast<const int2*>(a.trie);
+    if (p.trie && plan.persistent) return fail(YF_E_UNSUPPORTED, "tree verify needs the chunked schedule");
     const size_t units = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups;
     p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;
     if (plan.persistent && !p.counters) return fail(YF_E_UNSUPPORTED, "persistent decode needs the merge counters");

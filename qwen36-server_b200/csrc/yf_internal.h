@@ -86,7 +86,10 @@ struct SplitPlan {
     size_t ws_bytes;   // partial O + lse
 };
 
-SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k);
+SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k,
+                     bool tree = false);
+// draft rows per entry of a tree verify (a 64-bit ancestor mask per row in the kernel)
+constexpr int kMaxTreeRowsHost = 64;
 
 struct AttnArgs {
     const yf_pool* pool;
@@ -109,6 +112,8 @@ struct AttnArgs {
     // sum of exp(scaled logits) per (row, q head), for a later yf_attn_combine
     float* part_o = nullptr;
     float* part_lse = nullptr;
+    // tree verify: int32 [total_q][2] inclusive subtree range of every draft row, or null
+    const int32_t* trie = nullptr;
 };
 
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).

@@ -1,5 +1,6 @@
 // Pool lifetime, page allocator, snapshot export/restore, argument checks and
 // the attention entry points of the C ABI (include/yfattn.h).
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -46,7 +47,7 @@ static size_t tile_bytes_of(const yf_pool_desc* d) {
 // Splits the tile range of every (entry, kv head, row group) into chunks so
 // that the grid covers the SMs several times over; the last chunk of each
 // unit is partial, so more, smaller chunks keep the tail short.
-SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k) {
+SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k, bool tree) {
     SplitPlan p;
     const int H = pool->desc.n_kv_heads;
     const int G = n_q_heads / H;
@@ -86,7 +87,7 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     // Persistent schedule: one row group per entry (decode, small verify blocks), a batch whose
     // tile prefix fits in shared memory, and the merge counters available.
     const char* ps = getenv("YF_PERSISTENT");
-    p.persistent = !(ps && atoi(ps) == 0) && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
+    p.persistent = !tree && !(ps && atoi(ps) == 0) && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
                    units <= kMaxCombineUnits && fused_env;
     if (p.persistent) p.fused_combine = true;
     const size_t row_bytes = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
@@ -366,20 +367,23 @@ static int check_attn(const yf_pool* pool, int32_t layer, const void* q, int32_t
 
 size_t yf_attn_workspace_size(const yf_pool* pool, int32_t hq, int32_t batch, int32_t max_q, int32_t max_k) {
     if (!pool || batch <= 0 || hq < pool->desc.n_kv_heads || hq % pool->desc.n_kv_heads) return 0;
-    if (max_q > 1 && prefill_tc_applies(pool, hq, max_q)) return 0;
-    return plan_split(pool, hq, batch, max_q, max_k).ws_bytes;
+    if (max_q > kMaxTreeRowsHost && prefill_tc_applies(pool, hq, max_q)) return 0;
+    // query blocks a tree verify can take: room for both schedules
+    const size_t ws = plan_split(pool, hq, batch, max_q, max_k, false).ws_bytes;
+    if (max_q <= 1 || max_q > kMaxTreeRowsHost) return ws;
+    return std::max(ws, plan_split(pool, hq, batch, max_q, max_k, true).ws_bytes);
 }
 
 static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,
                     const uint32_t* cu_k, const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_q,
                     int32_t max_k, float scale, void* out, void* ws, size_t ws_bytes, void* stream,
-                    float* part_o = nullptr, float* part_lse = nullptr) {
+                    float* part_o = nullptr, float* part_lse = nullptr, const int32_t* trie = nullptr) {
     const int rc =
         check_attn(pool, layer, q, hq, cu_k, bt, max_blocks, batch, max_q, max_k, scale, part_o ? part_o : out);
     if (rc || batch == 0) return rc;
     if (part_o && (!part_lse || !aligned(part_lse, 4))) return fail(YF_E_INVALID, "lse output null or misaligned");
-    const bool tc = !part_o && cu_q && prefill_tc_applies(pool, hq, max_q);
-    const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k);
+    const bool tc = !part_o && !trie && cu_q && prefill_tc_applies(pool, hq, max_q);
+    const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k, trie != nullptr);
     if (!tc && plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
         return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", plan.ws_bytes,
                     ws ? ws_bytes : (size_t)0);
@@ -402,6 +406,7 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     a.stream = static_cast<cudaStream_t>(stream);
     a.part_o = part_o;
     a.part_lse = part_lse;
+    a.trie = trie;
     if (tc) return launch_prefill_tc(a);
     return launch_splitkv(a, plan);
 }
@@ -427,6 +432,19 @@ int yf_attn_prefill(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     if (batch > 0 && !cu_q) return fail(YF_E_INVALID, "cu_seqlens_q is null");
     return run_attn(pool, layer, q, hq, cu_q, cu_k, bt, max_blocks, batch, max_q, max_k, scale, out, ws, ws_bytes,
                     stream);
+}
+
+int yf_attn_verify_tree(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,
+                        const uint32_t* cu_k, const uint32_t* bt, int32_t max_blocks, int32_t batch, int32_t max_q,
+                        int32_t max_k, float scale, const int32_t* trie_ranges, void* out, void* ws,
+                        size_t ws_bytes, void* stream) {
+    if (batch > 0 && !cu_q) return fail(YF_E_INVALID, "cu_seqlens_q is null");
+    if (batch > 0 && (!trie_ranges || !aligned(trie_ranges, 8)))
+        return fail(YF_E_INVALID, "trie_ranges null or not 8-byte aligned");
+    if (max_q > kMaxTreeRowsHost)
+        return fail(YF_E_UNSUPPORTED, "tree verify of %d rows per entry (at most %d)", max_q, kMaxTreeRowsHost);
+    return run_attn(pool, layer, q, hq, cu_q, cu_k, bt, max_blocks, batch, max_q, max_k, scale, out, ws, ws_bytes,
+                    stream, nullptr, nullptr, batch > 0 ? trie_ranges : nullptr);
 }
 
 }  // extern "C"

@@ -333,5 +333,37 @@ def forward_verify_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, cu_seql
     return forward_attn_prefill_paged(q, pool, layer, cu_seqlens_q, cu_seqlens_k, table, scale, **kw)
 
 
+def forward_verify_tree_paged(q: torch.Tensor, pool: PagedKvPool, layer: int, cu_seqlens_q, cu_seqlens_k, table,
+                              scale: float, trie_ranges, max_seqlen_q: Optional[int] = None,
+                              max_seqlen_k: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                              workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Tree speculative verify (the reference's forward_verify_tree_graphed with trie_ranges,
+    docs/plans/2026-10-09-tree-speculative-decoding.md:26-38): each entry's <= 64 draft rows are
+    trie nodes in depth-first order and trie_ranges (int32 [total_q, 2]) holds every node's
+    inclusive subtree range [start, end] within its entry; row i sees the committed keys and the
+    draft keys of i and its ancestors (node j with j <= i and start_j <= i <= end_j)."""
+    T, Hq, D = q.shape
+    if q.dtype != torch.float16 or D != pool.head_dim or not q.is_contiguous():
+        raise YfError(_abi.YF_E_INVALID, "forward_verify_tree_paged", "q must be contiguous f16 [T, Hq, D]")
+    if max_seqlen_q is None:
+        max_seqlen_q = _max_len(cu_seqlens_q)
+    if max_seqlen_k is None:
+        max_seqlen_k = _max_len(cu_seqlens_k)
+    max_seqlen_q = max(int(max_seqlen_q), 1)
+    cq = _i32(cu_seqlens_q, pool.device)
+    ck = _i32(cu_seqlens_k, pool.device)
+    table = _i32(table, pool.device)
+    tr = _i32(trie_ranges, pool.device).reshape(-1, 2).contiguous()
+    if tr.shape[0] != T:
+        raise YfError(_abi.YF_E_INVALID, "forward_verify_tree_paged", "trie_ranges must be int32 [total_q, 2]")
+    B = ck.numel() - 1
+    if out is None:
+        out = torch.empty_like(q)
+    ws, ws_bytes = _ws_args(pool, workspace, pool.workspace_size(Hq, B, max_seqlen_q, max_seqlen_k))
+    call("yf_attn_verify_tree", pool.handle, layer, _ptr(q), Hq, _ptr(cq), _ptr(ck), _ptr(table), table.shape[1], B,
+         max_seqlen_q, max_seqlen_k, ctypes.c_float(scale), _ptr(tr), _ptr(out), ws, ws_bytes, _stream(pool.device))
+    return out
+
+
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)

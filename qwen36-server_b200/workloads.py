@@ -11,6 +11,7 @@ permutation so that every slot's page table is fragmented.
   decode_long    1 slot, ctx 131072, Hq 16 x D 256, Hkv 2
   prefill_chunk  4 entries x (8192 restored prefix + 2048-token chunk), Hq 32 x D 128, Hkv 8
   mtp_verify     64 slots x 4 draft rows, ctx ~ U[4096, 65536], Hq 32 x D 128, Hkv 8, 36 layers
+  tree_verify    mtp_verify's shape with an 8-node draft trie per slot (tree speculative verify)
 
 "ctx" counts every key the step attends to, the step's own new rows included.
 """
@@ -38,6 +39,7 @@ class Workload:
     extra_pages: int = 0
     block_table: np.ndarray = field(default=None, repr=False)
     n_pages: int = 0
+    trie: Optional[np.ndarray] = field(default=None, repr=False)  # int32 [total_q, 2] subtree ranges
 
     def __post_init__(self):
         self.ctx = np.asarray(self.ctx, np.int64)
@@ -100,6 +102,23 @@ def fragmented_tables(ctx: np.ndarray, page_size: int, seed: int, extra_pages: i
     return table, n_pages
 
 
+def random_trie(rng: np.random.Generator, n: int, max_children: int = 3) -> np.ndarray:
+    """A seeded token trie of n draft nodes in depth-first order, as int32 [n, 2] inclusive
+    subtree ranges (node 0 is the root; a chain is [[j, n-1]]).  Each new node hangs under a node
+    of the previous node's root path, which keeps every subtree a contiguous index range."""
+    parent = [-1]
+    for j in range(1, n):
+        path = [j - 1]
+        while parent[path[-1]] >= 0:
+            path.append(parent[path[-1]])
+        kids = [p for p in path if sum(1 for x in parent if x == p) < max_children]
+        parent.append(int(rng.choice(kids)) if kids else j - 1)
+    end = list(range(n))
+    for j in range(n - 1, 0, -1):
+        end[parent[j]] = max(end[parent[j]], end[j])
+    return np.array([[j, end[j]] for j in range(n)], np.int32)
+
+
 def decode_small(seed: int = 1) -> Workload:
     return Workload("decode_small", 32, 8, 128, ctx=[4096], q_rows=[1], seed=seed)
 
@@ -124,12 +143,21 @@ def mtp_verify(seed: int = 5, n_slots: int = 64, drafts: int = 4, n_layers: int 
     return Workload("mtp_verify", 32, 8, 128, ctx=ctx, q_rows=[drafts] * n_slots, n_layers=n_layers, seed=seed)
 
 
+def tree_verify(seed: int = 6, n_slots: int = 64, nodes: int = 8, n_layers: int = 36) -> Workload:
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(4096, 65536, size=n_slots, endpoint=True)
+    trie = np.concatenate([random_trie(rng, nodes) for _ in range(n_slots)])
+    return Workload("tree_verify", 32, 8, 128, ctx=ctx, q_rows=[nodes] * n_slots, n_layers=n_layers, seed=seed,
+                    trie=trie)
+
+
 CONFIGS = {
     "decode_small": decode_small,
     "decode_batch": decode_batch,
     "decode_long": decode_long,
     "prefill_chunk": prefill_chunk,
     "mtp_verify": mtp_verify,
+    "tree_verify": tree_verify,
 }
 
 

@@ -163,3 +163,55 @@ def test_attention_matches_dense_reference(oracle):
         p = np.exp(s - s.max(1, keepdims=True))
         ref = (p / p.sum(1, keepdims=True)) @ V
         assert np.abs(out[:, h] - ref).max() < 1e-5
+
+
+def test_tree_mask_of_a_chain_is_causal(oracle):
+    """A chain trie (node j's subtree = j .. n-1) lets row i see nodes 0 .. i, the causal rows."""
+    n = 9
+    chain = np.array([[j, n - 1] for j in range(n)], np.int32)
+    for i in range(n):
+        assert np.array_equal(np.nonzero(oracle.tree_visible(chain, i))[0], np.arange(i + 1))
+
+
+def test_random_trie_ranges_are_depth_first(oracle):
+    """Every generated trie: start_j = j, ranges nested or disjoint, and row i's visible nodes
+    form a root-to-i path (each one's range contains the next)."""
+    rng = np.random.default_rng(11)
+    for n in [1, 2, 5, 16, 64]:
+        r = W.random_trie(rng, n)
+        assert np.array_equal(r[:, 0], np.arange(n)) and (r[:, 1] >= r[:, 0]).all() and (r[:, 1] < n).all()
+        for a in range(n):
+            for b in range(a + 1, n):
+                inside = r[a, 0] <= b <= r[a, 1]
+                assert inside == (r[b, 1] <= r[a, 1]) or not inside and r[b, 0] > r[a, 1]
+        for i in range(n):
+            path = np.nonzero(oracle.tree_visible(r, i))[0]
+            assert path[0] == 0 and path[-1] == i
+            for x, y in zip(path[:-1], path[1:]):
+                assert r[x, 0] <= y <= r[x, 1]
+
+
+def test_tree_attention_chain_equals_causal(oracle):
+    """np_attn_tree with chain ranges equals the causal np_attn; a branching trie differs only
+    in the rows whose path skips a node."""
+    wl = W.Workload("t", 8, 2, 128, ctx=[40, 9], q_rows=[6, 9], seed=12)
+    desc = oracle.PoolDesc(1, wl.n_pages, 2, 128)
+    rng = np.random.default_rng(13)
+    n = int(wl.ctx.sum())
+    k = W.kv_rows_np(rng, n, 2, 128)
+    v = W.kv_rows_np(rng, n, 2, 128)
+    pool = np.zeros(desc.pool_bytes, np.uint8)
+    entry = np.repeat(np.arange(wl.batch), wl.ctx).astype(np.int32)
+    pos = np.concatenate([np.arange(c) for c in wl.ctx]).astype(np.int32)
+    oracle.np_kv_write_rows(desc, pool, 0, k, v, entry, pos, wl.block_table)
+    q = rng.standard_normal((int(wl.q_rows.sum()), 8, 128)).astype(np.float16)
+    chain = np.concatenate([[[j, t - 1] for j in range(t)] for t in wl.q_rows]).astype(np.int32)
+    causal = oracle.np_attn(desc, pool, 0, q, wl.cu_q, wl.cu_k, wl.block_table, 0.088)
+    tree = oracle.np_attn_tree(desc, pool, 0, q, wl.cu_q, wl.cu_k, wl.block_table, 0.088, chain)
+    assert np.abs(causal - tree).max() < 1e-6
+    # two branches under the root in the second entry: rows of the second branch skip the first
+    r = chain.copy()
+    r[6:] = [[0, 8], [1, 4], [2, 4], [3, 4], [4, 4], [5, 8], [6, 8], [7, 8], [8, 8]]
+    tree2 = oracle.np_attn_tree(desc, pool, 0, q, wl.cu_q, wl.cu_k, wl.block_table, 0.088, r)
+    assert np.abs(tree2[:11] - causal[:11]).max() < 1e-6
+    assert np.abs(tree2[11:] - causal[11:]).max() > 1e-3
