@@ -164,6 +164,34 @@ YF_API int yf_kv_append_paged_multi(yf_pool* pool, int32_t layer, const void* d_
                                     const uint32_t* d_block_table, int32_t max_blocks, int32_t batch,
                                     int32_t max_rows, void* stream);
 
+/* Fused attention prep + KV append: replaces attn_prepare_decode (RMSNorm of q
+ * and k with their own weights, partial RoPE, the gate half of the q projection
+ * split out; docs/research/2026-09-16-head-to-head-llamacpp-and-phase-profile.md:181-216)
+ * followed by yf_kv_append_paged_multi, in one launch.  Rows as in
+ * yf_kv_append_paged_multi (entry b: rows d_cu_rows[b].., positions
+ * d_start_pos[b] + i, which are also the RoPE positions).
+ * d_qg: f16 [total_rows, Hq, 2*D], per head the q half then the gate half;
+ * d_k, d_v: f16 [total_rows, Hkv, D]; d_q_norm_w, d_k_norm_w: f32 [D].
+ * q, k: y = x / sqrt(mean(x^2) + eps) * (w + norm_weight_offset) (offset 1 for
+ * zero-centred weights), then on dims [0, rope_dim) the rotate-half RoPE
+ * y'[i] = y[i] c - y[i+h] s, y'[i+h] = y[i+h] c + y[i] s, h = rope_dim/2,
+ * c = d_rope_cos[pos*h + i], s = d_rope_sin[pos*h + i] (f32 [rope_rows, h]).
+ * Outputs: d_q_out f16 [total_rows, Hq, D] (normed, rotated q), d_gate_out f16
+ * [total_rows, Hq, D] (the gate half as given); K (normed, rotated, rounded to
+ * f16) and V are quantized into the pool exactly as yf_kv_append_paged_multi
+ * would from those f16 rows.  Every float step is an IEEE round-to-nearest
+ * operation in a fixed order (the sum of squares per lane in dim order, then an
+ * xor butterfly over the 32 lanes of D/32 dims each, offsets 16..1).
+ * rope_dim: 0, or 2*(D/32)*2^k <= D.  Pointers 16-byte aligned.  A position
+ * outside [0, rope_rows) or the block table flags YF_DEV_BAD_POS and skips the row. */
+YF_API int yf_attn_prepare_append(yf_pool* pool, int32_t layer, int32_t n_q_heads, const void* d_qg,
+                                  const void* d_k, const void* d_v, const float* d_q_norm_w,
+                                  const float* d_k_norm_w, float eps, int32_t norm_weight_offset,
+                                  const float* d_rope_cos, const float* d_rope_sin, int32_t rope_dim,
+                                  int32_t rope_rows, const int32_t* d_cu_rows, const int32_t* d_start_pos,
+                                  const uint32_t* d_block_table, int32_t max_blocks, int32_t batch,
+                                  int32_t max_rows, void* d_q_out, void* d_gate_out, void* stream);
+
 /* ---- attention ---------------------------------------------------------------
  * Split-KV workspace for a call with these shapes (0 is a valid answer). */
 YF_API size_t yf_attn_workspace_size(const yf_pool* pool, int32_t n_q_heads, int32_t batch,

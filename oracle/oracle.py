@@ -303,6 +303,51 @@ def np_attn(desc: PoolDesc, pool: np.ndarray, layer: int, q: np.ndarray, cu_q, c
     return out
 
 
+def np_norm_rope(x: np.ndarray, w: np.ndarray, eps: float, w_offset: int, cos: np.ndarray, sin: np.ndarray,
+                 rope_dim: int, pos: np.ndarray) -> np.ndarray:
+    """The attention prep of attn_prepare_decode
+    (docs/research/2026-09-16-head-to-head-llamacpp-and-phase-profile.md:181-216) for rows
+    x f16 [rows, heads, D] at positions pos [rows]: RMSNorm with weights (w + w_offset), then the
+    rotate-half RoPE on dims [0, rope_dim) from the cos/sin tables [*, rope_dim/2].  float32,
+    every step rounded like the kernel's IEEE operations, the sum of squares in the kernel's order
+    (32 lanes of D/32 consecutive dims, each summed in dim order, then an xor butterfly over the
+    lanes with offsets 16, 8, 4, 2, 1)."""
+    f32 = np.float32
+    x = np.asarray(x, np.float16).astype(f32)
+    R, Hh, D = x.shape
+    E = D // 32
+    lanes = x.reshape(R, Hh, 32, E)
+    ss = np.zeros((R, Hh, 32), f32)
+    for e in range(E):
+        ss = (ss + lanes[..., e] * lanes[..., e]).astype(f32)
+    idx = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        ss = (ss + ss[..., idx ^ off]).astype(f32)
+    mean = (ss[..., 0] * f32(1.0 / D)).astype(f32)
+    r = (f32(1.0) / np.sqrt((mean + f32(eps)).astype(f32))).astype(f32)
+    wf = (np.asarray(w, f32) + f32(w_offset)).astype(f32)
+    y = ((x * r[..., None]).astype(f32) * wf).astype(f32)
+    if rope_dim:
+        h = rope_dim // 2
+        c = np.asarray(cos, f32)[pos][:, None, :]
+        s = np.asarray(sin, f32)[pos][:, None, :]
+        x1, x2 = y[..., :h].copy(), y[..., h:rope_dim].copy()
+        y[..., :h] = ((x1 * c).astype(f32) - (x2 * s).astype(f32)).astype(f32)
+        y[..., h:rope_dim] = ((x2 * c).astype(f32) + (x1 * s).astype(f32)).astype(f32)
+    return y
+
+
+def np_attn_prep(qg: np.ndarray, k: np.ndarray, wq, wk, eps: float, w_offset: int, cos, sin, rope_dim: int,
+                 pos: np.ndarray):
+    """q f16, gate f16 [rows, Hq, D] and the normed, rotated K rounded to f16 [rows, Hkv, D] (the
+    tensor the unfused path would hand to the KV append) of the fused attention prep."""
+    qg = np.asarray(qg, np.float16)
+    D = qg.shape[2] // 2
+    q = np_norm_rope(qg[..., :D], wq, eps, w_offset, cos, sin, rope_dim, pos).astype(np.float16)
+    kk = np_norm_rope(k, wk, eps, w_offset, cos, sin, rope_dim, pos).astype(np.float16)
+    return q, qg[..., D:].copy(), kk
+
+
 def tree_visible(ranges: np.ndarray, i: int) -> np.ndarray:
     """Draft nodes row i of a trie verify sees: node j with j <= i and start_j <= i <= end_j,
     ranges int [Tq, 2] of inclusive depth-first subtree ranges (the reference's trie mask

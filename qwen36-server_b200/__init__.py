@@ -7,6 +7,7 @@ package is the host-side mirror of the engine's operator surface
 from ._abi import YfError, lib  # noqa: F401
 from .paged_attn import (  # noqa: F401
     PagedKvPool,
+    attn_prepare_append,
     combine_partials,
     default_scale,
     dispatch_flash_decode_paged,

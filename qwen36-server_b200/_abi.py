@@ -73,6 +73,8 @@ SIGNATURES = {
     "yf_pool_status": (_ci, [_vp, ctypes.POINTER(_u32), _ci]),
     "yf_kv_append_paged": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
     "yf_kv_append_paged_multi": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "yf_attn_prepare_append": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _f32, _i32, _vp, _vp, _i32, _i32,
+                                     _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp]),
     "yf_attn_workspace_size": (_sz, [_vp, _i32, _i32, _i32, _i32]),
     "yf_attn_decode": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
     "yf_attn_decode_noalloc": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),

@@ -5,15 +5,13 @@
 // cited at docs/plans/2026-08-27-tiered-kv-cache.md:61-64 and
 // docs/plans/2026-08-27-mtp-cuda-graphs.md:132-134.
 //
-// One warp per (row, kv head).  Lane l owns dims [l*E, l*E+E) with E = D/32
-// (one 8- or 16-byte load of f16 per tensor); a Q8_0 group of 32 dims is
-// 32/E lanes, whose |x| maximum is a butterfly of xor-shuffles.  The rounding
-// is GGML's Q8_0 rule and is bit-exact with the oracle: d = amax/127 and
-// 1/d are IEEE divisions, q = roundf(x * (1/d)), d is stored as f16 (RNE).
-// K bytes land as one E-byte store per lane (contiguous in the tile layout);
-// V bytes and the scales are single stores into their permuted slots.
+// One warp per (row, kv head); the row's load, Q8_0 rounding and stores are
+// yf_q8row.cuh's (one 8- or 16-byte f16 load per lane and tensor; K bytes land
+// as one E-byte store per lane, V bytes and the scales as single stores into
+// their permuted slots).
 #include "yf_device.cuh"
 #include "yf_internal.h"
+#include "yf_q8row.cuh"
 
 namespace yf {
 
@@ -38,12 +36,7 @@ struct WriteParams {
 template <int D, int NB, int TPP, bool MULTI>
 __global__ void __launch_bounds__(kWriteWarps * 32) kv_write_kernel(const WriteParams p) {
     constexpr int E = D / 32;   // elements per lane
-    constexpr int G = D / NB;   // group size
-    constexpr int LPG = G / E;  // lanes per group
     constexpr int TB = 32 * D + 64 * NB;
-    constexpr int KS_OFF = 16 * D;
-    constexpr int V_OFF = 16 * D + 32 * NB;
-    constexpr int VS_OFF = 32 * D + 32 * NB;
     constexpr int P = TPP * 16;
 
     const int lane = threadIdx.x & 31;
@@ -73,77 +66,12 @@ __global__ void __launch_bounds__(kWriteWarps * 32) kv_write_kernel(const WriteP
     }
     uint8_t* tile = p.layer_base + ((size_t)page * p.H + h) * p.phb + ((pos % P) / 16) * TB;
     const int t = pos % 16;
-    const int d0 = lane * E;
-    const int grp = d0 / G;
 
 #pragma unroll
     for (int kv = 0; kv < 2; ++kv) {
-        const __half* src = (kv ? p.v : p.k) + ((size_t)row * p.H + h) * D + d0;
         float x[E];
-        if constexpr (E == 4) {
-            const uint2 w = *reinterpret_cast<const uint2*>(src);
-            const __half2 a = *reinterpret_cast<const __half2*>(&w.x);
-            const __half2 c = *reinterpret_cast<const __half2*>(&w.y);
-            x[0] = __low2float(a);
-            x[1] = __high2float(a);
-            x[2] = __low2float(c);
-            x[3] = __high2float(c);
-        } else {
-            const uint4 w = *reinterpret_cast<const uint4*>(src);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const __half2 a = *reinterpret_cast<const __half2*>(&ww[k]);
-                x[2 * k] = __low2float(a);
-                x[2 * k + 1] = __high2float(a);
-            }
-        }
-        float amax = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(x[e]));
-#pragma unroll
-        for (int off = 1; off < LPG; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const float d = __fdiv_rn(amax, 127.0f);
-        const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-        int8_t qv[E];
-#pragma unroll
-        for (int e = 0; e < E; ++e) qv[e] = (int8_t)(int)roundf(__fmul_rn(x[e], id));
-
-        if (kv == 0) {
-            // dims d0..d0+E-1 are contiguous bytes of one K word
-            const int b32 = d0 / 32, r = d0 % 32;
-            uint8_t* dst = tile + b32 * 512 + ((t % 8) * 4 + r / 8) * 16 + (t / 8) * 8 + r % 8;
-            if constexpr (E == 4) {
-                uint32_t w = 0;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) w |= (uint32_t)excess128(qv[e]) << (8 * e);
-                *reinterpret_cast<uint32_t*>(dst) = w;
-            } else {
-                uint2 w = make_uint2(0, 0);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    w.x |= (uint32_t)excess128(qv[e]) << (8 * e);
-                    w.y |= (uint32_t)excess128(qv[4 + e]) << (8 * e);
-                }
-                *reinterpret_cast<uint2*>(dst) = w;
-            }
-            if (lane % LPG == 0) {
-                const int off = KS_OFF + 2 * (((t % 8) * 2 + t / 8) * NB + grp);
-                *reinterpret_cast<__half*>(tile + off) = __float2half_rn(d);
-            }
-        } else {
-            const int tig = (t % 8) / 2, j = (t & 1) * 2 + t / 8;
-#pragma unroll
-            for (int e = 0; e < E; ++e) {
-                const int dim = d0 + e, m = dim / 16, ii = dim % 16;
-                tile[V_OFF + (m / 2) * 512 + ((ii % 8) * 4 + tig) * 16 + (m % 2) * 8 + (ii / 8) * 4 + j] =
-                    excess128(qv[e]);
-            }
-            if (lane % LPG == 0) {
-                const int off = VS_OFF + 2 * ((tig * NB + grp) * 4 + j);
-                *reinterpret_cast<__half*>(tile + off) = __float2half_rn(d);
-            }
-        }
+        load_f16_row<E>((kv ? p.v : p.k) + ((size_t)row * p.H + h) * D + lane * E, x);
+        q8_store_row<D, NB>(tile, t, kv, lane, x);
     }
 }
 

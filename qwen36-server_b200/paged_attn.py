@@ -215,6 +215,47 @@ def launch_append_multi(pool: PagedKvPool, layer: int, k: torch.Tensor, v: torch
 
 # ---- attention -----------------------------------------------------------------------
 
+def attn_prepare_append(pool: PagedKvPool, layer: int, qg: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                        q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, eps: float, rope_cos: Optional[torch.Tensor],
+                        rope_sin: Optional[torch.Tensor], rope_dim: int, cu_rows, start_pos, block_table,
+                        norm_weight_offset: int = 1, max_rows: Optional[int] = None,
+                        q_out: Optional[torch.Tensor] = None, gate_out: Optional[torch.Tensor] = None):
+    """The engine's attn_prepare_decode fused with the KV append
+    (docs/research/2026-09-16-head-to-head-llamacpp-and-phase-profile.md:181-216): q and k RMSNorm
+    (weights w + norm_weight_offset), rotate-half RoPE on the first rope_dim dims from the cos/sin
+    tables [rows, rope_dim/2], the gate half split out, and K/V written into the pool as Q8_0.
+    qg f16 [T, Hq, 2D] (q then gate per head), k/v f16 [T, Hkv, D]; returns (q, gate) f16
+    [T, Hq, D]."""
+    T, Hq, D2 = qg.shape
+    D = pool.head_dim
+    if qg.dtype != torch.float16 or D2 != 2 * D or not qg.is_contiguous():
+        raise YfError(_abi.YF_E_INVALID, "attn_prepare_append", "qg must be contiguous f16 [T, Hq, 2*head_dim]")
+    _check_rows(pool, k, v)
+    cu = _i32(cu_rows, pool.device)
+    start = _i32(start_pos, pool.device)
+    table = _i32(block_table, pool.device)
+    if max_rows is None:
+        max_rows = _max_len(cu_rows)
+    wq = q_norm_w.to(device=pool.device, dtype=torch.float32).contiguous()
+    wk = k_norm_w.to(device=pool.device, dtype=torch.float32).contiguous()
+    if rope_dim:
+        rc = rope_cos.to(device=pool.device, dtype=torch.float32).contiguous()
+        rs = rope_sin.to(device=pool.device, dtype=torch.float32).contiguous()
+        rows = rc.shape[0]
+    else:
+        rc = rs = None
+        rows = 0
+    if q_out is None:
+        q_out = torch.empty((T, Hq, D), dtype=torch.float16, device=qg.device)
+    if gate_out is None:
+        gate_out = torch.empty((T, Hq, D), dtype=torch.float16, device=qg.device)
+    call("yf_attn_prepare_append", pool.handle, layer, Hq, _ptr(qg), _ptr(k), _ptr(v), _ptr(wq), _ptr(wk),
+         ctypes.c_float(eps), int(norm_weight_offset), _ptr(rc), _ptr(rs), int(rope_dim), int(rows), _ptr(cu),
+         _ptr(start), _ptr(table), table.shape[1], cu.numel() - 1, int(max_rows), _ptr(q_out), _ptr(gate_out),
+         _stream(pool.device))
+    return q_out, gate_out
+
+
 def _max_len(cu) -> int:
     c = torch.as_tensor(cu).to("cpu", torch.int64)
     return int((c[1:] - c[:-1]).max()) if c.numel() > 1 else 0

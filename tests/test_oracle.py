@@ -215,3 +215,21 @@ def test_tree_attention_chain_equals_causal(oracle):
     tree2 = oracle.np_attn_tree(desc, pool, 0, q, wl.cu_q, wl.cu_k, wl.block_table, 0.088, r)
     assert np.abs(tree2[:11] - causal[:11]).max() < 1e-6
     assert np.abs(tree2[11:] - causal[11:]).max() > 1e-3
+
+
+def test_norm_rope_known_answers(oracle):
+    """RMSNorm of a constant row is (w + offset) * sign; RoPE with c = 1, s = 0 is the identity and
+    with c = 0, s = 1 maps (x1, x2) -> (-x2, x1) on the rotated dims only."""
+    D, R = 128, 32
+    x = np.full((1, 1, D), 3.0, np.float16)
+    w = np.linspace(-0.5, 0.5, D).astype(np.float32)
+    ones, zeros = np.ones((4, R // 2), np.float32), np.zeros((4, R // 2), np.float32)
+    y = oracle.np_norm_rope(x, w, 0.0, 1, ones, zeros, R, np.array([2]))
+    assert np.allclose(y[0, 0], 1.0 + w, atol=1e-6)
+    x = np.random.default_rng(3).standard_normal((1, 1, D)).astype(np.float16)
+    base = oracle.np_norm_rope(x, w, 1e-6, 0, ones, zeros, 0, np.array([0]))
+    assert np.array_equal(oracle.np_norm_rope(x, w, 1e-6, 0, ones, zeros, R, np.array([1])), base)
+    rot = oracle.np_norm_rope(x, w, 1e-6, 0, zeros, ones, R, np.array([1]))
+    assert np.array_equal(rot[..., :R // 2], -base[..., R // 2:R])
+    assert np.array_equal(rot[..., R // 2:R], base[..., :R // 2])
+    assert np.array_equal(rot[..., R:], base[..., R:])
