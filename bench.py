@@ -46,7 +46,8 @@ def peaks():
 
 def dominant_kernel(config: str) -> str:
     """The kernel that dominates one attention call of the workload."""
-    return "prefill_tc_kernel" if config == "prefill_chunk" else "decode_persistent_kernel"
+    return {"prefill_chunk": "prefill_tc_kernel", "tree_verify": "splitkv_kernel",
+            "attn_prep": "attn_prep_kernel"}.get(config, "decode_persistent_kernel")
 
 
 def profile_traffic(config: str):
@@ -546,7 +547,167 @@ def cpu_baseline(wl, seconds: float):
                                            "skipped branch nodes)" if wl.trie is not None else "")}
 
 
+def prep_arm(args, rank: int, world: int, local_rank: int):
+    """--config attn_prep: the fused attention prep + Q8_0 append (yf_attn_prepare_append) over
+    prefill_chunk's new rows (4 entries x 2048 rows at their 8192-token prefixes, Hq 32 x D 128,
+    Hkv 8, RoPE on the first 32 dims).  A step is one launch over all rows; HBM-bound: it reads
+    q|gate, k, v (f16) and writes q, gate (f16) and the rows' Q8_0 pool bytes."""
+    import torch
+    import torch.distributed as dist
+
+    yf = graft.load_package()
+    from qwen36_server_b200 import workloads as W
+
+    wl = W.prefill_chunk(seed=4 + 1000 * rank)
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    Hq, H, D, R = wl.n_q_heads, wl.n_kv_heads, wl.head_dim, 32
+    T = int(wl.q_rows.sum())
+    g = torch.Generator(device=dev)
+    g.manual_seed(17 + rank)
+    qg = torch.randn((T, Hq, 2 * D), generator=g, device=dev).half()
+    k = torch.randn((T, H, D), generator=g, device=dev).half()
+    v = torch.randn((T, H, D), generator=g, device=dev).half()
+    wq = (torch.randn(D, generator=g, device=dev) * 0.2).float()
+    wk = (torch.randn(D, generator=g, device=dev) * 0.2).float()
+    n_pos = int(wl.ctx.max())
+    inv = 1e7 ** (-torch.arange(0, R, 2, dtype=torch.float64) / R)
+    ang = torch.arange(n_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    cos, sin = ang.cos().float().to(dev), ang.sin().float().to(dev)
+    pool = yf.PagedKvPool(1, wl.n_pages, H, D, device=local_rank)
+    cu = torch.from_numpy(wl.cu_q).to(dev)
+    start = torch.from_numpy(wl.prefix.astype(np.int32)).to(dev)
+    bt = torch.from_numpy(wl.block_table).to(dev)
+    q_out = torch.empty((T, Hq, D), dtype=torch.float16, device=dev)
+    gate_out = torch.empty_like(q_out)
+    L = yf.lib()
+    P = ctypes.c_void_p
+    ptr = lambda t: P(t.data_ptr())  # noqa: E731
+    args_c = (pool.handle, 0, Hq, ptr(qg), ptr(k), ptr(v), ptr(wq), ptr(wk), ctypes.c_float(1e-6), 1, ptr(cos),
+              ptr(sin), R, n_pos, ptr(cu), ptr(start), ptr(bt), wl.max_blocks, wl.batch, int(wl.q_rows.max()),
+              ptr(q_out), ptr(gate_out), P(stream.cuda_stream))
+
+    def run():
+        if L.yf_attn_prepare_append(*args_c):
+            raise RuntimeError(L.yf_last_error().decode())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    alg = T * (Hq * 2 * D * 2 + 2 * H * D * 2 + 2 * Hq * D * 2) + T * wl.kv_bytes_per_token
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+        barrier()
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in evs:
+            a.record(stream)
+            run()
+            b.record(stream)
+        barrier()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        # end to end: the step's inputs from pinned host memory, q and gate back
+        pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
+        h_in = [(pin(t), t) for t in (qg, k, v)]
+        h_out = [(torch.empty(t.shape, dtype=t.dtype, pin_memory=True), t) for t in (q_out, gate_out)]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for h, d in h_in:
+                d.copy_(h, non_blocking=True)
+            run()
+            for h, d in h_out:
+                h.copy_(d, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        clk = clocks.stop()
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    hbm, _, peak_kind = peaks()
+    gbs = alg / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC + " (fused attention prep + KV append)", "value": T * world / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 norm/RoPE on f16 rows, Q8_0 KV", "data": "synthetic (seeded N(0,1) rows and weights)",
+        "config": {"workload": f"attn_prep: {T} new rows ({wl.batch} x {int(wl.q_rows[0])} at {int(wl.prefix[0])}"
+                               f"-token prefixes), Hq {Hq} x D {D}, Hkv {H}, rope_dim {R}",
+                   "l2": "inputs larger than L2", "parallelism": f"row-sharded x{world}, no collective",
+                   "launch": "direct C-ABI calls"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "traffic": profile_traffic("attn_prep"), "kernel": "attn_prep_kernel",
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
+                     "algorithmic_bytes_per_launch": alg, "launch_ms": ms},
+        "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h, _ in h_in),
+                "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h, _ in h_out), "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "device_status": pool.status(),
+    }
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        O = graft.load_oracle()
+        n = 256
+        rows = np.arange(n)
+        qh, kh = qg[:n].cpu().numpy(), k[:n].cpu().numpy()
+        c_np, s_np, wq_np, wk_np = cos.cpu().numpy(), sin.cpu().numpy(), wq.cpu().numpy(), wk.cpu().numpy()
+        pos = (wl.prefix[0] + rows).astype(np.int64)
+        O.np_attn_prep(qh, kh, wq_np, wk_np, 1e-6, 1, c_np, s_np, R, pos)
+        t0, reps = time.perf_counter(), 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 10.0):
+            O.np_attn_prep(qh, kh, wq_np, wk_np, 1e-6, 1, c_np, s_np, R, pos)
+            reps += 1
+        line["cpu_baseline"] = {"value": n * reps / (time.perf_counter() - t0), "unit": "tokens/s", "cores": 1,
+                                "kind": "port", "sample": f"{n} rows per call, oracle.np_attn_prep (numpy, "
+                                                          "norm + RoPE + gate split; the Q8_0 append not included)"}
+    pool.close()
+    return line
+
+
+def prep_reference_arm(args):
+    """--impl reference for attn_prep: the oracle's restatement of the prep (numpy, one thread) on
+    256 of the rows per step; the reference's candle path cannot be built here."""
+    from qwen36_server_b200 import workloads as W
+
+    O = graft.load_oracle()
+    wl = W.prefill_chunk(seed=4)
+    rng = np.random.default_rng(17)
+    n, Hq, H, D, R = 256, wl.n_q_heads, wl.n_kv_heads, wl.head_dim, 32
+    qg = rng.standard_normal((n, Hq, 2 * D)).astype(np.float16)
+    k = rng.standard_normal((n, H, D)).astype(np.float16)
+    w = (rng.standard_normal(D) * 0.2).astype(np.float32)
+    ang = np.arange(int(wl.ctx.max()))[:, None] * 1e7 ** (-np.arange(0, R, 2) / R)[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    pos = int(wl.prefix[0]) + np.arange(n)
+    for _ in range(args.warmup):
+        O.np_attn_prep(qg, k, w, w, 1e-6, 1, cos, sin, R, pos)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.np_attn_prep(qg, k, w, w, 1e-6, 1, cos, sin, R, pos)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = n / dt
+    return {
+        "impl": "reference", "metric": METRIC + " (fused attention prep + KV append)", "value": v,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (oracle)",
+        "data": "synthetic", "config": {"workload": f"attn_prep: {n} rows per step, Hq {Hq} x D {D}, Hkv {H}"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": f"{n} rows per step, oracle.np_attn_prep (norm + RoPE + gate split)"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
 def reference_arm(args):
+    if args.config == "attn_prep":
+        return prep_reference_arm(args)
     wl = make_workload(args.config, 0)
     samp = CpuSample(wl, max_tokens=int(args.ref_tokens))
     for _ in range(args.warmup):
@@ -576,7 +737,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="decode_batch",
                     choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify",
-                             "tree_verify"])
+                             "tree_verify", "attn_prep"])
     ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")
@@ -607,7 +768,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = gpu_arm(args, rank, world, local_rank)
+        line = (prep_arm if args.config == "attn_prep" else gpu_arm)(args, rank, world, local_rank)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
