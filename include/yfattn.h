@@ -297,6 +297,27 @@ YF_API int yf_pool_export_pages(yf_pool* pool, int32_t layer, int32_t n, const i
 YF_API int yf_pool_restore_pages(yf_pool* pool, int32_t layer, int32_t n, const int32_t* h_pages,
                                  const void* src, void* stream);
 
+/* ---- snapshot wire records ------------------------------------------------------
+ * The prefix cache's page records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:143-145,
+ * 237-251): one record per pool page, back to back at a stride of yf_pool_record_bytes,
+ *   [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload]
+ * little-endian, packed (20-byte header); payload = the page in every layer, layer 0 first
+ * (n_layers * yf_pool_page_head_bytes * n_kv_heads bytes); crc32c = CRC-32C (Castagnoli,
+ * reflected polynomial 0x82F63B78, preset and final xor 0xFFFFFFFF) of the payload. */
+YF_API size_t yf_pool_record_bytes(const yf_pool_desc* desc);
+/* Builds n records in device memory d_records (4-byte aligned) from pool pages d_pages[i], with
+ * the caller's d_chain_hashes[i] (the prefix chain fingerprint) and d_page_indices[i] (its
+ * position in the chain; null: the pool page id); the CRC is computed in the same pass as the
+ * copy.  Device arrays; a page id outside the pool flags YF_DEV_BAD_PAGE. */
+YF_API int yf_pool_export_records(yf_pool* pool, int32_t n, const int32_t* d_pages,
+                                  const uint64_t* d_chain_hashes, const uint32_t* d_page_indices,
+                                  void* d_records, void* stream);
+/* Checks the payload_len and CRC-32C of n records in device memory and copies each intact one
+ * into pool page d_pages[i] (every layer); d_ok[i] = 1 when restored, 0 when rejected (the page
+ * is then left as it was and the caller treats the context as a prefill). */
+YF_API int yf_pool_import_records(yf_pool* pool, int32_t n, const int32_t* d_pages, const void* d_records,
+                                  uint32_t* d_ok, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

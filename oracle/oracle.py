@@ -65,6 +65,8 @@ def lib() -> ctypes.CDLL:
         L.yfo_attn.restype = ci
         L.yfo_shuffled_pages.argtypes = [ctypes.c_uint32, ctypes.c_uint32, vp]
         L.yfo_shuffled_pages.restype = None
+        L.yfo_crc32c.argtypes = [vp, ctypes.c_size_t]
+        L.yfo_crc32c.restype = ctypes.c_uint32
         _lib = L
     return _lib
 
@@ -161,6 +163,30 @@ def c_read_kv(desc: PoolDesc, pool: np.ndarray, layer: int, page: int, head: int
     v = np.empty(desc.head_dim, np.float32)
     lib().yfo_read_kv(ctypes.byref(cd), _ptr(pool), layer, page, head, pos_in_page, _ptr(k), _ptr(v))
     return k, v
+
+
+def crc32c(data) -> int:
+    """CRC-32C (Castagnoli, reflected 0x82F63B78, preset and final xor 0xFFFFFFFF) through the
+    bitwise definition in yf_oracle.c."""
+    a = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else data,
+                             np.uint8)
+    return int(lib().yfo_crc32c(_ptr(a) if a.size else None, a.size))
+
+
+def page_records(desc: "PoolDesc", pool: np.ndarray, pages, chain_hashes, page_indices) -> np.ndarray:
+    """The prefix cache's page records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:237-251)
+    of pool-image pages: [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload],
+    little-endian, packed; payload = the page in every layer, layer 0 first."""
+    page_bytes = desc.page_head_bytes * desc.n_kv_heads
+    layer_bytes = desc.n_pages * page_bytes
+    out = []
+    for pg, hsh, idx in zip(pages, chain_hashes, page_indices):
+        payload = np.concatenate([pool[l * layer_bytes + int(pg) * page_bytes:
+                                       l * layer_bytes + (int(pg) + 1) * page_bytes] for l in range(desc.n_layers)])
+        head = np.array([int(hsh) & 0xFFFFFFFF, int(hsh) >> 32, int(idx), payload.size, crc32c(payload)],
+                        np.uint32)
+        out.append(np.concatenate([head.view(np.uint8), payload]))
+    return np.concatenate(out) if out else np.zeros(0, np.uint8)
 
 
 def shuffled_pages(count: int, seed: int = 0x9E3779B9) -> np.ndarray:

@@ -346,3 +346,16 @@ void yfo_shuffled_pages(uint32_t count, uint32_t seed, uint32_t* out) {
         out[j] = tmp;
     }
 }
+
+/* CRC-32C by its definition: the Castagnoli polynomial, bit-reflected (0x82F63B78), one input
+ * bit at a time, register preset and final xor 0xFFFFFFFF.  The check value of the ASCII digits
+ * "123456789" is 0xE3069283.  Used for the prefix cache's page records
+ * (docs/plans/2026-08-27-tiered-kv-cache.md:237-251: a CRC32C per page record). */
+uint32_t yfo_crc32c(const uint8_t* p, size_t n) {
+    uint32_t c = 0xFFFFFFFFu;
+    for (size_t i = 0; i < n; ++i) {
+        c ^= p[i];
+        for (int b = 0; b < 8; ++b) c = (c & 1u) ? (c >> 1) ^ 0x82F63B78u : c >> 1;
+    }
+    return c ^ 0xFFFFFFFFu;
+}

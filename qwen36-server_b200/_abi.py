@@ -85,6 +85,9 @@ SIGNATURES = {
     "yf_attn_decode_partial": (_ci, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _sz,
                                      _vp]),
     "yf_attn_combine": (_ci, [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _i32, _i32, _i32, _vp, _vp]),
+    "yf_pool_record_bytes": (_sz, [_vp]),
+    "yf_pool_export_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "yf_pool_import_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp]),
     "yf_pool_export_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "yf_pool_restore_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
 }

@@ -1,0 +1,248 @@
+// Snapshot wire records of pool pages, framed and checksummed on the GPU.
+//
+// The prefix cache's on-disk page format (docs/plans/2026-08-27-tiered-kv-cache.md:143-145,237-251):
+// append-only records [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload],
+// little-endian, packed, with a CRC-32C per page against media corruption.  Here a record's
+// payload is one pool page in every layer (layer 0 first), and the records are built and checked
+// where the pages live: the export kernel copies each page into its record and computes the CRC
+// in the same pass, the import kernel checks the CRC and restores only intact records, so the
+// host moves one contiguous, already framed buffer in either direction.
+//
+// CRC-32C: the Castagnoli polynomial, reflected (0x82F63B78), register preset and final xor
+// 0xFFFFFFFF.  A record is split into one chunk per thread; each thread runs the byte-table
+// (slicing-by-4) update over its chunk from a zero register, and the chunk results are joined
+// with the linearity of the CRC register: R(0, A||B) = R(0, A) * x^(8|B|) ^ R(0, B) mod P, the
+// product taken in the reflected representation (x^0 in bit 31), as zlib's crc32_combine does.
+#include <cuda_runtime.h>
+
+#include "yf_device.cuh"
+#include "yf_internal.h"
+
+namespace yf {
+namespace {
+
+constexpr uint32_t kCrcPoly = 0x82F63B78u;
+constexpr int kRecThreads = 256;
+constexpr int kRecHeader = 20;
+
+// a * b mod P (reflected; bit 31 = x^0), 32 fixed steps.
+__device__ __forceinline__ uint32_t gf2_mulmod(uint32_t a, uint32_t b) {
+    uint32_t p = 0;
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+        if (a & (0x80000000u >> i)) p ^= b;
+        b = (b & 1u) ? (b >> 1) ^ kCrcPoly : b >> 1;
+    }
+    return p;
+}
+
+// x^(8n) mod P from the table x2k[k] = x^(2^k) mod P.
+__device__ __forceinline__ uint32_t x8n_mod(unsigned long long n, const uint32_t* x2k) {
+    uint32_t p = 0x80000000u;  // x^0
+    n <<= 3;
+    for (int k = 0; n && k < 64; ++k, n >>= 1)
+        if (n & 1ull) p = gf2_mulmod(x2k[k & 31], p);
+    return p;
+}
+
+// The CTA's slicing-by-4 tables (T[0] is the byte table) and the x^(2^k) table, in shared memory.
+__device__ void build_tables(uint32_t (*T)[256], uint32_t* x2k) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        uint32_t c = (uint32_t)i;
+        for (int b = 0; b < 8; ++b) c = (c & 1u) ? (c >> 1) ^ kCrcPoly : c >> 1;
+        T[0][i] = c;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        uint32_t c = T[0][i];
+        for (int k = 1; k < 4; ++k) {
+            c = (c >> 8) ^ T[0][c & 0xffu];
+            T[k][i] = c;
+        }
+    }
+    if (threadIdx.x == 0) {
+        uint32_t p = 0x40000000u;  // x^1
+        for (int k = 0; k < 32; ++k) {
+            x2k[k] = p;
+            p = gf2_mulmod(p, p);
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ uint32_t crc_word(uint32_t c, uint32_t w, const uint32_t (*T)[256]) {
+    c ^= w;
+    return T[3][c & 0xffu] ^ T[2][(c >> 8) & 0xffu] ^ T[1][(c >> 16) & 0xffu] ^ T[0][c >> 24];
+}
+
+struct RecParams {
+    uint8_t* base;         // pool base (layer 0)
+    size_t layer_bytes;
+    size_t page_bytes;
+    int n_layers;
+    int n_pages;
+    const int32_t* pages;
+    const unsigned long long* hashes;
+    const uint32_t* page_index;
+    uint8_t* records;      // export: out; import: in
+    const uint8_t* records_in;
+    uint32_t* ok;
+    size_t rec_bytes;
+    uint32_t* status;
+};
+
+// The thread's 16-byte units of the payload: [u0, u1).
+__device__ __forceinline__ void chunk_of(size_t units, size_t& u0, size_t& u1) {
+    const size_t per = (units + kRecThreads - 1) / kRecThreads;
+    u0 = min(units, (size_t)threadIdx.x * per);
+    u1 = min(units, u0 + per);
+}
+
+// XOR of the threads' shifted chunk CRCs -> the payload's CRC-32C.
+__device__ uint32_t finish_crc(uint32_t raw_shifted, size_t payload, const uint32_t* x2k, uint32_t* red) {
+    uint32_t v = raw_shifted;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v ^= __shfl_xor_sync(0xffffffffu, v, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = 0;
+    for (int w = 0; w < kRecThreads / 32; ++w) r ^= red[w];
+    return gf2_mulmod(x8n_mod(payload, x2k), 0xFFFFFFFFu) ^ r ^ 0xFFFFFFFFu;
+}
+
+__global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecParams p) {
+    __shared__ uint32_t T[4][256];
+    __shared__ uint32_t x2k[32];
+    __shared__ uint32_t red[kRecThreads / 32];
+    build_tables(T, x2k);
+    const int r = blockIdx.x;
+    const int page = p.pages[r];
+    uint8_t* rec = p.records + (size_t)r * p.rec_bytes;
+    const size_t payload = (size_t)p.n_layers * p.page_bytes;
+    if (page < 0 || page >= p.n_pages) {  // refused on the host for host arrays; device arrays checked here
+        if (threadIdx.x == 0) atomicOr(p.status, YF_DEV_BAD_PAGE);
+        return;
+    }
+    const size_t units = payload / 16, upp = p.page_bytes / 16;
+    size_t u0, u1;
+    chunk_of(units, u0, u1);
+    uint32_t c = 0;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(rec + kRecHeader);
+    for (size_t u = u0; u < u1; ++u) {
+        const size_t l = u / upp, o = (u % upp) * 16;
+        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(p.base + l * p.layer_bytes + (size_t)page * p.page_bytes + o));
+        c = crc_word(c, w.x, T);
+        c = crc_word(c, w.y, T);
+        c = crc_word(c, w.z, T);
+        c = crc_word(c, w.w, T);
+        dst[u * 4 + 0] = w.x;
+        dst[u * 4 + 1] = w.y;
+        dst[u * 4 + 2] = w.z;
+        dst[u * 4 + 3] = w.w;
+    }
+    const uint32_t shifted = u1 > u0 ? gf2_mulmod(x8n_mod((units - u1) * 16, x2k), c) : 0u;
+    const uint32_t crc = finish_crc(shifted, payload, x2k, red);
+    if (threadIdx.x == 0) {
+        uint32_t* h = reinterpret_cast<uint32_t*>(rec);
+        const unsigned long long hash = p.hashes ? p.hashes[r] : 0ull;
+        h[0] = (uint32_t)hash;
+        h[1] = (uint32_t)(hash >> 32);
+        h[2] = p.page_index ? p.page_index[r] : (uint32_t)page;
+        h[3] = (uint32_t)payload;
+        h[4] = crc;
+    }
+}
+
+__global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecParams p) {
+    __shared__ uint32_t T[4][256];
+    __shared__ uint32_t x2k[32];
+    __shared__ uint32_t red[kRecThreads / 32];
+    __shared__ int s_good;
+    build_tables(T, x2k);
+    const int r = blockIdx.x;
+    const int page = p.pages[r];
+    const uint8_t* rec = p.records_in + (size_t)r * p.rec_bytes;
+    const size_t payload = (size_t)p.n_layers * p.page_bytes;
+    const uint32_t* h = reinterpret_cast<const uint32_t*>(rec);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(rec + kRecHeader);
+    const size_t units = payload / 16, upp = p.page_bytes / 16;
+    size_t u0, u1;
+    chunk_of(units, u0, u1);
+    uint32_t c = 0;
+    for (size_t u = u0; u < u1; ++u) {
+        c = crc_word(c, src[u * 4 + 0], T);
+        c = crc_word(c, src[u * 4 + 1], T);
+        c = crc_word(c, src[u * 4 + 2], T);
+        c = crc_word(c, src[u * 4 + 3], T);
+    }
+    const uint32_t shifted = u1 > u0 ? gf2_mulmod(x8n_mod((units - u1) * 16, x2k), c) : 0u;
+    const uint32_t crc = finish_crc(shifted, payload, x2k, red);
+    if (threadIdx.x == 0) {
+        const bool page_ok = page >= 0 && page < p.n_pages;
+        if (!page_ok) atomicOr(p.status, YF_DEV_BAD_PAGE);
+        s_good = page_ok && h[3] == (uint32_t)payload && h[4] == crc;
+        p.ok[r] = s_good ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_good) return;
+    for (size_t u = u0; u < u1; ++u) {
+        const size_t l = u / upp, o = (u % upp) * 16;
+        const uint4 w = make_uint4(src[u * 4 + 0], src[u * 4 + 1], src[u * 4 + 2], src[u * 4 + 3]);
+        *reinterpret_cast<uint4*>(p.base + l * p.layer_bytes + (size_t)page * p.page_bytes + o) = w;
+    }
+}
+
+int launch_records(yf_pool* pool, int32_t n, const int32_t* pages, const unsigned long long* hashes,
+                   const uint32_t* page_index, void* records, uint32_t* ok, bool do_export, void* stream) {
+    if (!pool) return fail(YF_E_INVALID, "pool is null");
+    if (!pool->base) return fail(YF_E_INVALID, "host-only pool has no device memory");
+    if (n < 0) return fail(YF_E_INVALID, "n %d < 0", n);
+    if (n == 0) return YF_OK;
+    if (!pages || !records || (!do_export && !ok)) return fail(YF_E_INVALID, "null device pointer");
+    if (!aligned(records, 4)) return fail(YF_E_INVALID, "records must be 4-byte aligned");
+    if (n > 0x7fffffff / 2) return fail(YF_E_UNSUPPORTED, "too many records");
+    RecParams p;
+    p.base = pool->base;
+    p.layer_bytes = pool->layer_bytes;
+    p.page_bytes = pool->page_bytes;
+    p.n_layers = pool->desc.n_layers;
+    p.n_pages = pool->desc.n_pages;
+    p.pages = pages;
+    p.hashes = hashes;
+    p.page_index = page_index;
+    p.records = static_cast<uint8_t*>(records);
+    p.records_in = static_cast<const uint8_t*>(records);
+    p.ok = ok;
+    p.rec_bytes = kRecHeader + (size_t)pool->desc.n_layers * pool->page_bytes;
+    p.status = pool->d_status;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (do_export)
+        export_records_kernel<<<n, kRecThreads, 0, s>>>(p);
+    else
+        import_records_kernel<<<n, kRecThreads, 0, s>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? YF_OK : cuda_fail(e, "snapshot record launch");
+}
+
+}  // namespace
+}  // namespace yf
+
+using namespace yf;
+
+extern "C" size_t yf_pool_record_bytes(const yf_pool_desc* desc) {
+    const size_t per_layer = yf_pool_page_head_bytes(desc) * (desc ? (size_t)desc->n_kv_heads : 0);
+    if (!per_layer) return 0;
+    return kRecHeader + (size_t)desc->n_layers * per_layer;
+}
+
+extern "C" int yf_pool_export_records(yf_pool* pool, int32_t n, const int32_t* d_pages,
+                                      const uint64_t* d_chain_hashes, const uint32_t* d_page_indices,
+                                      void* d_records, void* stream) {
+    return launch_records(pool, n, d_pages, reinterpret_cast<const unsigned long long*>(d_chain_hashes),
+                          d_page_indices, d_records, nullptr, true, stream);
+}
+
+extern "C" int yf_pool_import_records(yf_pool* pool, int32_t n, const int32_t* d_pages, const void* d_records,
+                                      uint32_t* d_ok, void* stream) {
+    return launch_records(pool, n, d_pages, nullptr, nullptr, const_cast<void*>(d_records), d_ok, false, stream);
+}

@@ -145,6 +145,36 @@ class PagedKvPool:
         call("yf_pool_restore_pages", self._h, layer, n, arr, ctypes.c_void_p(snapshot.data_ptr()),
              _stream(self.device))
 
+    # -- snapshot wire records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:237-251) ------
+    @property
+    def record_bytes(self) -> int:
+        """Bytes of one record: 20-byte header + the page in every layer."""
+        return lib().yf_pool_record_bytes(ctypes.byref(self.desc))
+
+    def export_records(self, pages, chain_hashes=None, page_indices=None,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Records [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload] of
+        ``pages`` back to back in a device uint8 tensor, the CRC-32C computed on the GPU."""
+        pg = _i32(pages, self.device)
+        n = pg.numel()
+        if out is None:
+            out = torch.empty(n * self.record_bytes, dtype=torch.uint8, device=self.device)
+        hs = None if chain_hashes is None else torch.as_tensor(chain_hashes, dtype=torch.int64).to(self.device)
+        pi = None if page_indices is None else _i32(page_indices, self.device)
+        call("yf_pool_export_records", self._h, n, _ptr(pg), _ptr(hs), _ptr(pi), _ptr(out), _stream(self.device))
+        return out
+
+    def import_records(self, pages, records: torch.Tensor) -> torch.Tensor:
+        """Restores the intact records of ``records`` (device) into ``pages``; returns the per-record
+        ok flags (uint32 1 / 0)."""
+        pg = _i32(pages, self.device)
+        n = pg.numel()
+        if records.numel() * records.element_size() < n * self.record_bytes:
+            raise YfError(_abi.YF_E_INVALID, "import_records", "records smaller than the page list")
+        ok = torch.zeros(n, dtype=torch.int32, device=self.device)
+        call("yf_pool_import_records", self._h, n, _ptr(pg), _ptr(records), _ptr(ok), _stream(self.device))
+        return ok
+
     # -- workspace ------------------------------------------------------------------
     def workspace_size(self, n_q_heads: int, batch: int, max_seqlen_q: int, max_seqlen_k: int) -> int:
         return lib().yf_attn_workspace_size(self._h, n_q_heads, batch, max_seqlen_q, max_seqlen_k)

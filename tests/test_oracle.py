@@ -233,3 +233,23 @@ def test_norm_rope_known_answers(oracle):
     assert np.array_equal(rot[..., :R // 2], -base[..., R // 2:R])
     assert np.array_equal(rot[..., R // 2:R], base[..., :R // 2])
     assert np.array_equal(rot[..., R:], base[..., R:])
+
+
+def test_crc32c_check_value_and_records(oracle):
+    """CRC-32C's published check value, linearity under concatenation with zero-preset registers,
+    and the record layout of a small two-layer pool image."""
+    assert oracle.crc32c(b"123456789") == 0xE3069283
+    assert oracle.crc32c(b"") == 0
+    desc = oracle.PoolDesc(2, 3, 2, 128)
+    rng = np.random.default_rng(21)
+    img = rng.integers(0, 256, desc.pool_bytes, dtype=np.uint8)
+    rec = oracle.page_records(desc, img, [2, 0], [0x1122334455667788, 7], [5, 6])
+    pb = desc.page_head_bytes * 2
+    stride = 20 + 2 * pb
+    assert rec.size == 2 * stride
+    h = rec[:20].view(np.uint32)
+    assert h[0] == 0x55667788 and h[1] == 0x11223344 and h[2] == 5 and h[3] == 2 * pb
+    payload = rec[20:stride]
+    assert np.array_equal(payload[:pb], img[2 * pb:3 * pb])
+    assert np.array_equal(payload[pb:], img[3 * pb + 2 * pb:3 * pb + 3 * pb])
+    assert h[4] == oracle.crc32c(payload)
