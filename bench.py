@@ -672,6 +672,122 @@ def prep_arm(args, rank: int, world: int, local_rank: int):
     return line
 
 
+def records_arm(args, rank: int, world: int, local_rank: int):
+    """--config snapshot_records: export to and import from the prefix cache's page records
+    (yf_pool_export_records / yf_pool_import_records, CRC-32C on the GPU) for prefill_chunk's
+    restored prefixes: 4 x 8192 tokens = 2048 16-token pages of one layer (71.3 MB of pages).
+    A step is one export plus one import of every page; a "token" is one prefix token moved."""
+    import torch
+    import torch.distributed as dist
+
+    yf = graft.load_package()
+    from qwen36_server_b200 import workloads as W
+
+    wl = W.prefill_chunk(seed=4 + 1000 * rank)
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    n = int(wl.prefix.sum()) // wl.page_size
+    src = yf.PagedKvPool(1, n, wl.n_kv_heads, wl.head_dim, device=local_rank)
+    dst = yf.PagedKvPool(1, n, wl.n_kv_heads, wl.head_dim, device=local_rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + rank)
+    view = src.layer_bytes_view(0)
+    view.copy_(torch.randint(0, 256, view.shape, generator=g, device=dev, dtype=torch.uint8))
+    pages = torch.randperm(n, generator=g, device=dev).int()
+    hashes = torch.arange(n, device=dev, dtype=torch.int64) * 0x9E3779B97F4A7C15 % (2 ** 62)
+    idx = torch.arange(n, device=dev, dtype=torch.int32)
+    rb = src.record_bytes
+    rec = torch.empty(n * rb, dtype=torch.uint8, device=dev)
+    ok = torch.zeros(n, dtype=torch.int32, device=dev)
+    L = yf.lib()
+    P = ctypes.c_void_p
+    ptr = lambda t: P(t.data_ptr())  # noqa: E731
+    s = P(stream.cuda_stream)
+
+    def run():
+        if L.yf_pool_export_records(src.handle, n, ptr(pages), ptr(hashes), ptr(idx), ptr(rec), s):
+            raise RuntimeError(L.yf_last_error().decode())
+        if L.yf_pool_import_records(dst.handle, n, ptr(pages), ptr(rec), ptr(ok), s):
+            raise RuntimeError(L.yf_last_error().decode())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    alg = 2 * (n * src.page_bytes + n * rb)  # each direction reads and writes the bytes once
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+        barrier()
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in evs:
+            a.record(stream)
+            run()
+            b.record(stream)
+        barrier()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        # end to end: the records go to pinned host memory and back (the disk tier's buffers)
+        h = torch.empty(rec.shape, dtype=torch.uint8, pin_memory=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            if L.yf_pool_export_records(src.handle, n, ptr(pages), ptr(hashes), ptr(idx), ptr(rec), s):
+                raise RuntimeError(L.yf_last_error().decode())
+            h.copy_(rec, non_blocking=True)
+            rec.copy_(h, non_blocking=True)
+            if L.yf_pool_import_records(dst.handle, n, ptr(pages), ptr(rec), ptr(ok), s):
+                raise RuntimeError(L.yf_last_error().decode())
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        clk = clocks.stop()
+    good = int(ok.sum().item())
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    hbm, _, peak_kind = peaks()
+    gbs = alg / (ms * 1e-3) / 1e9
+    tokens = n * wl.page_size
+    line = {
+        "metric": METRIC + " (prefix snapshot records: export + import)", "value": tokens * world / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 (bytes, CRC-32C)",
+        "data": "synthetic (random pool bytes)",
+        "config": {"workload": f"snapshot_records: {n} pages x {src.page_bytes} B (4 x {int(wl.prefix[0])} prefix "
+                               f"tokens, Hkv {wl.n_kv_heads} x D {wl.head_dim}, 1 layer), records of {rb} B",
+                   "records_intact": f"{good} of {n}", "parallelism": f"x{world} independent pools, no collective",
+                   "launch": "direct C-ABI calls"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "traffic": None, "kernel": "export_records_kernel + import_records_kernel",
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
+                     "algorithmic_bytes_per_launch": alg, "launch_ms": ms},
+        "e2e": {"value": tokens * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": rec.numel(),
+                "d2h_bytes_per_step": rec.numel(), "ms_per_step": e2e_ms},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+        "device_status": src.status() | dst.status(),
+    }
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        O = graft.load_oracle()
+        sample = rec[: 8 * rb].cpu().numpy()
+        t0, reps = time.perf_counter(), 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 10.0):
+            for r in range(8):
+                O.crc32c(sample[r * rb + 20:(r + 1) * rb])
+            reps += 1
+        line["cpu_baseline"] = {"value": 8 * reps * wl.page_size / (time.perf_counter() - t0), "unit": "tokens/s",
+                                "cores": 1, "kind": "port", "sample": "8 records per pass, the oracle's bitwise "
+                                                                      "CRC-32C of each payload (the copy not included)"}
+    src.close()
+    dst.close()
+    return line
+
+
 def prep_reference_arm(args):
     """--impl reference for attn_prep: the oracle's restatement of the prep (numpy, one thread) on
     256 of the rows per step; the reference's candle path cannot be built here."""
@@ -708,6 +824,10 @@ def prep_reference_arm(args):
 def reference_arm(args):
     if args.config == "attn_prep":
         return prep_reference_arm(args)
+    if args.config == "snapshot_records":
+        return {"impl": "reference", "unavailable": "the prefix cache's record writer lives in the un-vendored Rust "
+                                                    "fork (no Rust toolchain here); bench.py --config snapshot_records "
+                                                    "reports the oracle's CRC-32C as its cpu_baseline"}
     wl = make_workload(args.config, 0)
     samp = CpuSample(wl, max_tokens=int(args.ref_tokens))
     for _ in range(args.warmup):
@@ -737,7 +857,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="decode_batch",
                     choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify",
-                             "tree_verify", "attn_prep"])
+                             "tree_verify", "attn_prep", "snapshot_records"])
     ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")
@@ -768,7 +888,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = (prep_arm if args.config == "attn_prep" else gpu_arm)(args, rank, world, local_rank)
+        arm = {"attn_prep": prep_arm, "snapshot_records": records_arm}.get(args.config, gpu_arm)
+        line = arm(args, rank, world, local_rank)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

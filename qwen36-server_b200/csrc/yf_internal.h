@@ -61,6 +61,8 @@ struct yf_pool {
     int sm_count = 148;
     std::vector<int32_t> refcount;
     std::vector<int32_t> free_stack;  // LIFO of free page ids
+    // CRC-32C combine operators of this pool's snapshot records (computed at the first record call)
+    std::vector<uint32_t> crc_ops;
 };
 
 namespace yf {

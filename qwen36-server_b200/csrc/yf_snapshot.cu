@@ -15,6 +15,8 @@
 // product taken in the reflected representation (x^0 in bit 31), as zlib's crc32_combine does.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "yf_device.cuh"
 #include "yf_internal.h"
 
@@ -26,7 +28,7 @@ constexpr int kRecThreads = 256;
 constexpr int kRecHeader = 20;
 
 // a * b mod P (reflected; bit 31 = x^0), 32 fixed steps.
-__device__ __forceinline__ uint32_t gf2_mulmod(uint32_t a, uint32_t b) {
+__host__ __device__ __forceinline__ uint32_t gf2_mulmod(uint32_t a, uint32_t b) {
     uint32_t p = 0;
 #pragma unroll 4
     for (int i = 0; i < 32; ++i) {
@@ -36,17 +38,19 @@ __device__ __forceinline__ uint32_t gf2_mulmod(uint32_t a, uint32_t b) {
     return p;
 }
 
-// x^(8n) mod P from the table x2k[k] = x^(2^k) mod P.
-__device__ __forceinline__ uint32_t x8n_mod(unsigned long long n, const uint32_t* x2k) {
-    uint32_t p = 0x80000000u;  // x^0
-    n <<= 3;
-    for (int k = 0; n && k < 64; ++k, n >>= 1)
-        if (n & 1ull) p = gf2_mulmod(x2k[k & 31], p);
+// x^(8n) mod P (n < 2^29), by squaring.
+__host__ uint32_t x8n_mod(unsigned long long n) {
+    uint32_t x2k = 0x40000000u;  // x^(2^k), from x^1
+    uint32_t p = 0x80000000u;    // x^0
+    for (n <<= 3; n; n >>= 1) {
+        if (n & 1ull) p = gf2_mulmod(x2k, p);
+        x2k = gf2_mulmod(x2k, x2k);
+    }
     return p;
 }
 
-// The CTA's slicing-by-4 tables (T[0] is the byte table) and the x^(2^k) table, in shared memory.
-__device__ void build_tables(uint32_t (*T)[256], uint32_t* x2k) {
+// The CTA's slicing-by-4 tables in shared memory (T[0] is the byte table).
+__device__ void build_tables(uint32_t (*T)[256]) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
         uint32_t c = (uint32_t)i;
         for (int b = 0; b < 8; ++b) c = (c & 1u) ? (c >> 1) ^ kCrcPoly : c >> 1;
@@ -58,13 +62,6 @@ __device__ void build_tables(uint32_t (*T)[256], uint32_t* x2k) {
         for (int k = 1; k < 4; ++k) {
             c = (c >> 8) ^ T[0][c & 0xffu];
             T[k][i] = c;
-        }
-    }
-    if (threadIdx.x == 0) {
-        uint32_t p = 0x40000000u;  // x^1
-        for (int k = 0; k < 32; ++k) {
-            x2k[k] = p;
-            p = gf2_mulmod(p, p);
         }
     }
     __syncthreads();
@@ -89,6 +86,10 @@ struct RecParams {
     uint32_t* ok;
     size_t rec_bytes;
     uint32_t* status;
+    // x^(8 * bytes after thread t's chunk) mod P for every thread, and the preset's term
+    // 0xFFFFFFFF * x^(8 * payload) mod P: the chunk CRCs combine with one product each
+    uint32_t shift[kRecThreads];
+    uint32_t preset;
 };
 
 // The thread's 16-byte units of the payload: [u0, u1).
@@ -99,7 +100,7 @@ __device__ __forceinline__ void chunk_of(size_t units, size_t& u0, size_t& u1) {
 }
 
 // XOR of the threads' shifted chunk CRCs -> the payload's CRC-32C.
-__device__ uint32_t finish_crc(uint32_t raw_shifted, size_t payload, const uint32_t* x2k, uint32_t* red) {
+__device__ uint32_t finish_crc(uint32_t raw_shifted, uint32_t preset, uint32_t* red) {
     uint32_t v = raw_shifted;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v ^= __shfl_xor_sync(0xffffffffu, v, off);
@@ -107,14 +108,13 @@ __device__ uint32_t finish_crc(uint32_t raw_shifted, size_t payload, const uint3
     __syncthreads();
     uint32_t r = 0;
     for (int w = 0; w < kRecThreads / 32; ++w) r ^= red[w];
-    return gf2_mulmod(x8n_mod(payload, x2k), 0xFFFFFFFFu) ^ r ^ 0xFFFFFFFFu;
+    return preset ^ r ^ 0xFFFFFFFFu;
 }
 
 __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecParams p) {
     __shared__ uint32_t T[4][256];
-    __shared__ uint32_t x2k[32];
     __shared__ uint32_t red[kRecThreads / 32];
-    build_tables(T, x2k);
+    build_tables(T);
     const int r = blockIdx.x;
     const int page = p.pages[r];
     uint8_t* rec = p.records + (size_t)r * p.rec_bytes;
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecPa
     uint32_t* dst = reinterpret_cast<uint32_t*>(rec + kRecHeader);
     for (size_t u = u0; u < u1; ++u) {
         const size_t l = u / upp, o = (u % upp) * 16;
-        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(p.base + l * p.layer_bytes + (size_t)page * p.page_bytes + o));
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.base + l * p.layer_bytes + (size_t)page * p.page_bytes + o));
         c = crc_word(c, w.x, T);
         c = crc_word(c, w.y, T);
         c = crc_word(c, w.z, T);
@@ -140,8 +140,8 @@ __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecPa
         dst[u * 4 + 2] = w.z;
         dst[u * 4 + 3] = w.w;
     }
-    const uint32_t shifted = u1 > u0 ? gf2_mulmod(x8n_mod((units - u1) * 16, x2k), c) : 0u;
-    const uint32_t crc = finish_crc(shifted, payload, x2k, red);
+    const uint32_t shifted = u1 > u0 ? gf2_mulmod(p.shift[threadIdx.x], c) : 0u;
+    const uint32_t crc = finish_crc(shifted, p.preset, red);
     if (threadIdx.x == 0) {
         uint32_t* h = reinterpret_cast<uint32_t*>(rec);
         const unsigned long long hash = p.hashes ? p.hashes[r] : 0ull;
@@ -155,10 +155,9 @@ __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecPa
 
 __global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecParams p) {
     __shared__ uint32_t T[4][256];
-    __shared__ uint32_t x2k[32];
     __shared__ uint32_t red[kRecThreads / 32];
     __shared__ int s_good;
-    build_tables(T, x2k);
+    build_tables(T);
     const int r = blockIdx.x;
     const int page = p.pages[r];
     const uint8_t* rec = p.records_in + (size_t)r * p.rec_bytes;
@@ -175,8 +174,8 @@ __global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecPa
         c = crc_word(c, src[u * 4 + 2], T);
         c = crc_word(c, src[u * 4 + 3], T);
     }
-    const uint32_t shifted = u1 > u0 ? gf2_mulmod(x8n_mod((units - u1) * 16, x2k), c) : 0u;
-    const uint32_t crc = finish_crc(shifted, payload, x2k, red);
+    const uint32_t shifted = u1 > u0 ? gf2_mulmod(p.shift[threadIdx.x], c) : 0u;
+    const uint32_t crc = finish_crc(shifted, p.preset, red);
     if (threadIdx.x == 0) {
         const bool page_ok = page >= 0 && page < p.n_pages;
         if (!page_ok) atomicOr(p.status, YF_DEV_BAD_PAGE);
@@ -215,6 +214,20 @@ int launch_records(yf_pool* pool, int32_t n, const int32_t* pages, const unsigne
     p.ok = ok;
     p.rec_bytes = kRecHeader + (size_t)pool->desc.n_layers * pool->page_bytes;
     p.status = pool->d_status;
+    const size_t payload = p.rec_bytes - kRecHeader, units = payload / 16;
+    if (payload >= (1ull << 29)) return fail(YF_E_UNSUPPORTED, "record payload of %zu bytes", payload);
+    if (pool->crc_ops.size() != kRecThreads + 1) {  // the record shape is fixed per pool: once
+        std::vector<uint32_t> ops(kRecThreads + 1);
+        const size_t per = (units + kRecThreads - 1) / kRecThreads;
+        for (int t = 0; t < kRecThreads; ++t) {
+            const size_t u1 = std::min(units, (size_t)t * per + per);
+            ops[t] = x8n_mod((units - u1) * 16);
+        }
+        ops[kRecThreads] = gf2_mulmod(x8n_mod(payload), 0xFFFFFFFFu);
+        pool->crc_ops.swap(ops);
+    }
+    for (int t = 0; t < kRecThreads; ++t) p.shift[t] = pool->crc_ops[t];
+    p.preset = pool->crc_ops[kRecThreads];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (do_export)
         export_records_kernel<<<n, kRecThreads, 0, s>>>(p);
