@@ -47,7 +47,7 @@ def peaks():
 def dominant_kernel(config: str) -> str:
     """The kernel that dominates one attention call of the workload."""
     return {"prefill_chunk": "prefill_tc_kernel", "tree_verify": "splitkv_kernel",
-            "attn_prep": "attn_prep_kernel"}.get(config, "decode_persistent_kernel")
+            "attn_prep": "attn_prep_kernel", "snapshot_records": "records_kernel"}.get(config, "decode_persistent_kernel")
 
 
 def profile_traffic(config: str):
@@ -763,7 +763,7 @@ def records_arm(args, rank: int, world: int, local_rank: int):
                    "records_intact": f"{good} of {n}", "parallelism": f"x{world} independent pools, no collective",
                    "launch": "direct C-ABI calls"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                     "traffic": None, "kernel": "export_records_kernel + import_records_kernel",
+                     "traffic": profile_traffic("snapshot_records"), "kernel": "export_records_kernel + import_records_kernel",
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
                      "algorithmic_bytes_per_launch": alg, "launch_ms": ms},
         "e2e": {"value": tokens * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": rec.numel(),
