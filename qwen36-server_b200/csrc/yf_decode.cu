@@ -1175,7 +1175,11 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
                 occ_val[dev] = occ;
             }
         }
-        const int ctas = std::max(1, std::min(plan.persistent_ctas, occ * a.pool->sm_count));
+        int ctas = std::max(1, std::min(plan.persistent_ctas, occ * a.pool->sm_count));
+        // a few units over many CTAs: a multiple of the unit count puts the boundaries of
+        // equal-length units on CTA boundaries (no CTA switches units and joins two merges)
+        const long long units = (long long)a.batch * a.pool->desc.n_kv_heads * plan.n_row_groups;
+        if (units > 1 && ctas >= 16 * units) ctas -= (int)(ctas % units);
         kern<<<ctas, kThreads, smem, a.stream>>>(p);
         e = cudaGetLastError();
         return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_persistent launch");

@@ -96,6 +96,10 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
         const long long by_work = (units * tiles + 15) / 16;
         long long ctas = (long long)pool->sm_count * kMaxCtasPerSm;
         if (by_work < ctas) ctas = by_work > 0 ? by_work : 1;
+        // few long units: more than ~128 parts per unit only lengthens the merge once ~1.75 CTAs
+        // per SM keep HBM busy (the 131072-key, 2-head decode: 42 us at 444 CTAs, 39 at 256)
+        const long long by_units = std::max((long long)pool->sm_count * 7 / 4, units * 128);
+        if (by_units < ctas) ctas = by_units;
         if (2 * ctas > kMaxGroupCounters) ctas = kMaxGroupCounters / 2;
         p.persistent_ctas = (int)ctas;
         p.ws_bytes = (size_t)p.persistent_ctas * 2 * row_bytes;  // two partial slots per CTA
