@@ -9,10 +9,11 @@
 // host moves one contiguous, already framed buffer in either direction.
 //
 // CRC-32C: the Castagnoli polynomial, reflected (0x82F63B78), register preset and final xor
-// 0xFFFFFFFF.  A record is split into one chunk per thread; each thread runs the byte-table
-// (slicing-by-4) update over its chunk from a zero register, and the chunk results are joined
-// with the linearity of the CRC register: R(0, A||B) = R(0, A) * x^(8|B|) ^ R(0, B) mod P, the
-// product taken in the reflected representation (x^0 in bit 31), as zlib's crc32_combine does.
+// 0xFFFFFFFF.  A record's payload moves through shared memory in blocks of <= 32 KB (coalesced
+// loads and stores); each thread runs the byte-table (slicing-by-4) update over a contiguous run
+// of the staged words from a zero register, and the runs and then the blocks are joined with the
+// linearity of the CRC register: R(0, A||B) = R(0, A) * x^(8|B|) ^ R(0, B) mod P, the product
+// taken in the reflected representation (x^0 in bit 31), as zlib's crc32_combine does.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -86,62 +87,70 @@ struct RecParams {
     uint32_t* ok;
     size_t rec_bytes;
     uint32_t* status;
-    // x^(8 * bytes after thread t's chunk) mod P for every thread, and the preset's term
-    // 0xFFFFFFFF * x^(8 * payload) mod P: the chunk CRCs combine with one product each
+    int blk_words;         // words of one staged block (a page is 2^j blocks)
+    int blks_per_page;
+    // x^(8 * bytes of the block after thread t's words) mod P, x^(8 * block bytes) mod P, and the
+    // preset's term 0xFFFFFFFF * x^(8 * payload) mod P
     uint32_t shift[kRecThreads];
+    uint32_t blk_shift;
     uint32_t preset;
 };
 
-// The thread's 16-byte units of the payload: [u0, u1).
-__device__ __forceinline__ void chunk_of(size_t units, size_t& u0, size_t& u1) {
-    const size_t per = (units + kRecThreads - 1) / kRecThreads;
-    u0 = min(units, (size_t)threadIdx.x * per);
-    u1 = min(units, u0 + per);
+constexpr int kBlkMaxBytes = 32768;
+
+// Thread t's words of a staged block: [w0, w1), contiguous, in thread order.
+__device__ __forceinline__ void words_of(int n, int& w0, int& w1) {
+    w0 = (int)((long long)threadIdx.x * n / kRecThreads);
+    w1 = (int)((long long)(threadIdx.x + 1) * n / kRecThreads);
 }
 
-// XOR of the threads' shifted chunk CRCs -> the payload's CRC-32C.
-__device__ uint32_t finish_crc(uint32_t raw_shifted, uint32_t preset, uint32_t* red) {
-    uint32_t v = raw_shifted;
+// The block's CRC register from a zero preset (the staged words), joined across the threads.
+__device__ uint32_t block_crc(const uint32_t* blk, int n, uint32_t shift, const uint32_t (*T)[256], uint32_t* red) {
+    int w0, w1;
+    words_of(n, w0, w1);
+    uint32_t c = 0;
+    for (int w = w0; w < w1; ++w) c = crc_word(c, blk[w], T);
+    uint32_t v = w1 > w0 ? gf2_mulmod(shift, c) : 0u;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v ^= __shfl_xor_sync(0xffffffffu, v, off);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     uint32_t r = 0;
-    for (int w = 0; w < kRecThreads / 32; ++w) r ^= red[w];
-    return preset ^ r ^ 0xFFFFFFFFu;
+    for (int k = 0; k < kRecThreads / 32; ++k) r ^= red[k];
+    __syncthreads();  // red and the staged block are reused by the next block
+    return r;
 }
 
+// One CTA per record: the page's blocks (every layer) are staged through shared memory with
+// coalesced loads and stores, and each thread checksums a contiguous run of the staged words.
 __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecParams p) {
     __shared__ uint32_t T[4][256];
     __shared__ uint32_t red[kRecThreads / 32];
+    __shared__ __align__(16) uint32_t blk[kBlkMaxBytes / 4];
     build_tables(T);
     const int r = blockIdx.x;
     const int page = p.pages[r];
     uint8_t* rec = p.records + (size_t)r * p.rec_bytes;
     const size_t payload = (size_t)p.n_layers * p.page_bytes;
-    if (page < 0 || page >= p.n_pages) {  // refused on the host for host arrays; device arrays checked here
+    if (page < 0 || page >= p.n_pages) {
         if (threadIdx.x == 0) atomicOr(p.status, YF_DEV_BAD_PAGE);
         return;
     }
-    const size_t units = payload / 16, upp = p.page_bytes / 16;
-    size_t u0, u1;
-    chunk_of(units, u0, u1);
-    uint32_t c = 0;
+    const int nw = p.blk_words;
     uint32_t* dst = reinterpret_cast<uint32_t*>(rec + kRecHeader);
-    for (size_t u = u0; u < u1; ++u) {
-        const size_t l = u / upp, o = (u % upp) * 16;
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.base + l * p.layer_bytes + (size_t)page * p.page_bytes + o));
-        c = crc_word(c, w.x, T);
-        c = crc_word(c, w.y, T);
-        c = crc_word(c, w.z, T);
-        c = crc_word(c, w.w, T);
-        dst[u * 4 + 0] = w.x;
-        dst[u * 4 + 1] = w.y;
-        dst[u * 4 + 2] = w.z;
-        dst[u * 4 + 3] = w.w;
+    uint32_t acc = 0;  // the payload's CRC register from a zero preset, over the blocks so far
+    for (int l = 0; l < p.n_layers; ++l) {
+        const uint8_t* pg = p.base + (size_t)l * p.layer_bytes + (size_t)page * p.page_bytes;
+        for (int bi = 0; bi < p.blks_per_page; ++bi) {
+            const uint4* g = reinterpret_cast<const uint4*>(pg + (size_t)bi * nw * 4);
+            for (int k = threadIdx.x; k < nw / 4; k += kRecThreads) reinterpret_cast<uint4*>(blk)[k] = __ldcs(g + k);
+            __syncthreads();
+            uint32_t* d = dst + ((size_t)l * p.blks_per_page + bi) * nw;
+            for (int k = threadIdx.x; k < nw; k += kRecThreads) d[k] = blk[k];
+            const uint32_t b = block_crc(blk, nw, p.shift[threadIdx.x], T, red);
+            acc = gf2_mulmod(p.blk_shift, acc) ^ b;
+        }
     }
-    const uint32_t shifted = u1 > u0 ? gf2_mulmod(p.shift[threadIdx.x], c) : 0u;
-    const uint32_t crc = finish_crc(shifted, p.preset, red);
     if (threadIdx.x == 0) {
         uint32_t* h = reinterpret_cast<uint32_t*>(rec);
         const unsigned long long hash = p.hashes ? p.hashes[r] : 0ull;
@@ -149,13 +158,14 @@ __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecPa
         h[1] = (uint32_t)(hash >> 32);
         h[2] = p.page_index ? p.page_index[r] : (uint32_t)page;
         h[3] = (uint32_t)payload;
-        h[4] = crc;
+        h[4] = p.preset ^ acc ^ 0xFFFFFFFFu;
     }
 }
 
 __global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecParams p) {
     __shared__ uint32_t T[4][256];
     __shared__ uint32_t red[kRecThreads / 32];
+    __shared__ __align__(16) uint32_t blk[kBlkMaxBytes / 4];
     __shared__ int s_good;
     build_tables(T);
     const int r = blockIdx.x;
@@ -164,30 +174,31 @@ __global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecPa
     const size_t payload = (size_t)p.n_layers * p.page_bytes;
     const uint32_t* h = reinterpret_cast<const uint32_t*>(rec);
     const uint32_t* src = reinterpret_cast<const uint32_t*>(rec + kRecHeader);
-    const size_t units = payload / 16, upp = p.page_bytes / 16;
-    size_t u0, u1;
-    chunk_of(units, u0, u1);
-    uint32_t c = 0;
-    for (size_t u = u0; u < u1; ++u) {
-        c = crc_word(c, src[u * 4 + 0], T);
-        c = crc_word(c, src[u * 4 + 1], T);
-        c = crc_word(c, src[u * 4 + 2], T);
-        c = crc_word(c, src[u * 4 + 3], T);
+    const int nw = p.blk_words;
+    const int n_blk = p.n_layers * p.blks_per_page;
+    uint32_t acc = 0;
+    for (int bi = 0; bi < n_blk; ++bi) {
+        const uint32_t* s = src + (size_t)bi * nw;
+        for (int k = threadIdx.x; k < nw; k += kRecThreads) blk[k] = __ldcg(s + k);
+        __syncthreads();
+        const uint32_t b = block_crc(blk, nw, p.shift[threadIdx.x], T, red);
+        acc = gf2_mulmod(p.blk_shift, acc) ^ b;
     }
-    const uint32_t shifted = u1 > u0 ? gf2_mulmod(p.shift[threadIdx.x], c) : 0u;
-    const uint32_t crc = finish_crc(shifted, p.preset, red);
     if (threadIdx.x == 0) {
         const bool page_ok = page >= 0 && page < p.n_pages;
         if (!page_ok) atomicOr(p.status, YF_DEV_BAD_PAGE);
-        s_good = page_ok && h[3] == (uint32_t)payload && h[4] == crc;
+        s_good = page_ok && h[3] == (uint32_t)payload && h[4] == (p.preset ^ acc ^ 0xFFFFFFFFu);
         p.ok[r] = s_good ? 1u : 0u;
     }
     __syncthreads();
     if (!s_good) return;
-    for (size_t u = u0; u < u1; ++u) {
-        const size_t l = u / upp, o = (u % upp) * 16;
-        const uint4 w = make_uint4(src[u * 4 + 0], src[u * 4 + 1], src[u * 4 + 2], src[u * 4 + 3]);
-        *reinterpret_cast<uint4*>(p.base + l * p.layer_bytes + (size_t)page * p.page_bytes + o) = w;
+    // second pass: the intact payload into the page, 4-byte loads (the record is only 4-byte
+    // aligned) and 16-byte stores
+    for (int l = 0; l < p.n_layers; ++l) {
+        uint4* pg = reinterpret_cast<uint4*>(p.base + (size_t)l * p.layer_bytes + (size_t)page * p.page_bytes);
+        const uint32_t* s = src + (size_t)l * (p.page_bytes / 4);
+        for (size_t k = threadIdx.x; k < p.page_bytes / 16; k += kRecThreads)
+            pg[k] = make_uint4(__ldcg(s + 4 * k), __ldcg(s + 4 * k + 1), __ldcg(s + 4 * k + 2), __ldcg(s + 4 * k + 3));
     }
 }
 
@@ -214,20 +225,32 @@ int launch_records(yf_pool* pool, int32_t n, const int32_t* pages, const unsigne
     p.ok = ok;
     p.rec_bytes = kRecHeader + (size_t)pool->desc.n_layers * pool->page_bytes;
     p.status = pool->d_status;
-    const size_t payload = p.rec_bytes - kRecHeader, units = payload / 16;
+    const size_t payload = p.rec_bytes - kRecHeader;
     if (payload >= (1ull << 29)) return fail(YF_E_UNSUPPORTED, "record payload of %zu bytes", payload);
-    if (pool->crc_ops.size() != kRecThreads + 1) {  // the record shape is fixed per pool: once
-        std::vector<uint32_t> ops(kRecThreads + 1);
-        const size_t per = (units + kRecThreads - 1) / kRecThreads;
+    // a page = 2^j equal blocks of at most 32 KB (page bytes are 17 x 2^m)
+    size_t blk = pool->page_bytes;
+    int bpp = 1;
+    while (blk > (size_t)kBlkMaxBytes && blk % 32 == 0) {
+        blk /= 2;
+        bpp *= 2;
+    }
+    if (blk > (size_t)kBlkMaxBytes || blk % 16) return fail(YF_E_UNSUPPORTED, "page of %zu bytes", pool->page_bytes);
+    p.blk_words = (int)(blk / 4);
+    p.blks_per_page = bpp;
+    if (pool->crc_ops.size() != kRecThreads + 2) {  // the record shape is fixed per pool: once
+        std::vector<uint32_t> ops(kRecThreads + 2);
+        const int nw = p.blk_words;
         for (int t = 0; t < kRecThreads; ++t) {
-            const size_t u1 = std::min(units, (size_t)t * per + per);
-            ops[t] = x8n_mod((units - u1) * 16);
+            const int w1 = (int)((long long)(t + 1) * nw / kRecThreads);
+            ops[t] = x8n_mod((unsigned long long)(nw - w1) * 4);
         }
-        ops[kRecThreads] = gf2_mulmod(x8n_mod(payload), 0xFFFFFFFFu);
+        ops[kRecThreads] = x8n_mod(blk);
+        ops[kRecThreads + 1] = gf2_mulmod(x8n_mod(payload), 0xFFFFFFFFu);
         pool->crc_ops.swap(ops);
     }
     for (int t = 0; t < kRecThreads; ++t) p.shift[t] = pool->crc_ops[t];
-    p.preset = pool->crc_ops[kRecThreads];
+    p.blk_shift = pool->crc_ops[kRecThreads];
+    p.preset = pool->crc_ops[kRecThreads + 1];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (do_export)
         export_records_kernel<<<n, kRecThreads, 0, s>>>(p);
