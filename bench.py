@@ -314,6 +314,24 @@ class ShardedStep:
     def run_attn(self):
         self.sd.partial(self.q_local, self.cu_k, self.bt, self.scale, max(self.n, 1))
 
+    def capture(self):
+        """CUDA graphs of one step (NCCL all-gather included) and of the partial alone, after a
+        warm step has created the NCCL communicator and the workspace."""
+        torch = self.torch
+        with torch.cuda.stream(self.stream):
+            self.run()
+        self.stream.synchronize()
+        self.g_step, self.g_attn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g_step, stream=self.stream, capture_error_mode="relaxed"):
+            self.run()
+        with torch.cuda.graph(self.g_attn, stream=self.stream, capture_error_mode="relaxed"):
+            self.run_attn()
+        self.stream.synchronize()
+
+    def release(self):
+        """Drops the graphs (the step's holds an NCCL call: gone before the process group)."""
+        self.g_step = self.g_attn = None
+
     def launches_per_step(self) -> int:
         """KV write (owner only) + partial decode + one combine per head group (the all-gather
         is NCCL's kernel, the q slice a torch copy)."""
@@ -343,10 +361,10 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         layers_resident = max(1, min(wl.n_layers, int(0.8 * free // per_layer)))
     step = ShardedStep(wl, local_rank, rank, world) if sharded else Step(wl, local_rank, layers_resident)
     stream = step.stream
-    if args.no_graph or sharded:  # the sharded step holds an NCCL call: launched directly
+    if args.no_graph:
         run_step, run_attn = step.run, step.run_attn
     else:
-        step.capture()
+        step.capture()  # the sharded step's graph holds its NCCL all-gather
         run_step, run_attn = step.g_step.replay, step.g_attn.replay
 
     def barrier():
@@ -454,7 +472,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
             else "pool fits in L2 (small workload)",
             "parallelism": (f"kv-head x sequence sharded x{world} (partials all-gathered over NCCL, LSE combine)"
                             if sharded else f"slot-sharded x{world} (each rank its own slots, no collective)"),
-            "launch": "direct C-ABI calls" if (args.no_graph or sharded) else "CUDA graph replay of the step's C-ABI calls",
+            "launch": "direct C-ABI calls" if args.no_graph else (
+                "CUDA graph replay of the step (partial, NCCL all-gather, combine)" if sharded
+                else "CUDA graph replay of the step's C-ABI calls"),
         },
         "kv_gbs": kv_bytes * world / (ms * 1e-3) / 1e9,
         "hbm_frac_step": kv_bytes / (ms * 1e-3) / 1e9 / hbm,
@@ -465,6 +485,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         "clocks": clk,
         "device_status": status,
     }
+    if sharded and hasattr(step, "release"):
+        step.release()
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
     return line
