@@ -5,8 +5,8 @@
 // kv_append_paged_f16 / launch_append_multi (docs/plans/2026-08-27-tiered-kv-cache.md:61-64):
 // K leaves this kernel as Q8_0 pool bytes instead of an f16 tensor that a second launch reads.
 //
-// One warp per (new row, head slot); slots 0..Hq-1 are the q heads (norm, RoPE, q and gate out),
-// slots Hq..Hq+Hkv-1 the kv heads (k: norm, RoPE, rounded to f16 as the unfused path stores it,
+// One warp per (new row, head slot); the first ceil(Hq/4) slots take four q heads each (norm, RoPE,
+// q and gate out; the weights and cos/sin loaded once for the four), the next Hkv the kv heads (k: norm, RoPE, rounded to f16 as the unfused path stores it,
 // then Q8_0 into the pool; v: Q8_0 into the pool).  Every float operation is an explicit IEEE
 // round-to-nearest operation in a fixed order (no contraction, the sum of squares in lane order
 // then an xor butterfly 16, 8, 4, 2, 1), so the oracle reproduces q, gate and the pool bytes
@@ -23,6 +23,7 @@ namespace yf {
 namespace {
 
 constexpr int kPrepWarps = 4;
+constexpr int kPrepQHeads = 4;  // q heads per warp
 
 struct PrepParams {
     uint8_t* layer_base;
@@ -62,10 +63,11 @@ __device__ __forceinline__ void store_f16_row(__half* dst, const float (&x)[E]) 
         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// RMSNorm of the warp's row (lane values x, dims lane*E ..) times (w + w_offset), then RoPE.
+// RMSNorm of the warp's row (lane values x, dims lane*E ..) times wf = (w + w_offset), then RoPE
+// with the lane's cos/sin values c, s of the row's position.
 template <int D>
-__device__ __forceinline__ void norm_rope(const PrepParams& p, const float* w, int pos, int lane,
-                                          float (&x)[D / 32]) {
+__device__ __forceinline__ void norm_rope(const PrepParams& p, const float (&wf)[D / 32], const float (&c)[D / 32],
+                                          const float (&s)[D / 32], int lane, float (&x)[D / 32]) {
     constexpr int E = D / 32;
     const int d0 = lane * E;
     float ss = 0.f;
@@ -76,21 +78,36 @@ __device__ __forceinline__ void norm_rope(const PrepParams& p, const float* w, i
     const float mean = __fmul_rn(ss, 1.0f / D);  // D is a power of two: exact
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], r), __fadd_rn(__ldg(w + d0 + e), p.w_offset));
+    for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], r), wf[e]);
     if (p.rope_dim == 0) return;
     const int half = p.rope_dim >> 1;
     float part[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) part[e] = __shfl_xor_sync(0xffffffffu, x[e], half / E);
     if (d0 >= p.rope_dim) return;
-    const int j0 = d0 % half;
-    const float* cp = p.cosb + (size_t)pos * half + j0;
-    const float* sp = p.sinb + (size_t)pos * half + j0;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        x[e] = d0 < half ? __fsub_rn(__fmul_rn(x[e], c[e]), __fmul_rn(part[e], s[e]))
+                         : __fadd_rn(__fmul_rn(x[e], c[e]), __fmul_rn(part[e], s[e]));
+}
+
+// The lane's norm weights (w + w_offset) and the position's cos/sin values, loaded once per warp.
+template <int E>
+__device__ __forceinline__ void load_row_consts(const PrepParams& p, const float* w, int pos, int lane,
+                                                float (&wf)[E], float (&c)[E], float (&s)[E]) {
+    const int d0 = lane * E;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        const float c = __ldg(cp + e), s = __ldg(sp + e);
-        x[e] = d0 < half ? __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(part[e], s))
-                         : __fadd_rn(__fmul_rn(x[e], c), __fmul_rn(part[e], s));
+        wf[e] = __fadd_rn(__ldg(w + d0 + e), p.w_offset);
+        c[e] = 0.f;
+        s[e] = 0.f;
+    }
+    if (p.rope_dim == 0 || d0 >= p.rope_dim) return;
+    const int half = p.rope_dim >> 1, j0 = d0 % half;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        c[e] = __ldg(p.cosb + (size_t)pos * half + j0 + e);
+        s[e] = __ldg(p.sinb + (size_t)pos * half + j0 + e);
     }
 }
 
@@ -102,7 +119,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const PrepPa
     const int lane = threadIdx.x & 31;
     const int wi = blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
     const int b = blockIdx.y;
-    const int S = p.Hq + p.H;
+    const int QW = (p.Hq + kPrepQHeads - 1) / kPrepQHeads;  // q-head warps per row
+    const int S = QW + p.H;
     const int i = wi / S, slot = wi % S;
     const int r0 = p.cu_rows[b], n = p.cu_rows[b + 1] - r0;
     if (i == 0 && slot == 0 && lane == 0 && (n > p.max_rows || n < 0)) atomicOr(p.status, YF_DEV_BAD_ROWS);
@@ -114,23 +132,28 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const PrepPa
         return;
     }
     const int d0 = lane * E;
-    float x[E];
-    if (slot < p.Hq) {
-        const int h = slot;
-        const __half* src = p.qg + ((size_t)row * p.Hq + h) * (2 * D);
-        load_f16_row<E>(src + d0, x);
-        norm_rope<D>(p, p.wq, pos, lane, x);
-        __half* qo = p.q_out + ((size_t)row * p.Hq + h) * D + d0;
-        store_f16_row<E>(qo, x);
-        // the gate half, unchanged
-        __half* go = p.gate_out + ((size_t)row * p.Hq + h) * D + d0;
-        if constexpr (E == 4)
-            *reinterpret_cast<uint2*>(go) = *reinterpret_cast<const uint2*>(src + D + d0);
-        else
-            *reinterpret_cast<uint4*>(go) = *reinterpret_cast<const uint4*>(src + D + d0);
+    float x[E], wf[E], c[E], s[E];
+    if (slot < QW) {
+        // kPrepQHeads q heads of the row: the weights and cos/sin are loaded once for all of them
+        load_row_consts<E>(p, p.wq, pos, lane, wf, c, s);
+#pragma unroll
+        for (int j = 0; j < kPrepQHeads; ++j) {
+            const int h = slot * kPrepQHeads + j;
+            if (h >= p.Hq) break;
+            const __half* src = p.qg + ((size_t)row * p.Hq + h) * (2 * D);
+            load_f16_row<E>(src + d0, x);
+            norm_rope<D>(p, wf, c, s, lane, x);
+            store_f16_row<E>(p.q_out + ((size_t)row * p.Hq + h) * D + d0, x);
+            // the gate half, unchanged
+            __half* go = p.gate_out + ((size_t)row * p.Hq + h) * D + d0;
+            if constexpr (E == 4)
+                *reinterpret_cast<uint2*>(go) = *reinterpret_cast<const uint2*>(src + D + d0);
+            else
+                *reinterpret_cast<uint4*>(go) = *reinterpret_cast<const uint4*>(src + D + d0);
+        }
         return;
     }
-    const int h = slot - p.Hq;
+    const int h = slot - QW;
     if (pos >= p.max_blocks * P) {
         if (lane == 0) atomicOr(p.status, YF_DEV_BAD_POS);
         return;
@@ -142,8 +165,9 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const PrepPa
     }
     uint8_t* tile = p.layer_base + ((size_t)page * p.H + h) * p.phb + ((pos % P) / 16) * TB;
     const int t = pos % 16;
+    load_row_consts<E>(p, p.wk, pos, lane, wf, c, s);
     load_f16_row<E>(p.k + ((size_t)row * p.H + h) * D + d0, x);
-    norm_rope<D>(p, p.wk, pos, lane, x);
+    norm_rope<D>(p, wf, c, s, lane, x);
 #pragma unroll
     for (int e = 0; e < E; ++e) x[e] = __half2float(__float2half_rn(x[e]));  // K as the f16 tensor it replaces
     q8_store_row<D, NB>(tile, t, 0, lane, x);
@@ -153,7 +177,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const PrepPa
 
 template <int D, int NB, int TPP>
 int launch_prep(const PrepParams& p, int batch, int max_rows, cudaStream_t s) {
-    const long long warps = (long long)max_rows * (p.Hq + p.H);
+    const long long warps = (long long)max_rows * ((p.Hq + kPrepQHeads - 1) / kPrepQHeads + p.H);
     const dim3 grid((unsigned)((warps + kPrepWarps - 1) / kPrepWarps), batch);
     attn_prep_kernel<D, NB, TPP><<<grid, kPrepWarps * 32, 0, s>>>(p);
     const cudaError_t e = cudaGetLastError();
