@@ -112,3 +112,9 @@ def test_workspace_size_plan(yf):
     assert L.yf_attn_workspace_size(pool.handle, 32, 2000, 1, 256) == 0
     assert L.yf_attn_workspace_size(pool.handle, 30, 16, 1, 32768) == 0   # Hq not a multiple of Hkv
     pool.close()
+    # few long units (one 131072-key entry, 2 kv heads, D 256): at most max(1.75 x 148, 128 per unit)
+    # = 259 CTAs instead of a full 4-per-SM wave
+    long_pool = yf.PagedKvPool(1, 4, 2, 256, device=None)
+    row256 = 8 * 257 * 4
+    assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 259 * 2 * row256
+    long_pool.close()
