@@ -249,7 +249,7 @@ class Step:
         rows = wl.n_q_heads // wl.n_kv_heads * (1 if self.decode else self.max_q)
         rpc = 8 if (rows <= 8 or wl.head_dim > 128) else 16
         units = wl.batch * wl.n_kv_heads * -(-rows // rpc)
-        fused = os.environ.get("YF_FUSED_COMBINE", "1") != "0" and units <= (1 << 16)
+        fused = self.pool.options()["merge"] == 0 and units <= (1 << 16)
         separate = self.ws_bytes > 0 and not fused
         return wl.n_layers * (2 + (1 if separate else 0))
 

@@ -139,8 +139,44 @@ YF_API int yf_pool_free_count(const yf_pool* pool, int32_t* out_free);
 YF_API int yf_pool_refcount(const yf_pool* pool, int32_t page, int32_t* out_refcount);
 
 /* Reads the device status word (synchronizes the pool's device) into
- * *out_bits; clears it when clear != 0. */
+ * *out_bits; clears it when clear != 0.  Clearing a word that holds
+ * YF_DEV_TIMEOUT also resets the pool's merge arrival counters (a wait that
+ * gave up leaves them mid-count), so the pool is usable again; a pool whose
+ * status shows YF_DEV_TIMEOUT must be cleared this way before its next call. */
 YF_API int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear);
+
+/* ---- pool: attention options ---------------------------------------------------
+ * Explicit per-pool choices that every attention call on the pool, and
+ * yf_attn_workspace_size, read (the library reads no environment variables).
+ * A zero-filled struct is the default.  The engine's counterpart is its
+ * command-line / config flags (src/cli.rs), fixed for the life of the pool. */
+#define YF_SCHED_AUTO 0        /* persistent decode schedule where it applies, else chunked split-KV */
+#define YF_SCHED_CHUNKED 1     /* always the chunked (unit x chunk grid) split-KV schedule */
+#define YF_MERGE_IN_KERNEL 0   /* split partials merged inside the attention kernel */
+#define YF_MERGE_SEPARATE 1    /* chunked schedule: a separate combine launch merges the partials */
+#define YF_PREFILL_AUTO 0      /* tcgen05 prefill kernel where it applies (>= 128 rows per kv head) */
+#define YF_PREFILL_SPLITKV 1   /* every query block on the split-KV kernel */
+typedef struct yf_attn_options {
+    int32_t schedule;        /* YF_SCHED_* */
+    int32_t chunk_tiles;     /* chunked schedule: 16-token tiles per CTA; 0 = sized from the grid */
+    int32_t copy_stages;     /* bulk-copy ring depth per warp: 0 = default (4 at D 128, 2 at D 256) or 3 */
+    int32_t merge;           /* YF_MERGE_* */
+    int32_t prefill_kernel;  /* YF_PREFILL_* */
+    uint32_t wait_limit_us;  /* bound of every in-kernel wait (copies, merges); 0 = 1 000 000 (1 s) */
+    int32_t reserved[10];    /* zero */
+} yf_attn_options;
+/* Replaces the pool's options (validated: YF_E_INVALID for an unknown value).  Not
+ * stream-ordered: set them between calls, not while the pool's kernels run. */
+YF_API int yf_pool_set_options(yf_pool* pool, const yf_attn_options* opts);
+YF_API int yf_pool_get_options(const yf_pool* pool, yf_attn_options* out_opts);
+
+/* Fault-injection hook for testing the bounded waits (no counterpart in the reference):
+ * writes `value` into the pool's merge arrival counter `index` (stream-ordered).  A value of
+ * 0xFFFF makes the next merge of that unit wait for parts that never arrive, so the wait runs
+ * out after wait_limit_us and flags YF_DEV_TIMEOUT; yf_pool_status(clear) then resets the
+ * counters.  index < YF_POOL_COUNTERS. */
+#define YF_POOL_COUNTERS (65536 + 4096)
+YF_API int yf_pool_plant_counter(yf_pool* pool, int32_t index, uint32_t value, void* stream);
 
 /* ---- KV write: Q8_0 quantize-and-scatter ------------------------------------
  * yf_kv_append_paged replaces kv_append_paged_f16 (fork quantized.cu:6996,

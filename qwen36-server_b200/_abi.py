@@ -27,6 +27,14 @@ YF_DEV_BAD_ROWS = 8
 YF_DEV_TIMEOUT = 16
 YF_DEV_SMEM_ALIGN = 32
 
+YF_SCHED_AUTO = 0
+YF_SCHED_CHUNKED = 1
+YF_MERGE_IN_KERNEL = 0
+YF_MERGE_SEPARATE = 1
+YF_PREFILL_AUTO = 0
+YF_PREFILL_SPLITKV = 1
+YF_POOL_COUNTERS = 65536 + 4096
+
 ERROR_NAMES = {
     YF_E_INVALID: "YF_E_INVALID", YF_E_UNSUPPORTED: "YF_E_UNSUPPORTED", YF_E_NOMEM: "YF_E_NOMEM",
     YF_E_CUDA: "YF_E_CUDA", YF_E_RANGE: "YF_E_RANGE", YF_E_WORKSPACE: "YF_E_WORKSPACE", YF_E_STATE: "YF_E_STATE",
@@ -46,6 +54,15 @@ class PoolDesc(ctypes.Structure):
         ("n_layers", ctypes.c_int32), ("n_pages", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
         ("head_dim", ctypes.c_int32), ("page_size", ctypes.c_int32), ("group_size", ctypes.c_int32),
         ("device", ctypes.c_int32), ("reserved", ctypes.c_int32), ("device_mem", ctypes.c_void_p),
+    ]
+
+
+class AttnOptions(ctypes.Structure):
+    """yf_attn_options: the pool's explicit attention choices (all zero = the defaults)."""
+    _fields_ = [
+        ("schedule", ctypes.c_int32), ("chunk_tiles", ctypes.c_int32), ("copy_stages", ctypes.c_int32),
+        ("merge", ctypes.c_int32), ("prefill_kernel", ctypes.c_int32), ("wait_limit_us", ctypes.c_uint32),
+        ("reserved", ctypes.c_int32 * 10),
     ]
 
 
@@ -71,6 +88,9 @@ SIGNATURES = {
     "yf_pool_free_count": (_ci, [_vp, _P_i32]),
     "yf_pool_refcount": (_ci, [_vp, _i32, _P_i32]),
     "yf_pool_status": (_ci, [_vp, ctypes.POINTER(_u32), _ci]),
+    "yf_pool_set_options": (_ci, [_vp, _vp]),
+    "yf_pool_get_options": (_ci, [_vp, _vp]),
+    "yf_pool_plant_counter": (_ci, [_vp, _i32, _u32, _vp]),
     "yf_kv_append_paged": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
     "yf_kv_append_paged_multi": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "yf_attn_prepare_append": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _f32, _i32, _vp, _vp, _i32, _i32,

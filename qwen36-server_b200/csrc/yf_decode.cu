@@ -88,6 +88,7 @@ struct SplitParams {
     uint32_t* counters;  // per-unit arrival counters for the merge, or null (separate combine)
     uint32_t* status;
     const int2* trie;    // tree verify: inclusive subtree range of every draft row, or null
+    uint64_t wait_ns;    // bound of every wait (copies, merge arrivals)
 };
 
 // Tree verify: the draft rows of an entry are the nodes of a token trie in depth-first order;
@@ -533,7 +534,7 @@ __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * 
     for (int i = 0; i < my_n; ++i) {
         const int pos = ring.base + i;
         const int slot = pos % STAGES;
-        if (!__all_sync(0xffffffffu, mbar_wait(&ring.bar[slot], (uint32_t)(pos / STAGES) & 1u))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&ring.bar[slot], (uint32_t)(pos / STAGES) & 1u, p.wait_ns))) {
             if (lane == 0) atomicOr(p.status, YF_DEV_TIMEOUT);
             ok = false;
             break;
@@ -550,7 +551,7 @@ __device__ __forceinline__ void stream_unit(const SplitParams& p, TileRing<32 * 
     }
     if (!ok) {  // wait (bounded) for the copies still in flight before the ring is reused
         for (int i = done; i < my_n && i < done + STAGES; ++i)
-            (void)mbar_wait(&ring.bar[(ring.base + i) % STAGES], (uint32_t)((ring.base + i) / STAGES) & 1u);
+            (void)mbar_wait(&ring.bar[(ring.base + i) % STAGES], (uint32_t)((ring.base + i) / STAGES) & 1u, p.wait_ns);
     }
     ring.base += my_n;
 }
@@ -783,7 +784,7 @@ __device__ __forceinline__ void arrive_and_merge(const SplitParams& p, const Uni
 // unit's output columns (all of a slice's loads in flight at once), and count their
 // departure (high 16 bits); the last to leave resets the counter for the next call.  A CTA
 // that goes on to the next unit only arrives.  The grid is a single resident wave, so the
-// waits end; each is bounded by kWaitLimitNs and flags YF_DEV_TIMEOUT if it gives up.
+// waits end; each is bounded by the call's wait limit and flags YF_DEV_TIMEOUT if it gives up.
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* ptr) {
     uint32_t v;
@@ -917,7 +918,7 @@ __device__ __forceinline__ void cooperative_merge(const SplitParams& p, const Un
             const uint64_t t0 = globaltimer_ns();
             for (uint32_t i = 0;; ++i) {
                 if ((ld_acquire_u32(ctr) & 0xFFFFu) >= (uint32_t)n_parts) break;
-                if ((i & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+                if ((i & 63u) == 63u && globaltimer_ns() - t0 > p.wait_ns) {
                     ok = false;
                     break;
                 }
@@ -1139,16 +1140,6 @@ __global__ void __launch_bounds__(kThreads) splitkv_combine(const SplitParams p)
 
 // ---- launch ----------------------------------------------------------------------------------
 
-// Per-device flag that a kernel's dynamic shared-memory limit was raised.
-template <typename K>
-static int raise_smem(K kern, int smem, int dev, int* set_to) {
-    if (dev >= 0 && dev < 64 && set_to[dev] >= smem) return YF_OK;
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(split-KV)");
-    if (dev >= 0 && dev < 64) set_to[dev] = smem;
-    return YF_OK;
-}
-
 template <int D, int NB, int NT, int TPP, int STAGES, bool TREE = false>
 static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
     constexpr int TB = 32 * D + 64 * NB;
@@ -1157,36 +1148,40 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
     cudaError_t e;
     if (!TREE && plan.persistent) {
         auto kern = decode_persistent_kernel<D, NB, NT, TPP, STAGES>;
-        static int set_to[64] = {};
+        static LaunchCache cache;
         const int smem = SMEM + (a.batch + 1) * (int)sizeof(long long);
-        const int rc = raise_smem(kern, SMEM + (kPersistentMaxBatch + 1) * (int)sizeof(long long), dev, set_to);
+        int rc = raise_smem_attr((const void*)kern, SMEM + (kPersistentMaxBatch + 1) * (int)sizeof(long long), dev,
+                                 cache);
         if (rc) return rc;
-        // every CTA must be resident at once: cap the grid by the occupancy at this shared-memory
-        // size (cached per device for the last size asked)
-        static int occ_smem[64] = {}, occ_val[64] = {};
+        // every CTA must be resident at once (mergers wait for the parts of other CTAs): the grid
+        // is capped by the occupancy at this shared-memory size and launched cooperatively, so a
+        // grid that cannot be co-resident (another kernel holding SMs) is refused or deferred by
+        // the launch instead of stalling its mergers
         int occ = 0;
-        if (dev >= 0 && dev < 64 && occ_smem[dev] == smem) {
-            occ = occ_val[dev];
-        } else {
-            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
-            if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
-            if (dev >= 0 && dev < 64) {
-                occ_smem[dev] = smem;
-                occ_val[dev] = occ;
-            }
-        }
+        rc = occupancy((const void*)kern, kThreads, smem, dev, cache, &occ);
+        if (rc) return rc;
         int ctas = std::max(1, std::min(plan.persistent_ctas, occ * a.pool->sm_count));
         // a few units over many CTAs: a multiple of the unit count puts the boundaries of
         // equal-length units on CTA boundaries (no CTA switches units and joins two merges)
         const long long units = (long long)a.batch * a.pool->desc.n_kv_heads * plan.n_row_groups;
         if (units > 1 && ctas >= 16 * units) ctas -= (int)(ctas % units);
-        kern<<<ctas, kThreads, smem, a.stream>>>(p);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(ctas);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = a.stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, p);
+        if (e == cudaSuccess) e = cudaGetLastError();
         return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_persistent launch");
     }
     auto kern = splitkv_kernel<D, NB, NT, TPP, STAGES, TREE>;
-    static int set_to2[64] = {};
-    const int rc = raise_smem(kern, SMEM, dev, set_to2);
+    static LaunchCache cache2;
+    const int rc = raise_smem_attr((const void*)kern, SMEM, dev, cache2);
     if (rc) return rc;
     const dim3 grid(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch, plan.max_chunks);
     kern<<<grid, kThreads, SMEM, a.stream>>>(p);
@@ -1247,6 +1242,7 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.part_lse = a.part_lse;
     p.status = a.pool->d_status;
     p.trie = reinterpret_cast<const int2*>(a.trie);
+    p.wait_ns = wait_limit_ns(a.pool);
     if (p.trie && plan.persistent) return fail(YF_E_UNSUPPORTED, "tree verify needs the chunked schedule");
     const size_t units = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups;
     p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;

@@ -7,11 +7,11 @@
 
 namespace yf {
 
-// Bounds of an mbarrier wait: it gives up after kWaitLimitNs of global time or kMaxWaitIters
-// tries, whichever comes first (a try_wait may itself suspend for a hardware-defined interval,
-// so the iteration bound alone could stretch to minutes).
+// Bounds of an mbarrier wait: it gives up after the call's limit of global time (the pool's
+// wait_limit_us option, 1 s by default) or kMaxWaitIters tries, whichever comes first (a
+// try_wait may itself suspend for a hardware-defined interval, so the iteration bound alone
+// could stretch to minutes).
 constexpr uint32_t kMaxWaitIters = 1u << 20;
-constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
@@ -59,12 +59,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the given phase parity; false if it gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1; i < kMaxWaitIters; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if ((i & 7u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
     }
     return false;
 }

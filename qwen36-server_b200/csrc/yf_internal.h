@@ -61,8 +61,10 @@ struct yf_pool {
     int sm_count = 148;
     std::vector<int32_t> refcount;
     std::vector<int32_t> free_stack;  // LIFO of free page ids
-    // CRC-32C combine operators of this pool's snapshot records (computed at the first record call)
+    // CRC-32C combine operators of this pool's snapshot records (computed when the pool is created)
     std::vector<uint32_t> crc_ops;
+    // attention choices every call and the workspace query read (yf_pool_set_options)
+    yf_attn_options opts{};
 };
 
 namespace yf {
@@ -73,6 +75,23 @@ int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Bound of every in-kernel wait of this pool's calls, in nanoseconds.
+inline uint64_t wait_limit_ns(const yf_pool* pool) {
+    return (uint64_t)(pool->opts.wait_limit_us ? pool->opts.wait_limit_us : 1000000u) * 1000ull;
+}
+
+// Per-device launch facts cached behind a mutex (any host thread may launch): the dynamic
+// shared memory a kernel was raised to, and the resident CTAs per SM at one size.
+struct LaunchCache {
+    int smem_set[64] = {};
+    int occ_smem[64] = {};
+    int occ_val[64] = {};
+};
+// Raises `kern`'s dynamic shared-memory limit to `smem` once per device.
+int raise_smem_attr(const void* kern, int smem, int dev, LaunchCache& c);
+// Resident CTAs per SM of `kern` at `threads` x `smem` (cached per device for the last size).
+int occupancy(const void* kern, int threads, int smem, int dev, LaunchCache& c, int* out);
 
 // Split-KV plan of one attention call; identical in the workspace query and
 // the launch so that the caller's workspace always fits.

@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "yf_internal.h"
@@ -25,6 +26,36 @@ int fail(int code, const char* fmt, ...) {
 
 int cuda_fail(cudaError_t e, const char* what) {
     return fail(YF_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+namespace {
+std::mutex g_launch_mu;  // guards every LaunchCache
+}
+
+int raise_smem_attr(const void* kern, int smem, int dev, LaunchCache& c) {
+    std::lock_guard<std::mutex> lock(g_launch_mu);
+    if (dev >= 0 && dev < 64 && c.smem_set[dev] >= smem) return YF_OK;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+    if (dev >= 0 && dev < 64) c.smem_set[dev] = smem;
+    return YF_OK;
+}
+
+int occupancy(const void* kern, int threads, int smem, int dev, LaunchCache& c, int* out) {
+    std::lock_guard<std::mutex> lock(g_launch_mu);
+    if (dev >= 0 && dev < 64 && c.occ_smem[dev] == smem && c.occ_val[dev] > 0) {
+        *out = c.occ_val[dev];
+        return YF_OK;
+    }
+    int occ = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+    if (dev >= 0 && dev < 64) {
+        c.occ_smem[dev] = smem;
+        c.occ_val[dev] = occ;
+    }
+    *out = occ;
+    return YF_OK;
 }
 
 static int check_desc(const yf_pool_desc* d) {
@@ -57,10 +88,10 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     const int tiles = (max_seqlen_k + kTileTokens - 1) / kTileTokens;
     const long long units = (long long)batch * H * p.n_row_groups;
     const long long target = (long long)pool->sm_count * 16;
-    const char* ov = getenv("YF_CHUNK_TILES");  // host-side tuning override
+    const yf_attn_options& o = pool->opts;
     int chunk;
-    if (ov && atoi(ov) > 0) {
-        chunk = atoi(ov);
+    if (o.chunk_tiles > 0) {
+        chunk = o.chunk_tiles;
     } else {
         long long c = (units * tiles + target - 1) / target;
         if (c < 8) c = 8;
@@ -71,24 +102,20 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     if (tiles > 65535LL * chunk) chunk = (tiles + 65534) / 65535;  // grid z <= 65535
     p.chunk_tiles = chunk;
     p.max_chunks = tiles > 0 ? (tiles + chunk - 1) / chunk : 1;
-    p.stages = pool->desc.head_dim == 128 ? 4 : 2;
-    const char* st = getenv("YF_DECODE_STAGES");  // host-side tuning override
-    if (st && atoi(st) == 3) p.stages = 3;
-    const char* fc = getenv("YF_FUSED_COMBINE");
-    const bool fused_env = !(fc && atoi(fc) == 0);
+    p.stages = o.copy_stages == 3 ? 3 : (pool->desc.head_dim == 128 ? 4 : 2);
+    const bool in_kernel_merge = o.merge != YF_MERGE_SEPARATE;
     // the in-kernel merge of the chunked schedule keeps (chunks + 1) x rows floats of weights
     // in the CTA's stage area (4 warps x stages x tile bytes); the persistent schedule merges
     // its CTAs (at most kMaxGroupCounters / 2) in one cooperative pass
     {
         const int D = pool->desc.head_dim, NB = D / pool->desc.group_size;
         const long long area_floats = 4LL * p.stages * (32 * D + 64 * NB) / 4;
-        p.fused_combine = fused_env && (long long)(p.max_chunks + 1) * p.rows_per_cta <= area_floats;
+        p.fused_combine = in_kernel_merge && (long long)(p.max_chunks + 1) * p.rows_per_cta <= area_floats;
     }
     // Persistent schedule: one row group per entry (decode, small verify blocks), a batch whose
     // tile prefix fits in shared memory, and the merge counters available.
-    const char* ps = getenv("YF_PERSISTENT");
-    p.persistent = !tree && !(ps && atoi(ps) == 0) && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
-                   units <= kMaxCombineUnits && fused_env;
+    p.persistent = !tree && o.schedule != YF_SCHED_CHUNKED && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
+                   units <= kMaxCombineUnits && in_kernel_merge;
     if (p.persistent) p.fused_combine = true;
     const size_t row_bytes = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
     if (p.persistent) {
@@ -113,6 +140,9 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
 }  // namespace yf
 
 using namespace yf;
+
+// One stream-ordered word store (the counter fault-injection hook).
+__global__ void store_word_kernel(uint32_t* dst, uint32_t value) { *dst = value; }
 
 extern "C" {
 
@@ -303,8 +333,55 @@ int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpy(out_bits, pool->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && clear) e = cudaMemset(pool->d_status, 0, sizeof(uint32_t));
+    // a merge wait that gave up left its unit's arrival counter mid-count (late parts may still
+    // have arrived after the mergers left): start every counter from zero again
+    if (e == cudaSuccess && clear && (*out_bits & YF_DEV_TIMEOUT))
+        e = cudaMemset(pool->d_counters, 0, sizeof(uint32_t) * ((size_t)kMaxCombineUnits + kMaxGroupCounters));
+    if (e == cudaSuccess && clear) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "status read");
     return YF_OK;
+}
+
+static int check_options(const yf_attn_options* o) {
+    if (!o) return fail(YF_E_INVALID, "options are null");
+    if (o->schedule != YF_SCHED_AUTO && o->schedule != YF_SCHED_CHUNKED)
+        return fail(YF_E_INVALID, "schedule %d unknown", o->schedule);
+    if (o->chunk_tiles < 0) return fail(YF_E_INVALID, "chunk_tiles %d < 0", o->chunk_tiles);
+    if (o->copy_stages != 0 && o->copy_stages != 3)
+        return fail(YF_E_INVALID, "copy_stages %d: 0 (default) or 3", o->copy_stages);
+    if (o->merge != YF_MERGE_IN_KERNEL && o->merge != YF_MERGE_SEPARATE)
+        return fail(YF_E_INVALID, "merge %d unknown", o->merge);
+    if (o->prefill_kernel != YF_PREFILL_AUTO && o->prefill_kernel != YF_PREFILL_SPLITKV)
+        return fail(YF_E_INVALID, "prefill_kernel %d unknown", o->prefill_kernel);
+    if (o->wait_limit_us > 60u * 1000000u) return fail(YF_E_INVALID, "wait_limit_us above 60 s");
+    for (int32_t r : o->reserved)
+        if (r) return fail(YF_E_INVALID, "reserved option fields must be zero");
+    return YF_OK;
+}
+
+int yf_pool_set_options(yf_pool* pool, const yf_attn_options* opts) {
+    if (!pool) return fail(YF_E_INVALID, "pool is null");
+    const int rc = check_options(opts);
+    if (rc) return rc;
+    pool->opts = *opts;
+    return YF_OK;
+}
+
+int yf_pool_get_options(const yf_pool* pool, yf_attn_options* out) {
+    if (!pool || !out) return fail(YF_E_INVALID, "null argument");
+    *out = pool->opts;
+    return YF_OK;
+}
+
+int yf_pool_plant_counter(yf_pool* pool, int32_t index, uint32_t value, void* stream) {
+    if (!pool) return fail(YF_E_INVALID, "pool is null");
+    if (!pool->d_counters) return fail(YF_E_INVALID, "host-only pool has no device counters");
+    if (index < 0 || index >= kMaxCombineUnits + kMaxGroupCounters)
+        return fail(YF_E_RANGE, "counter %d out of range", index);
+    cudaSetDevice(pool->desc.device);
+    store_word_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(pool->d_counters + index, value);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? YF_OK : cuda_fail(e, "counter store");
 }
 
 // Page copies between the pool and a snapshot buffer: one cudaMemcpyAsync per

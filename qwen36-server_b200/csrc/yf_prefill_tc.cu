@@ -82,6 +82,7 @@ struct PrefillParams {
     float scale_log2;
     __half* out;
     uint32_t* status;
+    uint64_t wait_ns;  // bound of every wait
 };
 
 // ---- tcgen05 / UMMA helpers ----------------------------------------------------------
@@ -339,11 +340,11 @@ __device__ __forceinline__ void give_up(volatile int* abort, uint32_t* status, u
     if (!(old & YF_DEV_TIMEOUT)) atomicOr(status, tag << 16);
 }
 
-// Bounded wait for the use-th completion (0-based) of `bar` (kWaitLimitNs of global time).
+// Bounded wait for the use-th completion (0-based) of `bar` (limit_ns of global time).
 // A wait that gives up raises the CTA's abort flag, after which every role skips its
 // remaining waits and drains quickly.
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int* abort, uint32_t* status,
-                                           uint32_t tag) {
+                                           uint64_t limit_ns, uint32_t tag) {
     if (*abort) return false;
     if (mbar_try_wait(bar, (uint32_t)use & 1u)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -351,7 +352,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int*
         if (mbar_try_wait(bar, (uint32_t)use & 1u)) return true;
         if ((i & 7u) == 0) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            if (globaltimer_ns() - t0 > limit_ns) break;
         }
     }
     give_up(abort, status, tag);
@@ -504,13 +505,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                     idle = 0;
                 } else if (++idle == 1) {
                     idle_t0 = globaltimer_ns();
-                } else if ((idle & 63u) == 0 && globaltimer_ns() - idle_t0 > kWaitLimitNs) {
+                } else if ((idle & 63u) == 0 && globaltimer_ns() - idle_t0 > p.wait_ns) {
                     give_up(s_abort, p.status, wait_tag(1, kBarIdle, (qk[0] & 31) | ((pv[0] & 31) << 5)));
                 }
             }
             // every MMA of this CTA has completed before TMEM is released
             umma_commit(&bars->drain);
-            if (!mbar_wait(&bars->drain, 0u)) give_up(s_abort, p.status, wait_tag(1, kBarDrain, 0));
+            if (!mbar_wait(&bars->drain, 0u, p.wait_ns)) give_up(s_abort, p.status, wait_tag(1, kBarDrain, 0));
         }
         __syncwarp();
     } else if (warp == kCopyWarp) {
@@ -532,7 +533,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                 for (int j = 0; j < 4; ++j) cur[j] = page[j];
                 if (kt + 1 < n_kt) fetch_pages(hf + 2);  // in flight while this half waits
                 if (kt >= 2 &&
-                    !wait_phase(&bars->raw_free[slot], (kt >> 1) - 1, s_abort, p.status, wait_tag(1, kBarRawFree, kt)))
+                    !wait_phase(&bars->raw_free[slot], (kt >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(1, kBarRawFree, kt)))
                     break;
                 uint8_t* dst = base + kSmRaw + slot * kRawHalf;
                 uint32_t bytes = 0;
@@ -571,11 +572,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
         const uint32_t peer_v_full1 = peer_addr(smem_u32(&bars->v_full[1]), peer);
         for (int j = 0; j < n_kt; ++j) {
             const int e = rank, slot = j & 1;  // half e of key tile j
-            (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, wait_tag(2, kBarRawFull, j));
+            (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarRawFull, j));
             // stage j&1 was last read by QK(j-2) (K) and PV(j-2) (V^T), here and in the peer
             // K stage j&1 was last read by QK(j-2) here and in the peer
             if (j >= 2)
-                (void)wait_phase(&bars->k_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarKFree, j));
+                (void)wait_phase(&bars->k_free[j & 1], (j >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarKFree, j));
             const uint8_t* raw = base + kSmRaw + slot * kRawHalf;
             const uint32_t kdst = sbase + kSmK + (j & 1) * 32768, vdst = sbase + kSmVt + (j & 1) * 32768 + e * 16384;
 #pragma unroll
@@ -613,7 +614,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
             }
             // V^T stage j&1 was last read by PV(j-2) here and in the peer
             if (j >= 2)
-                (void)wait_phase(&bars->v_free[j & 1], (j >> 1) - 1, s_abort, p.status, wait_tag(2, kBarVFree, j));
+                (void)wait_phase(&bars->v_free[j & 1], (j >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarVFree, j));
             // V: the thread's four dims share one scale group (dims 32dw .. 32dw+31) of tile vjt
             const uint8_t* TV = raw + vjt * kRawPitch;
             const bool vvalid = s_valid[slot * 4 + vjt] != 0;
@@ -672,7 +673,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
             const float sl2 = p.scale_log2;
             float m_run = -INFINITY, l_run = 0.f;  // running max (scaled, base 2) and sum
             for (int it = 0; it < n_kt; ++it) {
-                (void)wait_phase(&bars->s_full[qt], it, s_abort, p.status, wait_tag(3, kBarSFull, it));
+                (void)wait_phase(&bars->s_full[qt], it, s_abort, p.status, p.wait_ns, wait_tag(3, kBarSFull, it));
                 __syncwarp();
                 tc_fence_after();
                 const int key0 = it * kPfKeys, lim = kvlen - key0;
@@ -729,7 +730,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
             }
             // ---- epilogue: thread r writes row r of O_i / l
             if (n_kt > 0) {
-                (void)wait_phase(&bars->o_done[qt], 0, s_abort, p.status, wait_tag(3, kBarODone, 0));
+                (void)wait_phase(&bars->o_done[qt], 0, s_abort, p.status, p.wait_ns, wait_tag(3, kBarODone, 0));
                 __syncwarp();
                 tc_fence_after();
             }
@@ -771,8 +772,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
 
 // True when the tensor-core prefill kernel handles this call.
 bool prefill_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q) {
-    const char* env = getenv("YF_PREFILL_TC");  // host-side switch for A/B runs
-    if (env && atoi(env) == 0) return false;
+    if (pool->opts.prefill_kernel == YF_PREFILL_SPLITKV) return false;
     const yf_pool_desc& d = pool->desc;
     const int G = n_q_heads / d.n_kv_heads;
     return d.head_dim == kPfD && d.group_size == 32 && kPfRows % G == 0 && (long long)G * max_seqlen_q >= kPfRows;
@@ -797,14 +797,10 @@ int launch_prefill_tc(const AttnArgs& a) {
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.out = a.out;
     p.status = a.pool->d_status;
-    static int attr_dev[64] = {};
-    const int dev = d.device;
-    if (dev < 0 || dev >= 64 || !attr_dev[dev]) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmAlloc);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
-        if (dev >= 0 && dev < 64) attr_dev[dev] = 1;
-    }
+    p.wait_ns = wait_limit_ns(a.pool);
+    static LaunchCache cache;
+    const int rc = raise_smem_attr((const void*)prefill_tc_kernel, kSmAlloc, d.device, cache);
+    if (rc) return rc;
     const int ppb = kPfTiles * kPfRows / p.G;
     const long long blocks = (a.max_seqlen_q + ppb - 1) / ppb;
     const dim3 grid((unsigned)((blocks + 1) / 2 * 2), d.n_kv_heads, a.batch);  // clusters of 2 along x

@@ -133,7 +133,13 @@ __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecPa
     uint8_t* rec = p.records + (size_t)r * p.rec_bytes;
     const size_t payload = (size_t)p.n_layers * p.page_bytes;
     if (page < 0 || page >= p.n_pages) {
-        if (threadIdx.x == 0) atomicOr(p.status, YF_DEV_BAD_PAGE);
+        // a header that every import rejects (length 0), so that a reused staging buffer never
+        // passes an older record off as this one
+        if (threadIdx.x == 0) {
+            atomicOr(p.status, YF_DEV_BAD_PAGE);
+            uint32_t* h = reinterpret_cast<uint32_t*>(rec);
+            for (int k = 0; k < 5; ++k) h[k] = 0u;
+        }
         return;
     }
     const int nw = p.blk_words;

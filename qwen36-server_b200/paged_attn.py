@@ -120,6 +120,25 @@ class PagedKvPool:
         call("yf_pool_refcount", self._h, page, ctypes.byref(v))
         return v.value
 
+    # -- options (yf_attn_options) ----------------------------------------------------
+    def options(self) -> dict:
+        """The pool's attention options as a dict of field -> value."""
+        o = _abi.AttnOptions()
+        call("yf_pool_get_options", self._h, ctypes.byref(o))
+        return {f: getattr(o, f) for f, _ in o._fields_ if f != "reserved"}
+
+    def set_options(self, **fields) -> None:
+        """Replaces the named options (others keep their values): schedule, chunk_tiles,
+        copy_stages, merge, prefill_kernel, wait_limit_us."""
+        cur = self.options()
+        cur.update(fields)
+        o = _abi.AttnOptions(**cur)
+        call("yf_pool_set_options", self._h, ctypes.byref(o))
+
+    def plant_counter(self, index: int, value: int) -> None:
+        """Fault-injection hook for the bounded waits: stores ``value`` into merge counter ``index``."""
+        call("yf_pool_plant_counter", self._h, index, value, _stream(self.device))
+
     def status(self, clear: bool = True) -> int:
         """Device status bits (YF_DEV_*); synchronizes the device."""
         v = ctypes.c_uint32()

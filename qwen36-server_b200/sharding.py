@@ -110,17 +110,22 @@ class ShardedLongDecode:
         self.out = torch.empty((batch, n_q_heads, head_dim), dtype=torch.float16, device=self.dev)
         self._grp_out = None if batch == 1 or shard.n_head_groups == 1 else torch.empty(
             (shard.n_head_groups, batch * self.hq, head_dim), dtype=torch.float16, device=self.dev)
-        self.ws = None
+        # workspace for the shard's whole key range, so a context that grows step by step never
+        # outgrows it (partial() still re-checks against the call's own max_seqlen_k)
+        self.ws = self._workspace(max(shard.k1 - shard.k0, 1))
 
     def q_slice(self, q: torch.Tensor) -> torch.Tensor:
         """This rank's q heads of a full q [B, Hq, D]."""
         h0 = self.shard.kv_head0 * self.G
         return q[:, h0:h0 + self.hq].contiguous()
 
+    def _workspace(self, max_seqlen_k: int) -> torch.Tensor:
+        n = self.pool.workspace_size(self.hq, self.batch, 1, max_seqlen_k)
+        return torch.empty(max(n, 16), dtype=torch.uint8, device=self.dev)
+
     def partial(self, q_local: torch.Tensor, cu_k, table, scale: float, max_seqlen_k: int):
-        if self.ws is None:
-            n = self.pool.workspace_size(self.hq, self.batch, 1, max_seqlen_k)
-            self.ws = torch.empty(max(n, 16), dtype=torch.uint8, device=self.dev)
+        if self.pool.workspace_size(self.hq, self.batch, 1, max_seqlen_k) > self.ws.numel():
+            self.ws = self._workspace(max_seqlen_k)  # a longer range than the shard was built for
         pa.dispatch_flash_decode_partial(q_local, self.pool, 0, cu_k, table, scale, max_seqlen_k=max_seqlen_k,
                                          o_part=self.o_part, lse_part=self.lse_part, workspace=self.ws)
 

@@ -118,3 +118,29 @@ def test_workspace_size_plan(yf):
     row256 = 8 * 257 * 4
     assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 259 * 2 * row256
     long_pool.close()
+
+
+def test_attention_options_are_explicit_and_validated(yf):
+    """The pool's options replace every hidden tuning switch: zero is the default, unknown values
+    are refused and leave the options unchanged, and the workspace query follows the schedule."""
+    pool = yf.PagedKvPool(1, 4096, 8, 128, device=None)
+    assert pool.options() == {"schedule": 0, "chunk_tiles": 0, "copy_stages": 0, "merge": 0,
+                              "prefill_kernel": 0, "wait_limit_us": 0}
+    pool.set_options(schedule=_abi.YF_SCHED_CHUNKED, chunk_tiles=8, wait_limit_us=20000)
+    assert pool.options()["schedule"] == 1 and pool.options()["chunk_tiles"] == 8
+    for bad in ({"schedule": 2}, {"copy_stages": 2}, {"merge": 5}, {"prefill_kernel": -1},
+                {"chunk_tiles": -1}, {"wait_limit_us": 61_000_000}):
+        with pytest.raises(yf.YfError) as e:
+            pool.set_options(**bad)
+        assert e.value.code == _abi.YF_E_INVALID, bad
+    assert pool.options()["chunk_tiles"] == 8
+    o = _abi.AttnOptions()
+    o.reserved[3] = 1
+    assert yf.lib().yf_pool_set_options(pool.handle, ctypes.byref(o)) == _abi.YF_E_INVALID
+    # the chunked schedule sizes its workspace by chunks, the persistent one by CTAs
+    L = yf.lib()
+    chunked = L.yf_attn_workspace_size(pool.handle, 32, 16, 1, 32768)
+    pool.set_options(schedule=0, chunk_tiles=0)
+    persistent = L.yf_attn_workspace_size(pool.handle, 32, 16, 1, 32768)
+    assert chunked > 0 and persistent > 0 and chunked != persistent
+    assert L.yf_pool_plant_counter(pool.handle, 0, 1, None) == _abi.YF_E_INVALID   # host-only pool

@@ -1,6 +1,4 @@
 """Batched paged decode on the GPU against the oracle (max |err| <= 2e-3)."""
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -65,19 +63,18 @@ def test_decode_batch_ragged_with_outliers(yf, oracle, cuda):
     assert np.abs(got - ref).max() <= TOL
     # the schedule must not change the result beyond rounding: persistent with 3 copy stages;
     # chunked with 8-tile chunks merged by the last CTA or by the separate combine kernel; one chunk
-    chunked = {"YF_PERSISTENT": "0"}
-    for env in ({"YF_DECODE_STAGES": "3"}, {**chunked, "YF_CHUNK_TILES": "8"},
-                {**chunked, "YF_CHUNK_TILES": "8", "YF_FUSED_COMBINE": "0"},
-                {**chunked, "YF_CHUNK_TILES": "24", "YF_DECODE_STAGES": "3"}, {**chunked, "YF_CHUNK_TILES": "100000"}):
-        os.environ.update(env)
+    chunked = {"schedule": _abi.YF_SCHED_CHUNKED}
+    for opts in ({"copy_stages": 3}, {**chunked, "chunk_tiles": 8},
+                 {**chunked, "chunk_tiles": 8, "merge": _abi.YF_MERGE_SEPARATE},
+                 {**chunked, "chunk_tiles": 24, "copy_stages": 3}, {**chunked, "chunk_tiles": 100000}):
+        pool.set_options(**opts)
         try:
             alt = run_decode(yf, pool, wl, q, cuda)
             alt2 = run_decode(yf, pool, wl, q, cuda)   # counters reset between calls
         finally:
-            for key in env:
-                del os.environ[key]
-        assert np.abs(alt - ref).max() <= TOL, env
-        assert np.array_equal(alt, alt2), env
+            pool.set_options(schedule=0, chunk_tiles=0, copy_stages=0, merge=0)
+        assert np.abs(alt - ref).max() <= TOL, opts
+        assert np.array_equal(alt, alt2), opts
     assert pool.status() == 0
     pool.close()
 

@@ -1,24 +1,23 @@
 """Causal chunked prefill on the tcgen05 tensor-core kernel against the oracle."""
-import os
-
 import numpy as np
 import pytest
 import torch
 
 from helpers import TOL, filled_pool, queries
+from qwen36_server_b200 import _abi
 from qwen36_server_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
 
 
 def run_prefill(yf, pool, wl, q, cuda, tc=True):
-    os.environ["YF_PREFILL_TC"] = "1" if tc else "0"
+    pool.set_options(prefill_kernel=_abi.YF_PREFILL_AUTO if tc else _abi.YF_PREFILL_SPLITKV)
     try:
         out = yf.forward_attn_prefill_paged(torch.from_numpy(q).to(cuda), pool, 0, wl.cu_q, wl.cu_k,
                                             torch.from_numpy(wl.block_table).to(cuda), yf.default_scale(wl.head_dim))
         return out.float().cpu().numpy()
     finally:
-        del os.environ["YF_PREFILL_TC"]
+        pool.set_options(prefill_kernel=_abi.YF_PREFILL_AUTO)
 
 
 def test_prefill_tc_ragged(yf, oracle, cuda):
