@@ -348,17 +348,75 @@ def make_workload(name: str, rank: int, layers: int = 0):
     return fn(seed=base_seed + 1000 * rank)
 
 
+def partition(wl_full, world: int, rank: int):
+    """This rank's share of the workload at N GPUs, and how the job is split:
+    - "slots": independent entries bin-packed by context over the GPUs (LPT); the same job at
+      every N (strong scaling), no collective on the data path;
+    - "sharded": the one long sequence split by kv head x key range (partials all-gathered);
+    - "replica": a workload with fewer entries than GPUs runs whole on every GPU (weak scaling)."""
+    from qwen36_server_b200 import sharding as S
+    from qwen36_server_b200 import workloads as W
+
+    if world == 1:
+        return wl_full, "slots", [list(range(wl_full.batch))]
+    if wl_full.name == "decode_long":
+        return wl_full, "sharded", None
+    if wl_full.batch >= world:
+        bins = S.lpt_partition(wl_full.ctx, world)
+        return W.subset(wl_full, bins[rank], seed=wl_full.seed + 1000 * rank), "slots", bins
+    return make_workload(wl_full.name, rank), "replica", None
+
+
+class Timer:
+    """Device time of passes of `steps` replays on one stream.  The pass count is agreed over the
+    ranks (a calibration pass, max over ranks), so that steps holding collectives stay in step;
+    passes run until `min_s` seconds of GPU time have elapsed.  Returns the median pass's ms per
+    step (max over ranks is taken by the caller) and the number of passes."""
+
+    def __init__(self, stream, world: int):
+        import torch
+
+        self.torch, self.stream, self.world = torch, stream, world
+
+    def _pass(self, run, steps: int) -> float:
+        torch = self.torch
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        for _ in range(steps):
+            run()
+        b.record(self.stream)
+        b.synchronize()
+        return a.elapsed_time(b)
+
+    def agreed(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        import torch.distributed as dist
+
+        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def run(self, run, steps: int, min_s: float, barrier):
+        first = self.agreed(self._pass(run, steps))
+        n = max(3, min(2000, int(-(-min_s * 1e3 // max(first, 1e-3)))))
+        barrier()
+        ms = [self._pass(run, steps) / steps for _ in range(n)]
+        return statistics.median(ms), n
+
+
 def gpu_arm(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
 
-    sharded = args.config == "decode_long" and world > 1
-    wl = make_workload(args.config, 0 if sharded else rank, args.layers)
+    wl_full = make_workload(args.config, 0, args.layers)
+    wl, mode, bins = partition(wl_full, world, rank)
+    sharded = mode == "sharded"
     layers_resident = wl.n_layers
     if args.config in ("mtp_verify", "tree_verify"):
         free = torch.cuda.mem_get_info(local_rank)[0]
         per_layer = wl.kv_bytes(1)
-        layers_resident = max(1, min(wl.n_layers, int(0.8 * free // per_layer)))
+        layers_resident = max(1, min(wl.n_layers, int(0.8 * free // max(per_layer, 1))))
     step = ShardedStep(wl, local_rank, rank, world) if sharded else Step(wl, local_rank, layers_resident)
     stream = step.stream
     if args.no_graph:
@@ -372,30 +430,25 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
             dist.barrier()
         torch.cuda.synchronize()
 
+    timer = Timer(stream, world)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             run_step()
         barrier()
         clocks = ClockSampler(local_rank)
         clocks.start()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(args.steps):
-            run_step()
-        t1.record(stream)
+        ms, passes = timer.run(run_step, args.steps, args.min_seconds, barrier)
         barrier()
-        ms = t0.elapsed_time(t1) / args.steps
 
         # dominant kernel: the attention call alone, events around each replay
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
+        n_ev = max(args.steps, 50)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ev)]
         for a, b in evs:
             a.record(stream)
             run_attn()
             b.record(stream)
         torch.cuda.synchronize()
-        attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps / wl.n_layers
+        attn_ms = sum(a.elapsed_time(b) for a, b in evs) / n_ev / wl.n_layers
 
         # end to end through the public API with host buffers: H2D of the step's inputs, D2H of
         # the output, every step
@@ -404,23 +457,18 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         h_out = torch.empty(step.out.shape, dtype=step.out.dtype, pin_memory=True)
         bytes_in = sum(h.numel() * h.element_size() for h, _ in h_in)
         bytes_out = h_out.numel() * h_out.element_size()
+
+        def e2e_step():
+            for h, d in h_in:
+                d.copy_(h, non_blocking=True)
+            run_step()
+            h_out.copy_(step.out, non_blocking=True)
+
         for _ in range(max(1, args.warmup)):
-            for h, d in h_in:
-                d.copy_(h, non_blocking=True)
-            run_step()
-            h_out.copy_(step.out, non_blocking=True)
+            e2e_step()
         barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            for h, d in h_in:
-                d.copy_(h, non_blocking=True)
-            run_step()
-            h_out.copy_(step.out, non_blocking=True)
-        e1.record(stream)
+        e2e_ms, _ = timer.run(e2e_step, args.steps, args.min_seconds / 3, barrier)
         barrier()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
         clk = clocks.stop()
 
     t = torch.tensor([ms, e2e_ms, attn_ms], dtype=torch.float64, device=step.dev)
@@ -429,8 +477,11 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     ms, e2e_ms, attn_ms = t.tolist()
     status = step.pool.status()
 
-    tokens = step.T * (1 if sharded else world)
-    kv_bytes = wl.kv_bytes() // (world if sharded else 1)  # per GPU
+    if mode == "replica":
+        tokens = step.T * world
+    else:
+        tokens = int(wl_full.q_rows.sum())   # the same job at every N
+    kv_bytes = wl.kv_bytes() // (world if sharded else 1)  # this GPU's
     hbm, tflops, peak_kind = peaks()
     alg_bytes_attn = wl.kv_bytes(1) // (world if sharded else 1)
     achieved_gbs = alg_bytes_attn / (attn_ms * 1e-3) / 1e9
@@ -440,13 +491,23 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     else:
         roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = profile_traffic(args.config)
+    roof["traffic"] = profile_traffic(args.config) if world == 1 else None
     roof["kernel"] = dominant_kernel(args.config) + (" (this rank's partial over its shard)" if sharded
                                                       else " (one attention call)")
     roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback"
     roof["algorithmic_bytes_per_launch"] = alg_bytes_attn
     roof["launch_ms"] = attn_ms
 
+    if mode == "slots" and world > 1:
+        loads = [int(wl_full.ctx[b].sum()) for b in bins]
+        parallelism = (f"slots LPT-packed by context over {world} GPUs (same {wl_full.batch} slots at every N, "
+                       "no collective on the data path)")
+    elif sharded:
+        parallelism = f"kv-head x sequence sharded x{world} (partials all-gathered over NCCL, LSE combine)"
+    elif mode == "replica":
+        parallelism = f"replicas x{world} (fewer entries than GPUs: each GPU runs the whole workload)"
+    else:
+        parallelism = "one GPU"
     line = {
         "metric": METRIC,
         "value": tokens / (ms * 1e-3),
@@ -456,40 +517,94 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "strong" if sharded else "weak",
+        "scaling": "weak" if mode == "replica" else "strong",
         "vs_baseline": None,
         "dtype": "f16 (int8 KV unpacked exactly to f16 for mma, f32 accumulate)",
         "data": "synthetic (seeded N(0,1) K/V, fragmented seeded page tables)",
         "config": {
-            "workload": describe(wl),
-            "slots_per_gpu": wl.batch,
-            "query_rows_per_gpu": step.T,
-            "sum_ctx_per_gpu": int(wl.ctx.sum()),
+            "workload": describe(wl_full),
+            "slots_this_gpu": wl.batch,
+            "query_rows_this_gpu": step.T,
+            "sum_ctx_this_gpu": int(wl.ctx.sum()),
             "layers": wl.n_layers,
             "layers_resident": step.layers,
-            "kv_bytes_per_step_per_gpu": kv_bytes,
-            "l2": "inputs larger than L2: the pool read per step exceeds 126 MB" if wl.kv_bytes(1) > 126e6
+            "kv_bytes_per_step_this_gpu": kv_bytes,
+            "l2": "inputs larger than L2: the pool read per step exceeds 126 MB" if wl_full.kv_bytes(1) > 126e6
             else "pool fits in L2 (small workload)",
-            "parallelism": (f"kv-head x sequence sharded x{world} (partials all-gathered over NCCL, LSE combine)"
-                            if sharded else f"slot-sharded x{world} (each rank its own slots, no collective)"),
+            "parallelism": parallelism,
             "launch": "direct C-ABI calls" if args.no_graph else (
                 "CUDA graph replay of the step (partial, NCCL all-gather, combine)" if sharded
                 else "CUDA graph replay of the step's C-ABI calls"),
+            "timing": f"median of {passes} passes of {args.steps} steps (>= {args.min_seconds} s of GPU time), "
+                      "CUDA events on the launching stream, max over ranks",
         },
-        "kv_gbs": kv_bytes * world / (ms * 1e-3) / 1e9,
+        "kv_gbs": (wl_full.kv_bytes() if mode != "replica" else wl.kv_bytes() * world) / (ms * 1e-3) / 1e9,
         "hbm_frac_step": kv_bytes / (ms * 1e-3) / 1e9 / hbm,
         "roofline": roof,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": bytes_in,
-                "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms,
+                "note": "this GPU's inputs from pinned host memory and its output back, every step"},
         "gpu_launches": step.launches_per_step() * args.steps,
         "clocks": clk,
         "device_status": status,
     }
+    if mode == "slots" and world > 1:
+        mean = sum(loads) / world
+        line["partition"] = {"keys_per_gpu": loads, "imbalance": max(loads) / mean,
+                             "limiter": "the largest GPU share (LPT imbalance) plus each GPU's fixed launch and "
+                                        "merge latency, which no longer shrink with N"}
     if sharded and hasattr(step, "release"):
         step.release()
+    if world > 1 and args.config == "decode_batch" and not args.no_long:
+        del step
+        torch.cuda.empty_cache()
+        line["decode_long_sharded"] = long_sharded_leg(args, rank, world, local_rank)
     if rank == 0 and not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(wl_full, args.cpu_seconds)
     return line
+
+
+def long_sharded_leg(args, rank: int, world: int, local_rank: int) -> dict:
+    """The 131072-key decode at the same N: kv head x key-range shards, partial decode, NCCL
+    all-gather of the packed partials, LSE combine; replayed as one CUDA graph per rank."""
+    import torch
+    import torch.distributed as dist
+
+    wl = make_workload("decode_long", 0)
+    step = ShardedStep(wl, local_rank, rank, world)
+    step.capture()
+    timer = Timer(step.stream, world)
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.cuda.stream(step.stream):
+        for _ in range(max(3, args.warmup)):
+            step.g_step.replay()
+        barrier()
+        ms, passes = timer.run(step.g_step.replay, args.steps, max(0.5, args.min_seconds / 3), barrier)
+        barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
+        for a, b in evs:
+            a.record(step.stream)
+            step.g_attn.replay()
+            b.record(step.stream)
+        torch.cuda.synchronize()
+        part_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    t = torch.tensor([ms, part_ms], dtype=torch.float64, device=step.dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, part_ms = t.tolist()
+    status = step.pool.status()
+    step.release()
+    hbm, _, _ = peaks()
+    shard_bytes = wl.kv_bytes(1) // world
+    return {"workload": describe(wl), "ms_per_step": ms, "tokens_per_s": 1.0 / (ms * 1e-3),
+            "partial_ms": part_ms, "partial_hbm_frac": shard_bytes / (part_ms * 1e-3) / 1e9 / hbm,
+            "exchange_and_combine_ms": ms - part_ms, "passes": passes,
+            "limiter": "the NCCL all-gather of the packed partials plus the combine launch (latency, a few KB "
+                       "moved) on top of the shard's partial decode",
+            "parallelism": f"kv-head x sequence sharded x{world}", "device_status": status}
 
 
 def describe(wl) -> str:
@@ -501,27 +616,37 @@ def describe(wl) -> str:
 
 
 # ---------------------------------------------------------------------------------------
-# CPU: the oracle's restatement of the path on a bounded sample
+# CPU: the oracle's restatement of the path on the workload (or a bounded sample of it)
 
 
 class CpuSample:
-    """A sample of the workload's entries (their own keys only) prepared for the CPU oracle."""
+    """The workload's entries (their own keys) prepared for the CPU oracle.  Entries are taken,
+    median context first, while their (query row x key) pairs fit `max_pairs`; a single entry
+    that alone exceeds it keeps only its last query rows (a shorter chunk over the same prefix)."""
 
-    def __init__(self, wl, max_tokens: int):
+    def __init__(self, wl, max_pairs: float):
         from qwen36_server_b200 import workloads as W
 
         self.O = graft.load_oracle()
-        order = np.argsort(wl.ctx)
+        max_pairs = max_pairs / wl.n_layers   # every layer repeats the step's work
+        pairs = wl.ctx * wl.q_rows
+        order = np.argsort(wl.ctx, kind="stable")
         pick, tot = [], 0
         for i in order[len(order) // 2:].tolist() + order[:len(order) // 2].tolist():   # median first
-            if tot + wl.ctx[i] > max_tokens and pick:
+            if tot + pairs[i] > max_pairs and pick:
                 continue
             pick.append(i)
-            tot += int(wl.ctx[i])
+            tot += int(pairs[i])
         pick = sorted(pick)
-        self.sub = W.Workload("cpu", wl.n_q_heads, wl.n_kv_heads, wl.head_dim, ctx=wl.ctx[pick],
-                              q_rows=wl.q_rows[pick], page_size=wl.page_size, group_size=wl.group_size,
-                              outlier_frac=wl.outlier_frac, seed=wl.seed)
+        ctx, q_rows = wl.ctx[pick].copy(), wl.q_rows[pick].copy()
+        if len(pick) == 1 and pairs[pick[0]] > max_pairs and q_rows[0] > 1:
+            keep = max(1, int(max_pairs // ctx[0]))
+            ctx[0] -= q_rows[0] - keep
+            q_rows[0] = keep
+        self.full = len(pick) == wl.batch and np.array_equal(q_rows, wl.q_rows)
+        self.sub = W.Workload("cpu", wl.n_q_heads, wl.n_kv_heads, wl.head_dim, ctx=ctx, q_rows=q_rows,
+                              page_size=wl.page_size, group_size=wl.group_size, outlier_frac=wl.outlier_frac,
+                              seed=wl.seed)
         s = self.sub
         self.desc = self.O.PoolDesc(1, s.n_pages, s.n_kv_heads, s.head_dim, s.page_size, s.group_size)
         rng = np.random.default_rng(s.seed)
@@ -535,7 +660,7 @@ class CpuSample:
         starts = np.concatenate([[0], np.cumsum(s.ctx)])[:-1]
         for b in range(s.batch):
             hist[starts[b] + s.prefix[b]: starts[b] + s.ctx[b]] = False
-        self.O.np_kv_write_rows(self.desc, self.pool, 0, k[hist], v[hist], entry[hist], pos[hist], s.block_table)
+        self.O.c_kv_write_rows(self.desc, self.pool, 0, k[hist], v[hist], entry[hist], pos[hist], s.block_table)
         self.new = (k[~hist], v[~hist], entry[~hist], pos[~hist])
         self.q = rng.standard_normal((int(s.q_rows.sum()), s.n_q_heads, s.head_dim)).astype(np.float16)
         self.threads = os.cpu_count() or 1
@@ -550,9 +675,21 @@ class CpuSample:
             self.O.c_attn(self.desc, self.pool, 0, self.q, s.cu_q, s.cu_k, s.block_table,
                           1.0 / np.sqrt(s.head_dim), self.threads)
 
+    def describe(self, wl, steps: int) -> str:
+        what = "the whole workload" if self.full else (
+            f"{self.sub.batch} of {wl.batch} entries, {int(self.sub.q_rows.sum())} of {int(wl.q_rows.sum())} "
+            f"query rows")
+        return (f"{what} ({int(self.sub.ctx.sum())} keys, {self.n_layers} layer(s)) per step, {steps} steps; "
+                "oracle/yf_oracle.c double-precision attention + Q8_0 scatter on all host threads")
+
+
+# pairs of (query row, key) in one CPU step: the whole decode_batch step (266k pairs, ~0.5 s on
+# 16 threads), a bounded sample of the larger workloads
+CPU_MAX_PAIRS = 3.0e5
+
 
 def cpu_baseline(wl, seconds: float):
-    samp = CpuSample(wl, max_tokens=int(2.5e5))
+    samp = CpuSample(wl, max_pairs=CPU_MAX_PAIRS)
     samp.step()
     t0 = time.perf_counter()
     n = 0
@@ -563,10 +700,9 @@ def cpu_baseline(wl, seconds: float):
             break
     dt = (time.perf_counter() - t0) / n
     return {"value": samp.tokens / dt, "unit": "tokens/s", "cores": samp.threads, "kind": "port",
-            "sample": f"{samp.sub.batch} of {wl.batch} entries ({int(samp.sub.ctx.sum())} keys, "
-                      f"{samp.n_layers} layer(s)), {n} steps; oracle/yf_oracle.c double-precision attention "
-                      f"+ Q8_0 scatter" + ("; causal rows stand in for the trie mask (same keys but the "
-                                           "skipped branch nodes)" if wl.trie is not None else "")}
+            "same_config": samp.full,
+            "sample": samp.describe(wl, n) + ("; causal rows stand in for the trie mask (same keys but the "
+                                              "skipped branch nodes)" if wl.trie is not None else "")}
 
 
 def prep_arm(args, rank: int, world: int, local_rank: int):
@@ -851,7 +987,7 @@ def reference_arm(args):
                                                     "fork (no Rust toolchain here); bench.py --config snapshot_records "
                                                     "reports the oracle's CRC-32C as its cpu_baseline"}
     wl = make_workload(args.config, 0)
-    samp = CpuSample(wl, max_tokens=int(args.ref_tokens))
+    samp = CpuSample(wl, max_pairs=args.ref_pairs)
     for _ in range(args.warmup):
         samp.step()
     t0 = time.perf_counter()
@@ -862,12 +998,14 @@ def reference_arm(args):
     return {
         "impl": "reference",
         "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong" if wl.batch > 1 else "weak",
         "vs_baseline": None, "dtype": "f64 (oracle)", "data": "synthetic",
-        "config": {"workload": describe(wl), "sample": describe(samp.sub)},
+        "config": {"workload": describe(wl), "sample": describe(samp.sub), "same_config": samp.full},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": samp.threads, "kind": "port",
-                         "sample": f"{samp.sub.batch} of {wl.batch} entries per step; the reference's candle "
-                                   "CPU path cannot be built here (no Rust toolchain, fork not vendored)"},
+                         "same_config": samp.full,
+                         "sample": samp.describe(wl, args.steps) + "; the reference's candle CPU path cannot be "
+                                                                   "built here (no Rust toolchain, fork not vendored)"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -884,7 +1022,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--ref-tokens", type=float, default=1.2e5)
+    ap.add_argument("--ref-pairs", type=float, default=CPU_MAX_PAIRS,
+                    help="--impl reference: (query row x key) pairs per CPU step (the whole decode_batch step fits)")
+    ap.add_argument("--min-seconds", type=float, default=1.5,
+                    help="GPU time the timed passes of --steps steps must cover (median pass reported)")
+    ap.add_argument("--no-long", action="store_true", help="N>1: skip the sharded decode_long leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="mtp_verify only: stack this many layers instead of 36 (one launch per layer keeps "
                          "its shape; for profiling a launch with a few GB resident, not a bench line)")

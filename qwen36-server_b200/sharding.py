@@ -1,4 +1,10 @@
-"""Long-context decode split across GPUs: kv heads first, then contiguous key ranges.
+"""Multi-GPU partitions of the attention path.
+
+Independent slots (continuous-batched decode, MTP verify) go to GPUs by longest-processing-time
+bin packing on their context (lpt_partition): each GPU holds its slots' pages in its own pool and
+nothing crosses NVLink on the data path.
+
+Long-context decode is split across GPUs: kv heads first, then contiguous key ranges.
 
 A sequence too long for one GPU to read quickly (the 131072-key, 2-kv-head decode) is
 split into world = n_head_groups x n_seq shards.  Rank r owns kv-head group r % n_head_groups
@@ -18,6 +24,24 @@ from typing import List
 import torch
 
 from . import paged_attn as pa
+
+
+def lpt_partition(costs, n_bins: int) -> List[List[int]]:
+    """Longest-processing-time-first assignment of independent slots to ``n_bins`` GPUs: slots
+    in order of falling cost (ties by index), each to the bin with the least cost so far (ties by
+    bin index).  A slot's cost is the KV bytes its attention reads, proportional to its context.
+    Returns each bin's slot indices in ascending order; deterministic for a given input."""
+    if n_bins < 1:
+        raise ValueError("n_bins must be >= 1")
+    c = [int(x) for x in costs]
+    order = sorted(range(len(c)), key=lambda i: (-c[i], i))
+    load = [0] * n_bins
+    bins: List[List[int]] = [[] for _ in range(n_bins)]
+    for i in order:
+        j = min(range(n_bins), key=lambda b: (load[b], b))
+        bins[j].append(i)
+        load[j] += c[i]
+    return [sorted(b) for b in bins]
 
 
 @dataclass(frozen=True)

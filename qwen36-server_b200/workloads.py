@@ -151,6 +151,19 @@ def tree_verify(seed: int = 6, n_slots: int = 64, nodes: int = 8, n_layers: int 
                     trie=trie)
 
 
+def subset(wl: Workload, entries, seed: int) -> Workload:
+    """The entries ``entries`` of ``wl`` (one GPU's share of its slots) as a workload of their own,
+    with a fragmented table over a pool sized for just those entries."""
+    idx = list(entries)
+    trie = None
+    if wl.trie is not None:
+        starts = np.concatenate([[0], np.cumsum(wl.q_rows)])
+        trie = np.concatenate([wl.trie[starts[b]:starts[b + 1]] for b in idx]) if idx else wl.trie[:0]
+    return Workload(wl.name, wl.n_q_heads, wl.n_kv_heads, wl.head_dim, ctx=wl.ctx[idx], q_rows=wl.q_rows[idx],
+                    page_size=wl.page_size, group_size=wl.group_size, n_layers=wl.n_layers,
+                    outlier_frac=wl.outlier_frac, seed=seed, trie=trie)
+
+
 CONFIGS = {
     "decode_small": decode_small,
     "decode_batch": decode_batch,

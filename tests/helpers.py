@@ -44,3 +44,43 @@ def queries(wl, seed=1):
     rng = np.random.default_rng(seed)
     T = int(wl.q_rows.sum())
     return rng.standard_normal((T, wl.n_q_heads, wl.head_dim)).astype(np.float16)
+
+
+def device_pool(yf, wl, seed=0, n_layers=1, layer=0, chunk_rows=1 << 18):
+    """A pool holding every key of every entry of ``wl`` in ``layer``, the K/V rows drawn on the
+    device (seeded N(0,1), with the workload's outliers) and written with launch_append_multi in
+    bounded row chunks: the full-size workloads are too large to stage their f16 rows on the host."""
+    dev = torch.device("cuda", 0)
+    pool = yf.PagedKvPool(n_layers, wl.n_pages, wl.n_kv_heads, wl.head_dim, wl.page_size, wl.group_size, device=0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    bt = torch.from_numpy(wl.block_table).to(dev)
+    for b in range(wl.batch):
+        n = int(wl.ctx[b])
+        for s in range(0, n, chunk_rows):
+            m = min(chunk_rows, n - s)
+            k = W.kv_rows_torch(gen, m, wl.n_kv_heads, wl.head_dim, wl.outlier_frac, dev)
+            v = W.kv_rows_torch(gen, m, wl.n_kv_heads, wl.head_dim, wl.outlier_frac, dev)
+            yf.launch_append_multi(pool, layer, k, v, [0, m], [s], bt[b:b + 1], max_rows=m)
+    torch.cuda.synchronize()
+    return pool
+
+
+def gathered_image(oracle, pool, wl, entries, layer=0):
+    """The pages of ``entries`` copied out of the device pool into a compact oracle image, with
+    their block-table rows renumbered onto it: (desc, image, sub-workload of those entries)."""
+    P = wl.page_size
+    rows = [wl.block_table[b, :-(-int(wl.ctx[b]) // P)] for b in entries]
+    pages = np.unique(np.concatenate(rows)) if rows else np.zeros(0, np.int32)
+    where = {int(p): i for i, p in enumerate(pages.tolist())}
+    width = max(len(r) for r in rows)
+    table = np.zeros((len(entries), width), np.int32)
+    for i, r in enumerate(rows):
+        table[i, :len(r)] = [where[int(p)] for p in r.tolist()]
+    view = pool.layer_bytes_view(layer).view(pool.n_pages, pool.page_bytes)
+    img = view.index_select(0, torch.from_numpy(pages.astype(np.int64)).to(view.device)).cpu().numpy().reshape(-1)
+    desc = oracle.PoolDesc(1, len(pages), wl.n_kv_heads, wl.head_dim, wl.page_size, wl.group_size)
+    sub = W.Workload("sub", wl.n_q_heads, wl.n_kv_heads, wl.head_dim, ctx=wl.ctx[list(entries)],
+                     q_rows=wl.q_rows[list(entries)], page_size=wl.page_size, group_size=wl.group_size,
+                     block_table=table, n_pages=len(pages))
+    return desc, img, sub

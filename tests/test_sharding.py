@@ -125,3 +125,23 @@ def test_gloo_ranks_all_gather_and_merge(world):
     for rank, err in res:
         assert isinstance(err, float), (rank, err)
         assert err < 1e-5, (rank, err)
+
+
+def test_lpt_partition_balances_and_covers_every_slot():
+    from qwen36_server_b200 import workloads as W
+
+    wl = W.decode_batch()
+    for n in (1, 2, 4, 8, 16):
+        bins = S.lpt_partition(wl.ctx, n)
+        flat = sorted(i for b in bins for i in b)
+        assert flat == list(range(wl.batch))
+        loads = [int(wl.ctx[b].sum()) for b in bins]
+        # LPT's bound: no bin exceeds the mean by more than the largest single slot
+        assert max(loads) <= wl.ctx.sum() / n + wl.ctx.max()
+        assert S.lpt_partition(wl.ctx, n) == bins          # deterministic
+    assert S.lpt_partition([5, 5, 5, 5], 2) == [[0, 2], [1, 3]]
+    assert S.lpt_partition([9, 1, 1, 1], 2) == [[0], [1, 2, 3]]
+    mv = W.mtp_verify(n_layers=1)
+    bins = S.lpt_partition(mv.ctx, 8)
+    loads = [int(mv.ctx[b].sum()) for b in bins]
+    assert max(loads) / (sum(loads) / 8) < 1.05                # 64 slots over 8 GPUs: within 5%
