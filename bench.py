@@ -855,6 +855,8 @@ def records_arm(args, rank: int, world: int, local_rank: int):
     pages = torch.randperm(n, generator=g, device=dev).int()
     hashes = torch.arange(n, device=dev, dtype=torch.int64) * 0x9E3779B97F4A7C15 % (2 ** 62)
     idx = torch.arange(n, device=dev, dtype=torch.int32)
+    prev = torch.cat([torch.zeros(1, device=dev, dtype=torch.int64), hashes[:-1]])
+    tokens = torch.randint(0, 151936, (n, wl.page_size), generator=g, device=dev, dtype=torch.int32)
     rb = src.record_bytes
     rec = torch.empty(n * rb, dtype=torch.uint8, device=dev)
     ok = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -864,9 +866,10 @@ def records_arm(args, rank: int, world: int, local_rank: int):
     s = P(stream.cuda_stream)
 
     def run():
-        if L.yf_pool_export_records(src.handle, n, ptr(pages), ptr(hashes), ptr(idx), ptr(rec), s):
+        if L.yf_pool_export_records(src.handle, n, ptr(pages), ptr(hashes), ptr(prev), ptr(idx), ptr(tokens),
+                                    ptr(rec), s):
             raise RuntimeError(L.yf_last_error().decode())
-        if L.yf_pool_import_records(dst.handle, n, ptr(pages), ptr(rec), ptr(ok), s):
+        if L.yf_pool_import_records(dst.handle, n, ptr(pages), ptr(rec), ptr(hashes), ptr(tokens), ptr(ok), s):
             raise RuntimeError(L.yf_last_error().decode())
 
     def barrier():
@@ -893,11 +896,12 @@ def records_arm(args, rank: int, world: int, local_rank: int):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            if L.yf_pool_export_records(src.handle, n, ptr(pages), ptr(hashes), ptr(idx), ptr(rec), s):
+            if L.yf_pool_export_records(src.handle, n, ptr(pages), ptr(hashes), ptr(prev), ptr(idx), ptr(tokens),
+                                        ptr(rec), s):
                 raise RuntimeError(L.yf_last_error().decode())
             h.copy_(rec, non_blocking=True)
             rec.copy_(h, non_blocking=True)
-            if L.yf_pool_import_records(dst.handle, n, ptr(pages), ptr(rec), ptr(ok), s):
+            if L.yf_pool_import_records(dst.handle, n, ptr(pages), ptr(rec), ptr(hashes), ptr(tokens), ptr(ok), s):
                 raise RuntimeError(L.yf_last_error().decode())
         e1.record(stream)
         barrier()

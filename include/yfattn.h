@@ -57,7 +57,7 @@
 extern "C" {
 #endif
 
-#define YFATTN_ABI_VERSION 1
+#define YFATTN_ABI_VERSION 2
 
 /* Return codes of every entry point. */
 #define YF_OK 0
@@ -156,6 +156,14 @@ YF_API int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear);
 #define YF_MERGE_SEPARATE 1    /* chunked schedule: a separate combine launch merges the partials */
 #define YF_PREFILL_AUTO 0      /* tcgen05 prefill kernel where it applies (>= 128 rows per kv head) */
 #define YF_PREFILL_SPLITKV 1   /* every query block on the split-KV kernel */
+/* The persistent decode's CTAs wait for one another's split partials, so all of them must be
+ * resident at once.  Its grid never exceeds one resident wave, so against other kernels that
+ * finish by themselves (other streams, other pools) a plain launch completes; only kernels that
+ * hold SMs indefinitely (another process's persistent kernel under MPS) can starve it, and then
+ * its bounded waits flag YF_DEV_TIMEOUT.  A cooperative launch rules that out at launch time and
+ * costs 2-3 us per call (measured on B200). */
+#define YF_LAUNCH_PLAIN 0        /* plain launch (default) */
+#define YF_LAUNCH_COOPERATIVE 1  /* cooperative launch: co-residency guaranteed by the launch */
 typedef struct yf_attn_options {
     int32_t schedule;        /* YF_SCHED_* */
     int32_t chunk_tiles;     /* chunked schedule: 16-token tiles per CTA; 0 = sized from the grid */
@@ -163,7 +171,8 @@ typedef struct yf_attn_options {
     int32_t merge;           /* YF_MERGE_* */
     int32_t prefill_kernel;  /* YF_PREFILL_* */
     uint32_t wait_limit_us;  /* bound of every in-kernel wait (copies, merges); 0 = 1 000 000 (1 s) */
-    int32_t reserved[10];    /* zero */
+    int32_t launch;          /* YF_LAUNCH_*: how the persistent decode is launched */
+    int32_t reserved[9];     /* zero */
 } yf_attn_options;
 /* Replaces the pool's options (validated: YF_E_INVALID for an unknown value).  Not
  * stream-ordered: set them between calls, not while the pool's kernels run. */
@@ -334,24 +343,38 @@ YF_API int yf_pool_restore_pages(yf_pool* pool, int32_t layer, int32_t n, const 
                                  const void* src, void* stream);
 
 /* ---- snapshot wire records ------------------------------------------------------
- * The prefix cache's page records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:143-145,
- * 237-251): one record per pool page, back to back at a stride of yf_pool_record_bytes,
- *   [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload]
- * little-endian, packed (20-byte header); payload = the page in every layer, layer 0 first
- * (n_layers * yf_pool_page_head_bytes * n_kv_heads bytes); crc32c = CRC-32C (Castagnoli,
- * reflected polynomial 0x82F63B78, preset and final xor 0xFFFFFFFF) of the payload. */
+ * The prefix cache's page records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:141-145,
+ * 237-251, whose page entry is { chain_hash, prev_hash, tokens[], payload }): one record per pool
+ * page, back to back at a stride of yf_pool_record_bytes,
+ *   [u64 chain_hash][u64 prev_hash][u32 page_index][u32 n_tokens][u32 payload_len][u32 crc32c]
+ *   [u32 tokens[page_size]][payload]
+ * little-endian, packed (32 + 4*page_size header bytes, a multiple of 16); n_tokens = page_size;
+ * payload = the page in every layer, layer 0 first (n_layers * yf_pool_page_head_bytes *
+ * n_kv_heads bytes); crc32c = CRC-32C (Castagnoli, reflected polynomial 0x82F63B78, preset and
+ * final xor 0xFFFFFFFF) of the token ids followed by the payload.  The token ids let a reader
+ * tell a chain-hash collision from a hit, as the prefix cache compares tokens before it uses a
+ * cached page (src/prefix_cache.rs:347-356). */
+#define YF_REC_REJECTED 0  /* corrupt: payload_len, n_tokens or CRC wrong, or a bad page id */
+#define YF_REC_RESTORED 1  /* intact and (where expected values were given) the same prefix: restored */
+#define YF_REC_MISMATCH 2  /* intact, but its chain hash or token ids differ from the expected ones */
 YF_API size_t yf_pool_record_bytes(const yf_pool_desc* desc);
-/* Builds n records in device memory d_records (4-byte aligned) from pool pages d_pages[i], with
- * the caller's d_chain_hashes[i] (the prefix chain fingerprint) and d_page_indices[i] (its
- * position in the chain; null: the pool page id); the CRC is computed in the same pass as the
- * copy.  Device arrays; a page id outside the pool flags YF_DEV_BAD_PAGE. */
+/* Builds n records in device memory d_records (16-byte aligned) from pool pages d_pages[i], with
+ * the caller's d_chain_hashes[i] (the prefix chain fingerprint), d_prev_hashes[i] (the previous
+ * page's chain hash), d_page_indices[i] (its position in the chain; null: the pool page id) and
+ * d_tokens (u32 [n][page_size], the page's token ids); null hash or token arrays write zeros.
+ * The CRC is computed in the same pass as the copy.  Device arrays; a page id outside the pool
+ * flags YF_DEV_BAD_PAGE and writes a header with payload_len 0, which every import rejects. */
 YF_API int yf_pool_export_records(yf_pool* pool, int32_t n, const int32_t* d_pages,
-                                  const uint64_t* d_chain_hashes, const uint32_t* d_page_indices,
-                                  void* d_records, void* stream);
-/* Checks the payload_len and CRC-32C of n records in device memory and copies each intact one
- * into pool page d_pages[i] (every layer); d_ok[i] = 1 when restored, 0 when rejected (the page
- * is then left as it was and the caller treats the context as a prefill). */
+                                  const uint64_t* d_chain_hashes, const uint64_t* d_prev_hashes,
+                                  const uint32_t* d_page_indices, const uint32_t* d_tokens, void* d_records,
+                                  void* stream);
+/* Checks n records in device memory (16-byte aligned): payload_len, n_tokens and the CRC-32C, and,
+ * where given, that record i carries d_expect_hashes[i] and the token ids d_expect_tokens[i][*];
+ * copies each intact, matching record into pool page d_pages[i] (every layer).  d_ok[i] = one of
+ * YF_REC_*; a page not restored is left as it was (the caller then treats the context as a
+ * prefill, as the reference does with a record it cannot use). */
 YF_API int yf_pool_import_records(yf_pool* pool, int32_t n, const int32_t* d_pages, const void* d_records,
+                                  const uint64_t* d_expect_hashes, const uint32_t* d_expect_tokens,
                                   uint32_t* d_ok, void* stream);
 
 #ifdef __cplusplus

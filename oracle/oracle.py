@@ -173,19 +173,28 @@ def crc32c(data) -> int:
     return int(lib().yfo_crc32c(_ptr(a) if a.size else None, a.size))
 
 
-def page_records(desc: "PoolDesc", pool: np.ndarray, pages, chain_hashes, page_indices) -> np.ndarray:
-    """The prefix cache's page records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:237-251)
-    of pool-image pages: [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload],
-    little-endian, packed; payload = the page in every layer, layer 0 first."""
+def page_records(desc: "PoolDesc", pool: np.ndarray, pages, chain_hashes, page_indices, prev_hashes=None,
+                 tokens=None) -> np.ndarray:
+    """The prefix cache's page records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:141-145,
+    237-251) of pool-image pages: [u64 chain_hash][u64 prev_hash][u32 page_index][u32 n_tokens]
+    [u32 payload_len][u32 crc32c][u32 tokens[page_size]][payload], little-endian, packed; payload =
+    the page in every layer, layer 0 first; the CRC-32C covers the token ids, then the payload."""
     page_bytes = desc.page_head_bytes * desc.n_kv_heads
     layer_bytes = desc.n_pages * page_bytes
+    P = desc.page_size
+    n = len(pages)
+    prev_hashes = [0] * n if prev_hashes is None else list(prev_hashes)
+    tokens = np.zeros((n, P), np.uint32) if tokens is None else np.asarray(tokens, np.int64).astype(np.uint32)
     out = []
-    for pg, hsh, idx in zip(pages, chain_hashes, page_indices):
+    for i, (pg, hsh, idx) in enumerate(zip(pages, chain_hashes, page_indices)):
         payload = np.concatenate([pool[l * layer_bytes + int(pg) * page_bytes:
                                        l * layer_bytes + (int(pg) + 1) * page_bytes] for l in range(desc.n_layers)])
-        head = np.array([int(hsh) & 0xFFFFFFFF, int(hsh) >> 32, int(idx), payload.size, crc32c(payload)],
+        tok = tokens[i].reshape(P).view(np.uint8)
+        crc = crc32c(np.concatenate([tok, payload]))
+        h, pv = int(hsh) & (2 ** 64 - 1), int(prev_hashes[i]) & (2 ** 64 - 1)
+        head = np.array([h & 0xFFFFFFFF, h >> 32, pv & 0xFFFFFFFF, pv >> 32, int(idx), P, payload.size, crc],
                         np.uint32)
-        out.append(np.concatenate([head.view(np.uint8), payload]))
+        out.append(np.concatenate([head.view(np.uint8), tok, payload]))
     return np.concatenate(out) if out else np.zeros(0, np.uint8)
 
 

@@ -33,7 +33,12 @@ YF_MERGE_IN_KERNEL = 0
 YF_MERGE_SEPARATE = 1
 YF_PREFILL_AUTO = 0
 YF_PREFILL_SPLITKV = 1
+YF_LAUNCH_PLAIN = 0
+YF_LAUNCH_COOPERATIVE = 1
 YF_POOL_COUNTERS = 65536 + 4096
+YF_REC_REJECTED = 0
+YF_REC_RESTORED = 1
+YF_REC_MISMATCH = 2
 
 ERROR_NAMES = {
     YF_E_INVALID: "YF_E_INVALID", YF_E_UNSUPPORTED: "YF_E_UNSUPPORTED", YF_E_NOMEM: "YF_E_NOMEM",
@@ -62,7 +67,7 @@ class AttnOptions(ctypes.Structure):
     _fields_ = [
         ("schedule", ctypes.c_int32), ("chunk_tiles", ctypes.c_int32), ("copy_stages", ctypes.c_int32),
         ("merge", ctypes.c_int32), ("prefill_kernel", ctypes.c_int32), ("wait_limit_us", ctypes.c_uint32),
-        ("reserved", ctypes.c_int32 * 10),
+        ("launch", ctypes.c_int32), ("reserved", ctypes.c_int32 * 9),
     ]
 
 
@@ -106,8 +111,8 @@ SIGNATURES = {
                                      _vp]),
     "yf_attn_combine": (_ci, [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _i32, _i32, _i32, _vp, _vp]),
     "yf_pool_record_bytes": (_sz, [_vp]),
-    "yf_pool_export_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp]),
-    "yf_pool_import_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp]),
+    "yf_pool_export_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "yf_pool_import_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "yf_pool_export_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "yf_pool_restore_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
 }

@@ -1154,9 +1154,9 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
                                  cache);
         if (rc) return rc;
         // every CTA must be resident at once (mergers wait for the parts of other CTAs): the grid
-        // is capped by the occupancy at this shared-memory size and launched cooperatively, so a
-        // grid that cannot be co-resident (another kernel holding SMs) is refused or deferred by
-        // the launch instead of stalling its mergers
+        // is capped by the occupancy at this shared-memory size; with YF_LAUNCH_COOPERATIVE the
+        // launch itself guarantees co-residency (a grid that cannot be co-resident is deferred or
+        // refused instead of stalling its mergers), at 2-3 us per call
         int occ = 0;
         rc = occupancy((const void*)kern, kThreads, smem, dev, cache, &occ);
         if (rc) return rc;
@@ -1174,7 +1174,7 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
         attr[0].id = cudaLaunchAttributeCooperative;
         attr[0].val.cooperative = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = a.pool->opts.launch == YF_LAUNCH_COOPERATIVE ? 1 : 0;
         e = cudaLaunchKernelEx(&cfg, kern, p);
         if (e == cudaSuccess) e = cudaGetLastError();
         return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_persistent launch");

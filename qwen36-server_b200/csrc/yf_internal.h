@@ -140,6 +140,9 @@ struct AttnArgs {
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan);
 
+// Snapshot records: the CRC combine operators of the pool's record shape (yf_snapshot.cu).
+void init_record_ops(yf_pool* pool);
+
 // Tensor-core (tcgen05) causal prefill for query blocks of >= 128 rows per kv head
 // (yf_prefill_tc.cu); needs no workspace.
 bool prefill_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q);

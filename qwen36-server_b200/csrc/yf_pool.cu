@@ -198,6 +198,7 @@ int yf_pool_create(const yf_pool_desc* desc, yf_pool** out_pool) {
     p->refcount.assign(desc->n_pages, 0);
     p->free_stack.resize(desc->n_pages);
     for (int i = 0; i < desc->n_pages; ++i) p->free_stack[i] = desc->n_pages - 1 - i;  // pops 0,1,2,...
+    init_record_ops(p);
     if (desc->device < 0) {  // host-only pool: the page allocator without device memory
         p->desc.device_mem = nullptr;
         *out_pool = p;
@@ -354,6 +355,8 @@ static int check_options(const yf_attn_options* o) {
     if (o->prefill_kernel != YF_PREFILL_AUTO && o->prefill_kernel != YF_PREFILL_SPLITKV)
         return fail(YF_E_INVALID, "prefill_kernel %d unknown", o->prefill_kernel);
     if (o->wait_limit_us > 60u * 1000000u) return fail(YF_E_INVALID, "wait_limit_us above 60 s");
+    if (o->launch != YF_LAUNCH_PLAIN && o->launch != YF_LAUNCH_COOPERATIVE)
+        return fail(YF_E_INVALID, "launch %d unknown", o->launch);
     for (int32_t r : o->reserved)
         if (r) return fail(YF_E_INVALID, "reserved option fields must be zero");
     return YF_OK;

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "yf_device.cuh"
 #include "yf_internal.h"
@@ -26,7 +27,9 @@ namespace {
 
 constexpr uint32_t kCrcPoly = 0x82F63B78u;
 constexpr int kRecThreads = 256;
-constexpr int kRecHeader = 20;
+// CRC combine operators of a pool's records: a shift per thread, the block shift, the preset,
+// a shift per token lane and the token block's multiplier (computed when the pool is created)
+constexpr size_t kRecOps = kRecThreads + 35;
 
 // a * b mod P (reflected; bit 31 = x^0), 32 fixed steps.
 __host__ __device__ __forceinline__ uint32_t gf2_mulmod(uint32_t a, uint32_t b) {
@@ -79,22 +82,35 @@ struct RecParams {
     size_t page_bytes;
     int n_layers;
     int n_pages;
+    int P;                 // tokens per page (= token ids per record)
     const int32_t* pages;
-    const unsigned long long* hashes;
-    const uint32_t* page_index;
-    uint8_t* records;      // export: out; import: in
-    const uint8_t* records_in;
+    const unsigned long long* hashes;       // export: chain hash per record, or null (0)
+    const unsigned long long* prev_hashes;  // export: the previous page's chain hash, or null (0)
+    const uint32_t* page_index;             // export: position in the chain, or null (the page id)
+    const uint32_t* tokens;                 // export: [n][P] token ids, or null (zeros)
+    const unsigned long long* expect_hashes;  // import: chain hash each record must carry, or null
+    const uint32_t* expect_tokens;            // import: [n][P] token ids each record must carry, or null
+    uint8_t* records;      // export: out; import: in (16-byte aligned, stride rec_bytes)
     uint32_t* ok;
     size_t rec_bytes;
+    size_t hdr_bytes;      // 32 + 4 * P
     uint32_t* status;
     int blk_words;         // words of one staged block (a page is 2^j blocks)
     int blks_per_page;
-    // x^(8 * bytes of the block after thread t's words) mod P, x^(8 * block bytes) mod P, and the
-    // preset's term 0xFFFFFFFF * x^(8 * payload) mod P
+    // x^(8 * bytes of the block after thread t's words) mod P, x^(8 * block bytes) mod P
     uint32_t shift[kRecThreads];
     uint32_t blk_shift;
+    // the preset's term 0xFFFFFFFF * x^(8 * (token bytes + payload)) mod P
     uint32_t preset;
+    // x^(8 * token bytes after lane l's token words) and x^(8 * payload bytes): the token block's
+    // register joined in front of the payload's
+    uint32_t tok_shift[32];
+    uint32_t tok_mul;
 };
+
+// Layout of the record header in 32-bit words.
+constexpr int kHdrChain = 0, kHdrPrev = 2, kHdrIndex = 4, kHdrTokens = 5, kHdrLen = 6, kHdrCrc = 7;
+constexpr int kHdrWords = 8;
 
 constexpr int kBlkMaxBytes = 32768;
 
@@ -121,8 +137,21 @@ __device__ uint32_t block_crc(const uint32_t* blk, int n, uint32_t shift, const 
     return r;
 }
 
+// Warp 0: the CRC register (zero preset) of the record's P token words, on every lane.
+__device__ __forceinline__ uint32_t token_crc(const uint32_t* tok, int P, const RecParams& p, const uint32_t (*T)[256]) {
+    const int lane = threadIdx.x & 31;
+    const int w0 = lane * P / 32, w1 = (lane + 1) * P / 32;
+    uint32_t c = 0;
+    for (int w = w0; w < w1; ++w) c = crc_word(c, tok[w], T);
+    uint32_t v = w1 > w0 ? gf2_mulmod(p.tok_shift[lane], c) : 0u;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v ^= __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
 // One CTA per record: the page's blocks (every layer) are staged through shared memory with
-// coalesced loads and stores, and each thread checksums a contiguous run of the staged words.
+// coalesced 16-byte loads and stores, and each thread checksums a contiguous run of the staged
+// words; warp 0 writes and checksums the token ids first.
 __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecParams p) {
     __shared__ uint32_t T[4][256];
     __shared__ uint32_t red[kRecThreads / 32];
@@ -131,40 +160,53 @@ __global__ void __launch_bounds__(kRecThreads) export_records_kernel(const RecPa
     const int r = blockIdx.x;
     const int page = p.pages[r];
     uint8_t* rec = p.records + (size_t)r * p.rec_bytes;
+    uint32_t* h = reinterpret_cast<uint32_t*>(rec);
     const size_t payload = (size_t)p.n_layers * p.page_bytes;
     if (page < 0 || page >= p.n_pages) {
         // a header that every import rejects (length 0), so that a reused staging buffer never
         // passes an older record off as this one
         if (threadIdx.x == 0) {
             atomicOr(p.status, YF_DEV_BAD_PAGE);
-            uint32_t* h = reinterpret_cast<uint32_t*>(rec);
-            for (int k = 0; k < 5; ++k) h[k] = 0u;
+            for (int k = 0; k < kHdrWords; ++k) h[k] = 0u;
         }
         return;
     }
+    uint32_t tok_reg = 0;
+    if (threadIdx.x < 32) {
+        uint32_t* tw = h + kHdrWords;
+        for (int i = threadIdx.x; i < p.P; i += 32) tw[i] = p.tokens ? p.tokens[(size_t)r * p.P + i] : 0u;
+        __syncwarp();
+        tok_reg = token_crc(tw, p.P, p, T);
+    }
     const int nw = p.blk_words;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(rec + kRecHeader);
+    uint4* dst = reinterpret_cast<uint4*>(rec + p.hdr_bytes);
     uint32_t acc = 0;  // the payload's CRC register from a zero preset, over the blocks so far
     for (int l = 0; l < p.n_layers; ++l) {
         const uint8_t* pg = p.base + (size_t)l * p.layer_bytes + (size_t)page * p.page_bytes;
         for (int bi = 0; bi < p.blks_per_page; ++bi) {
             const uint4* g = reinterpret_cast<const uint4*>(pg + (size_t)bi * nw * 4);
-            for (int k = threadIdx.x; k < nw / 4; k += kRecThreads) reinterpret_cast<uint4*>(blk)[k] = __ldcs(g + k);
+            uint4* d = dst + ((size_t)l * p.blks_per_page + bi) * (nw / 4);
+            for (int k = threadIdx.x; k < nw / 4; k += kRecThreads) {
+                const uint4 w = __ldcs(g + k);
+                reinterpret_cast<uint4*>(blk)[k] = w;
+                d[k] = w;
+            }
             __syncthreads();
-            uint32_t* d = dst + ((size_t)l * p.blks_per_page + bi) * nw;
-            for (int k = threadIdx.x; k < nw; k += kRecThreads) d[k] = blk[k];
             const uint32_t b = block_crc(blk, nw, p.shift[threadIdx.x], T, red);
             acc = gf2_mulmod(p.blk_shift, acc) ^ b;
         }
     }
     if (threadIdx.x == 0) {
-        uint32_t* h = reinterpret_cast<uint32_t*>(rec);
         const unsigned long long hash = p.hashes ? p.hashes[r] : 0ull;
-        h[0] = (uint32_t)hash;
-        h[1] = (uint32_t)(hash >> 32);
-        h[2] = p.page_index ? p.page_index[r] : (uint32_t)page;
-        h[3] = (uint32_t)payload;
-        h[4] = p.preset ^ acc ^ 0xFFFFFFFFu;
+        const unsigned long long prev = p.prev_hashes ? p.prev_hashes[r] : 0ull;
+        h[kHdrChain] = (uint32_t)hash;
+        h[kHdrChain + 1] = (uint32_t)(hash >> 32);
+        h[kHdrPrev] = (uint32_t)prev;
+        h[kHdrPrev + 1] = (uint32_t)(prev >> 32);
+        h[kHdrIndex] = p.page_index ? p.page_index[r] : (uint32_t)page;
+        h[kHdrTokens] = (uint32_t)p.P;
+        h[kHdrLen] = (uint32_t)payload;
+        h[kHdrCrc] = p.preset ^ gf2_mulmod(p.tok_mul, tok_reg) ^ acc ^ 0xFFFFFFFFu;
     }
 }
 
@@ -172,20 +214,30 @@ __global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecPa
     __shared__ uint32_t T[4][256];
     __shared__ uint32_t red[kRecThreads / 32];
     __shared__ __align__(16) uint32_t blk[kBlkMaxBytes / 4];
-    __shared__ int s_good;
+    __shared__ uint32_t s_verdict;
     build_tables(T);
     const int r = blockIdx.x;
     const int page = p.pages[r];
-    const uint8_t* rec = p.records_in + (size_t)r * p.rec_bytes;
+    const uint8_t* rec = p.records + (size_t)r * p.rec_bytes;
     const size_t payload = (size_t)p.n_layers * p.page_bytes;
     const uint32_t* h = reinterpret_cast<const uint32_t*>(rec);
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(rec + kRecHeader);
+    const uint4* src = reinterpret_cast<const uint4*>(rec + p.hdr_bytes);
+    uint32_t tok_reg = 0;
+    bool tok_match = true;
+    if (threadIdx.x < 32) {
+        const uint32_t* tw = h + kHdrWords;
+        tok_reg = token_crc(tw, p.P, p, T);
+        bool same = true;
+        if (p.expect_tokens)
+            for (int i = threadIdx.x; i < p.P; i += 32) same &= __ldcg(tw + i) == p.expect_tokens[(size_t)r * p.P + i];
+        tok_match = __all_sync(0xffffffffu, same);
+    }
     const int nw = p.blk_words;
     const int n_blk = p.n_layers * p.blks_per_page;
     uint32_t acc = 0;
     for (int bi = 0; bi < n_blk; ++bi) {
-        const uint32_t* s = src + (size_t)bi * nw;
-        for (int k = threadIdx.x; k < nw; k += kRecThreads) blk[k] = __ldcg(s + k);
+        const uint4* s4 = src + (size_t)bi * (nw / 4);
+        for (int k = threadIdx.x; k < nw / 4; k += kRecThreads) reinterpret_cast<uint4*>(blk)[k] = __ldcg(s4 + k);
         __syncthreads();
         const uint32_t b = block_crc(blk, nw, p.shift[threadIdx.x], T, red);
         acc = gf2_mulmod(p.blk_shift, acc) ^ b;
@@ -193,70 +245,79 @@ __global__ void __launch_bounds__(kRecThreads) import_records_kernel(const RecPa
     if (threadIdx.x == 0) {
         const bool page_ok = page >= 0 && page < p.n_pages;
         if (!page_ok) atomicOr(p.status, YF_DEV_BAD_PAGE);
-        s_good = page_ok && h[3] == (uint32_t)payload && h[4] == (p.preset ^ acc ^ 0xFFFFFFFFu);
-        p.ok[r] = s_good ? 1u : 0u;
+        const bool intact = h[kHdrLen] == (uint32_t)payload && h[kHdrTokens] == (uint32_t)p.P &&
+                            h[kHdrCrc] == (p.preset ^ gf2_mulmod(p.tok_mul, tok_reg) ^ acc ^ 0xFFFFFFFFu);
+        const unsigned long long hash = (unsigned long long)h[kHdrChain] | ((unsigned long long)h[kHdrChain + 1] << 32);
+        const bool match = tok_match && (!p.expect_hashes || p.expect_hashes[r] == hash);
+        const uint32_t v = !(intact && page_ok) ? YF_REC_REJECTED : (match ? YF_REC_RESTORED : YF_REC_MISMATCH);
+        p.ok[r] = v;
+        s_verdict = v;
     }
     __syncthreads();
-    if (!s_good) return;
-    // second pass: the intact payload into the page, 4-byte loads (the record is only 4-byte
-    // aligned) and 16-byte stores
+    if (s_verdict != YF_REC_RESTORED) return;
+    // second pass: the intact payload into the page with 16-byte loads and stores
     for (int l = 0; l < p.n_layers; ++l) {
         uint4* pg = reinterpret_cast<uint4*>(p.base + (size_t)l * p.layer_bytes + (size_t)page * p.page_bytes);
-        const uint32_t* s = src + (size_t)l * (p.page_bytes / 4);
-        for (size_t k = threadIdx.x; k < p.page_bytes / 16; k += kRecThreads)
-            pg[k] = make_uint4(__ldcg(s + 4 * k), __ldcg(s + 4 * k + 1), __ldcg(s + 4 * k + 2), __ldcg(s + 4 * k + 3));
+        const uint4* s4 = src + (size_t)l * (p.page_bytes / 16);
+        for (size_t k = threadIdx.x; k < p.page_bytes / 16; k += kRecThreads) pg[k] = __ldcg(s4 + k);
     }
 }
 
+// Block split of a page: 2^j equal blocks of at most 32 KB (page bytes are 17 x 2^m).
+bool record_blocks(size_t page_bytes, size_t* blk_out, int* bpp_out) {
+    size_t blk = page_bytes;
+    int bpp = 1;
+    while (blk > (size_t)kBlkMaxBytes && blk % 32 == 0) {
+        blk /= 2;
+        bpp *= 2;
+    }
+    if (blk > (size_t)kBlkMaxBytes || blk % 16) return false;
+    *blk_out = blk;
+    *bpp_out = bpp;
+    return true;
+}
+
 int launch_records(yf_pool* pool, int32_t n, const int32_t* pages, const unsigned long long* hashes,
-                   const uint32_t* page_index, void* records, uint32_t* ok, bool do_export, void* stream) {
+                   const unsigned long long* prev_hashes, const uint32_t* page_index, const uint32_t* tokens,
+                   const unsigned long long* expect_hashes, const uint32_t* expect_tokens, void* records,
+                   uint32_t* ok, bool do_export, void* stream) {
     if (!pool) return fail(YF_E_INVALID, "pool is null");
     if (!pool->base) return fail(YF_E_INVALID, "host-only pool has no device memory");
     if (n < 0) return fail(YF_E_INVALID, "n %d < 0", n);
     if (n == 0) return YF_OK;
     if (!pages || !records || (!do_export && !ok)) return fail(YF_E_INVALID, "null device pointer");
-    if (!aligned(records, 4)) return fail(YF_E_INVALID, "records must be 4-byte aligned");
+    if (!aligned(records, 16)) return fail(YF_E_INVALID, "records must be 16-byte aligned");
     if (n > 0x7fffffff / 2) return fail(YF_E_UNSUPPORTED, "too many records");
+    if (pool->crc_ops.size() != kRecOps) return fail(YF_E_UNSUPPORTED, "page of %zu bytes", pool->page_bytes);
     RecParams p;
     p.base = pool->base;
     p.layer_bytes = pool->layer_bytes;
     p.page_bytes = pool->page_bytes;
     p.n_layers = pool->desc.n_layers;
     p.n_pages = pool->desc.n_pages;
+    p.P = pool->desc.page_size;
     p.pages = pages;
     p.hashes = hashes;
+    p.prev_hashes = prev_hashes;
     p.page_index = page_index;
+    p.tokens = tokens;
+    p.expect_hashes = expect_hashes;
+    p.expect_tokens = expect_tokens;
     p.records = static_cast<uint8_t*>(records);
-    p.records_in = static_cast<const uint8_t*>(records);
     p.ok = ok;
-    p.rec_bytes = kRecHeader + (size_t)pool->desc.n_layers * pool->page_bytes;
+    p.hdr_bytes = 4 * kHdrWords + 4 * (size_t)p.P;
+    p.rec_bytes = p.hdr_bytes + (size_t)pool->desc.n_layers * pool->page_bytes;
     p.status = pool->d_status;
-    const size_t payload = p.rec_bytes - kRecHeader;
-    if (payload >= (1ull << 29)) return fail(YF_E_UNSUPPORTED, "record payload of %zu bytes", payload);
-    // a page = 2^j equal blocks of at most 32 KB (page bytes are 17 x 2^m)
-    size_t blk = pool->page_bytes;
-    int bpp = 1;
-    while (blk > (size_t)kBlkMaxBytes && blk % 32 == 0) {
-        blk /= 2;
-        bpp *= 2;
-    }
-    if (blk > (size_t)kBlkMaxBytes || blk % 16) return fail(YF_E_UNSUPPORTED, "page of %zu bytes", pool->page_bytes);
+    size_t blk;
+    int bpp;
+    record_blocks(pool->page_bytes, &blk, &bpp);
     p.blk_words = (int)(blk / 4);
     p.blks_per_page = bpp;
-    if (pool->crc_ops.size() != kRecThreads + 2) {  // the record shape is fixed per pool: once
-        std::vector<uint32_t> ops(kRecThreads + 2);
-        const int nw = p.blk_words;
-        for (int t = 0; t < kRecThreads; ++t) {
-            const int w1 = (int)((long long)(t + 1) * nw / kRecThreads);
-            ops[t] = x8n_mod((unsigned long long)(nw - w1) * 4);
-        }
-        ops[kRecThreads] = x8n_mod(blk);
-        ops[kRecThreads + 1] = gf2_mulmod(x8n_mod(payload), 0xFFFFFFFFu);
-        pool->crc_ops.swap(ops);
-    }
     for (int t = 0; t < kRecThreads; ++t) p.shift[t] = pool->crc_ops[t];
     p.blk_shift = pool->crc_ops[kRecThreads];
     p.preset = pool->crc_ops[kRecThreads + 1];
+    for (int l = 0; l < 32; ++l) p.tok_shift[l] = pool->crc_ops[kRecThreads + 2 + l];
+    p.tok_mul = pool->crc_ops[kRecThreads + 34];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (do_export)
         export_records_kernel<<<n, kRecThreads, 0, s>>>(p);
@@ -267,6 +328,31 @@ int launch_records(yf_pool* pool, int32_t n, const int32_t* pages, const unsigne
 }
 
 }  // namespace
+
+// The record CRC's combine operators for this pool's page shape (yf_pool_create).
+void init_record_ops(yf_pool* pool) {
+    pool->crc_ops.clear();
+    size_t blk;
+    int bpp;
+    if (!record_blocks(pool->page_bytes, &blk, &bpp)) return;  // records refused for this shape
+    const int P = pool->desc.page_size;
+    const size_t payload = (size_t)pool->desc.n_layers * pool->page_bytes;
+    std::vector<uint32_t> ops(kRecOps);
+    const int nw = (int)(blk / 4);
+    for (int t = 0; t < kRecThreads; ++t) {
+        const int w1 = (int)((long long)(t + 1) * nw / kRecThreads);
+        ops[t] = x8n_mod((unsigned long long)(nw - w1) * 4);
+    }
+    ops[kRecThreads] = x8n_mod(blk);
+    ops[kRecThreads + 1] = gf2_mulmod(x8n_mod(4ull * P + payload), 0xFFFFFFFFu);
+    for (int l = 0; l < 32; ++l) {
+        const int w1 = (l + 1) * P / 32;
+        ops[kRecThreads + 2 + l] = x8n_mod(4ull * (P - w1));
+    }
+    ops[kRecThreads + 34] = x8n_mod(payload);
+    pool->crc_ops.swap(ops);
+}
+
 }  // namespace yf
 
 using namespace yf;
@@ -274,17 +360,22 @@ using namespace yf;
 extern "C" size_t yf_pool_record_bytes(const yf_pool_desc* desc) {
     const size_t per_layer = yf_pool_page_head_bytes(desc) * (desc ? (size_t)desc->n_kv_heads : 0);
     if (!per_layer) return 0;
-    return kRecHeader + (size_t)desc->n_layers * per_layer;
+    return 4 * (size_t)kHdrWords + 4 * (size_t)desc->page_size + (size_t)desc->n_layers * per_layer;
 }
 
 extern "C" int yf_pool_export_records(yf_pool* pool, int32_t n, const int32_t* d_pages,
-                                      const uint64_t* d_chain_hashes, const uint32_t* d_page_indices,
-                                      void* d_records, void* stream) {
+                                      const uint64_t* d_chain_hashes, const uint64_t* d_prev_hashes,
+                                      const uint32_t* d_page_indices, const uint32_t* d_tokens, void* d_records,
+                                      void* stream) {
     return launch_records(pool, n, d_pages, reinterpret_cast<const unsigned long long*>(d_chain_hashes),
-                          d_page_indices, d_records, nullptr, true, stream);
+                          reinterpret_cast<const unsigned long long*>(d_prev_hashes), d_page_indices, d_tokens,
+                          nullptr, nullptr, d_records, nullptr, true, stream);
 }
 
 extern "C" int yf_pool_import_records(yf_pool* pool, int32_t n, const int32_t* d_pages, const void* d_records,
+                                      const uint64_t* d_expect_hashes, const uint32_t* d_expect_tokens,
                                       uint32_t* d_ok, void* stream) {
-    return launch_records(pool, n, d_pages, nullptr, nullptr, const_cast<void*>(d_records), d_ok, false, stream);
+    return launch_records(pool, n, d_pages, nullptr, nullptr, nullptr, nullptr,
+                          reinterpret_cast<const unsigned long long*>(d_expect_hashes), d_expect_tokens,
+                          const_cast<void*>(d_records), d_ok, false, stream);
 }

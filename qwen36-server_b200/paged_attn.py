@@ -164,34 +164,43 @@ class PagedKvPool:
         call("yf_pool_restore_pages", self._h, layer, n, arr, ctypes.c_void_p(snapshot.data_ptr()),
              _stream(self.device))
 
-    # -- snapshot wire records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:237-251) ------
+    # -- snapshot wire records (pages.kv, docs/plans/2026-08-27-tiered-kv-cache.md:141-145,237-251) --
     @property
     def record_bytes(self) -> int:
-        """Bytes of one record: 20-byte header + the page in every layer."""
+        """Bytes of one record: 32 + 4 * page_size header bytes + the page in every layer."""
         return lib().yf_pool_record_bytes(ctypes.byref(self.desc))
 
-    def export_records(self, pages, chain_hashes=None, page_indices=None,
+    def export_records(self, pages, chain_hashes=None, page_indices=None, prev_hashes=None, tokens=None,
                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Records [u64 chain_hash][u32 page_index][u32 payload_len][u32 crc32c][payload] of
-        ``pages`` back to back in a device uint8 tensor, the CRC-32C computed on the GPU."""
+        """Records [u64 chain_hash][u64 prev_hash][u32 page_index][u32 n_tokens][u32 payload_len]
+        [u32 crc32c][u32 tokens[page_size]][payload] of ``pages`` back to back in a device uint8
+        tensor, the CRC-32C (over token ids and payload) computed on the GPU.  ``tokens``: the
+        pages' token ids, [n, page_size]."""
         pg = _i32(pages, self.device)
         n = pg.numel()
         if out is None:
             out = torch.empty(n * self.record_bytes, dtype=torch.uint8, device=self.device)
-        hs = None if chain_hashes is None else torch.as_tensor(chain_hashes, dtype=torch.int64).to(self.device)
+        u64 = lambda a: None if a is None else torch.as_tensor(a, dtype=torch.int64).to(self.device)  # noqa: E731
         pi = None if page_indices is None else _i32(page_indices, self.device)
-        call("yf_pool_export_records", self._h, n, _ptr(pg), _ptr(hs), _ptr(pi), _ptr(out), _stream(self.device))
+        tk = None if tokens is None else _i32(tokens, self.device).reshape(n, self.page_size).contiguous()
+        hs, pv = u64(chain_hashes), u64(prev_hashes)   # held until the launch is queued
+        call("yf_pool_export_records", self._h, n, _ptr(pg), _ptr(hs), _ptr(pv), _ptr(pi), _ptr(tk), _ptr(out),
+             _stream(self.device))
         return out
 
-    def import_records(self, pages, records: torch.Tensor) -> torch.Tensor:
-        """Restores the intact records of ``records`` (device) into ``pages``; returns the per-record
-        ok flags (uint32 1 / 0)."""
+    def import_records(self, pages, records: torch.Tensor, expect_hashes=None, expect_tokens=None) -> torch.Tensor:
+        """Restores the intact records of ``records`` (device) into ``pages``; with expected chain
+        hashes and/or token ids, only records that carry them.  Returns per-record verdicts
+        (int32 YF_REC_REJECTED 0 / YF_REC_RESTORED 1 / YF_REC_MISMATCH 2)."""
         pg = _i32(pages, self.device)
         n = pg.numel()
         if records.numel() * records.element_size() < n * self.record_bytes:
             raise YfError(_abi.YF_E_INVALID, "import_records", "records smaller than the page list")
         ok = torch.zeros(n, dtype=torch.int32, device=self.device)
-        call("yf_pool_import_records", self._h, n, _ptr(pg), _ptr(records), _ptr(ok), _stream(self.device))
+        eh = None if expect_hashes is None else torch.as_tensor(expect_hashes, dtype=torch.int64).to(self.device)
+        et = None if expect_tokens is None else _i32(expect_tokens, self.device).reshape(n, self.page_size).contiguous()
+        call("yf_pool_import_records", self._h, n, _ptr(pg), _ptr(records), _ptr(eh), _ptr(et), _ptr(ok),
+             _stream(self.device))
         return ok
 
     # -- workspace ------------------------------------------------------------------

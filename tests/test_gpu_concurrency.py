@@ -1,7 +1,7 @@
-"""Two pools decoded at once from two host threads on two streams: the persistent decode is
-launched cooperatively (all of its CTAs resident together, or the launch waits), and the
-library's per-device launch caches are shared safely, so every concurrent result equals the
-serial one and no wait gives up."""
+"""Two pools decoded at once from two host threads on two streams, with the persistent decode
+launched plainly (the default) and cooperatively: each grid is one resident wave whose CTAs
+only wait for one another, and the library's per-device launch caches are shared safely, so
+every concurrent result equals the serial one and no wait gives up."""
 import threading
 
 import numpy as np
@@ -14,13 +14,15 @@ from qwen36_server_b200 import workloads as W
 pytestmark = pytest.mark.gpu
 
 
-def test_two_threads_two_streams_two_pools(yf, oracle, cuda):
+@pytest.mark.parametrize("launch", [0, 1])
+def test_two_threads_two_streams_two_pools(yf, oracle, cuda, launch):
     wls = [W.Workload("c0", 32, 8, 128, ctx=np.random.default_rng(151).integers(500, 9000, 16),
                       q_rows=np.ones(16), seed=152),
            W.Workload("c1", 16, 2, 256, ctx=[30000], q_rows=[1], seed=153)]
     pools, qs, bts = [], [], []
     for i, wl in enumerate(wls):
         pool, _, _, _, _ = filled_pool(yf, oracle, wl, seed=160 + i, oracle_image=False)
+        pool.set_options(launch=launch)
         pools.append(pool)
         qs.append(torch.from_numpy(queries(wl, 170 + i)).to(cuda))
         bts.append(torch.from_numpy(wl.block_table).to(cuda))

@@ -89,3 +89,54 @@ def test_out_of_range_rows_are_skipped_and_flagged(yf, oracle, cuda):
         yf.kv_append_paged(pool, 3, k, k, [0, 0], bt)
     assert e.value.code == _abi.YF_E_RANGE
     pool.close()
+
+
+@pytest.mark.parametrize("D,P,G", [(128, 16, 32), (256, 64, 32), (128, 64, 128)])
+def test_tile_writer_mid_tile_chunks_keep_earlier_rows(yf, oracle, cuda, D, P, G):
+    """Chunks of >= 16 rows (the staged tile writer) starting mid-tile on top of existing rows:
+    the partly covered tiles keep their other tokens; then a chunk that runs past the table, one on
+    a bad page and one longer than max_rows are skipped or clamped and flagged."""
+    H = 3
+    wl = W.Workload("t", H, H, D, ctx=[300, 200], q_rows=[1, 1], page_size=P, group_size=G, seed=17,
+                    outlier_frac=0.02)
+    pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=18)
+    bt = torch.from_numpy(wl.block_table).to(cuda)
+    rng = np.random.default_rng(19)
+    # entry 0: 40 rows at 37; entry 1: 23 rows at 100
+    cu, start = [0, 40, 63], [37, 100]
+    k = W.kv_rows_np(rng, 63, H, D, 0.02)
+    v = W.kv_rows_np(rng, 63, H, D, 0.02)
+    yf.launch_append_multi(pool, 0, torch.from_numpy(k).to(cuda), torch.from_numpy(v).to(cuda), cu, start, bt)
+    assert pool.status() == 0
+    oracle.np_kv_write_rows(desc, img, 0, k, v, np.r_[np.zeros(40), np.ones(23)].astype(np.int32),
+                            np.r_[np.arange(37, 77), np.arange(100, 123)].astype(np.int32), wl.block_table)
+    assert np.array_equal(pool_image(pool), img)
+    # past the end of entry 1's table: rows from its capacity on are skipped (BAD_POS)
+    cap = wl.max_blocks * P
+    k2 = W.kv_rows_np(rng, 40, H, D)
+    yf.launch_append_multi(pool, 0, torch.from_numpy(k2).to(cuda), torch.from_numpy(k2).to(cuda), [0, 0, 40],
+                           [0, cap - 8], bt)
+    assert pool.status() & _abi.YF_DEV_BAD_POS
+    oracle.np_kv_write_rows(desc, img, 0, k2[:8], k2[:8], np.ones(8, np.int32), np.arange(cap - 8, cap).astype(np.int32),
+                            wl.block_table)
+    assert np.array_equal(pool_image(pool), img)
+    # a bad page id in the table: that tile is skipped (BAD_PAGE), the others are written
+    bad = wl.block_table.copy()
+    bad[0, 1] = 10 ** 6
+    k3 = W.kv_rows_np(rng, 3 * P, H, D)
+    yf.launch_append_multi(pool, 0, torch.from_numpy(k3).to(cuda), torch.from_numpy(k3).to(cuda), [0, 3 * P, 3 * P],
+                           [0, 0], torch.from_numpy(bad).to(cuda))
+    assert pool.status() == _abi.YF_DEV_BAD_PAGE
+    keep = np.r_[np.arange(0, P), np.arange(2 * P, 3 * P)]
+    oracle.np_kv_write_rows(desc, img, 0, k3[keep], k3[keep], np.zeros(len(keep), np.int32), keep.astype(np.int32),
+                            wl.block_table)
+    assert np.array_equal(pool_image(pool), img)
+    # more rows than max_rows: clamped to max_rows and flagged
+    k4 = W.kv_rows_np(rng, 50, H, D)
+    yf.launch_append_multi(pool, 0, torch.from_numpy(k4).to(cuda), torch.from_numpy(k4).to(cuda), [0, 50, 50], [5, 0],
+                           bt, max_rows=32)
+    assert pool.status() == _abi.YF_DEV_BAD_ROWS
+    oracle.np_kv_write_rows(desc, img, 0, k4[:32], k4[:32], np.zeros(32, np.int32), np.arange(5, 37).astype(np.int32),
+                            wl.block_table)
+    assert np.array_equal(pool_image(pool), img)
+    pool.close()

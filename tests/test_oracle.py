@@ -243,13 +243,18 @@ def test_crc32c_check_value_and_records(oracle):
     desc = oracle.PoolDesc(2, 3, 2, 128)
     rng = np.random.default_rng(21)
     img = rng.integers(0, 256, desc.pool_bytes, dtype=np.uint8)
-    rec = oracle.page_records(desc, img, [2, 0], [0x1122334455667788, 7], [5, 6])
+    tok = np.arange(32, dtype=np.uint32).reshape(2, 16) * 1000 + 7
+    rec = oracle.page_records(desc, img, [2, 0], [0x1122334455667788, 7], [5, 6], prev_hashes=[0xABCDEF, 3],
+                              tokens=tok)
     pb = desc.page_head_bytes * 2
-    stride = 20 + 2 * pb
+    hdr = 32 + 4 * 16
+    stride = hdr + 2 * pb
     assert rec.size == 2 * stride
-    h = rec[:20].view(np.uint32)
-    assert h[0] == 0x55667788 and h[1] == 0x11223344 and h[2] == 5 and h[3] == 2 * pb
-    payload = rec[20:stride]
+    h = rec[:32].view(np.uint32)
+    assert h[0] == 0x55667788 and h[1] == 0x11223344 and h[2] == 0xABCDEF and h[3] == 0
+    assert h[4] == 5 and h[5] == 16 and h[6] == 2 * pb
+    assert np.array_equal(rec[32:hdr].view(np.uint32), tok[0])
+    payload = rec[hdr:stride]
     assert np.array_equal(payload[:pb], img[2 * pb:3 * pb])
     assert np.array_equal(payload[pb:], img[3 * pb + 2 * pb:3 * pb + 3 * pb])
-    assert h[4] == oracle.crc32c(payload)
+    assert h[7] == oracle.crc32c(rec[32:stride])      # token ids, then payload
