@@ -75,61 +75,35 @@ __global__ void __launch_bounds__(kWriteWarps * 32) kv_write_kernel(const WriteP
     }
 }
 
-// ---- multi-row writer: whole tiles staged in shared memory -------------------------------
+// ---- multi-row writer: one CTA per (entry, 16-token tile, kv head) --------------------------
 //
-// One CTA of two warps per (entry, 16-token tile its rows touch, kv head) quantizes the tile's K
-// and V rows into a shared-memory copy of the tile and then writes it out with 16-byte coalesced
-// stores; a tile the entry's rows only partly cover is first loaded, so its other tokens keep
-// their bytes.  Lane work: one Q8_0 group of one row.  A group of <= 32 dims is loaded once into
-// registers as packed f16 (the |x| maximum is exact in f16), then the pair of IEEE divisions and
-// the group's values; a row-scale group (G = D) takes an amax pass and a quantize pass over its
-// row.  Same arithmetic as q8_store_row: bit-exact with it.
+// Phase 1 loads the tile's K and V rows (16 tokens each) with coalesced 16-byte loads into a
+// padded f16 copy in shared memory and takes each Q8_0 group's |x| maximum (exact in f16) over
+// the group's lanes; one lane per group then forms d = amax/127 and 1/d (IEEE divisions) and
+// puts d, as f16, into a copy of the tile's scale areas.  Phase 2 builds every 16-byte chunk of
+// the pool tile from the staged rows -- a K chunk is 8 dims of tokens t and t+8, a V chunk is
+// 4 dims x the 4 tokens that share a word -- rounds the values (roundf(x * (1/d)), the Q8_0
+// rule of q8_store_row, bit-exact with it) and stores the chunk straight to the pool: each
+// warp's stores cover 512 contiguous bytes.  A tile the entry's rows only partly cover keeps
+// the bytes of its other tokens (their chunks are merged with the pool's current bytes).
 constexpr int kTileThreads = 64;
 
-// Stores the 8 quantized values of dims d0..d0+7 (d0 % 8 == 0) of token t into the tile.
-__device__ __forceinline__ void put8(uint8_t* tile, int D, int NB, int t, int kv, int d0, const uint8_t (&qb)[8]) {
-    const int V_OFF = 16 * D + 32 * NB;
-    if (kv == 0) {
-        const int b32 = d0 / 32, r = d0 % 32;
-        uint2 w;
-        w.x = qb[0] | (qb[1] << 8) | (qb[2] << 16) | ((uint32_t)qb[3] << 24);
-        w.y = qb[4] | (qb[5] << 8) | (qb[6] << 16) | ((uint32_t)qb[7] << 24);
-        *reinterpret_cast<uint2*>(tile + b32 * 512 + ((t % 8) * 4 + r / 8) * 16 + (t / 8) * 8) = w;
-    } else {
-        const int tig = (t % 8) / 2, j = (t & 1) * 2 + t / 8;
-        const int m = d0 / 16, hi8 = (d0 % 16) / 8;
-        uint8_t* vb = tile + V_OFF + (m / 2) * 512 + tig * 16 + (m % 2) * 8 + hi8 * 4 + j;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vb[e * 64] = qb[e];
-    }
-}
-
-__device__ __forceinline__ void quant8(const uint4 w, float id, uint8_t (&qb)[8]) {
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const __half2 a = *reinterpret_cast<const __half2*>(&ww[k]);
-        qb[2 * k] = excess128((int8_t)(int)roundf(__fmul_rn(__low2float(a), id)));
-        qb[2 * k + 1] = excess128((int8_t)(int)roundf(__fmul_rn(__high2float(a), id)));
-    }
-}
-
-__device__ __forceinline__ void put_scale(uint8_t* tile, int D, int NB, int t, int kv, int grp, float d) {
-    const int KS_OFF = 16 * D, VS_OFF = 32 * D + 32 * NB;
-    const int tig = (t % 8) / 2, j = (t & 1) * 2 + t / 8;
-    const int off = kv == 0 ? KS_OFF + 2 * (((t % 8) * 2 + t / 8) * NB + grp) : VS_OFF + 2 * ((tig * NB + grp) * 4 + j);
-    *reinterpret_cast<__half*>(tile + off) = __float2half_rn(d);
-}
+template <int D>
+constexpr int stage_pitch() { return 2 * D + 16; }  // bytes per staged row (16 B pad: spreads banks)
 
 template <int D, int NB, int TPP>
 __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const WriteParams p) {
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int P = TPP * 16;
     constexpr int G = D / NB;
-    constexpr int RPJ = 32 / NB;        // rows per warp job (a lane = one group of one row)
-    constexpr int JOBS = 32 / RPJ;      // (kv, token) rows of the tile = 32
-    constexpr int JPW = (JOBS + 1) / 2; // jobs per warp
-    __shared__ __align__(16) uint8_t stage[TB];
+    constexpr int RP = stage_pitch<D>();
+    constexpr int KS_OFF = 16 * D, V_OFF = 16 * D + 32 * NB, VS_OFF = 32 * D + 32 * NB;
+    constexpr int CPR = D / 8;   // 16-byte chunks per input row
+    constexpr int LPG = G / 8;   // lanes (chunks) per group in phase 1
+    static_assert(LPG <= 32 && (32 % LPG) == 0, "a group's chunks lie in one warp");
+    __shared__ __align__(16) uint8_t rows[2][16][RP];     // f16 K and V rows of the tile's tokens
+    __shared__ __align__(16) float inv[2][16][NB];         // 1/d per (kv, token, group)
+    __shared__ __align__(16) uint16_t scl[2][16 * NB];     // the tile's K and V scale areas (f16 bits)
     const int b = blockIdx.z, h = blockIdx.y;
     const int n_raw = p.cu_rows[b + 1] - p.cu_rows[b];
     if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0 && (n_raw > p.max_rows || n_raw < 0))
@@ -151,83 +125,117 @@ __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const Writ
         if (threadIdx.x == 0 && h == 0) atomicOr(p.status, YF_DEV_BAD_PAGE);
         return;
     }
-    uint4* gtile = reinterpret_cast<uint4*>(p.layer_base + ((size_t)page * p.H + h) * p.phb +
-                                            ((16 * T) % P) / 16 * (size_t)TB);
-    if (lo > 16 * T || hi < 16 * T + 16) {  // partly covered: keep the tile's other tokens
-        for (int k = threadIdx.x; k < TB / 16; k += kTileThreads) reinterpret_cast<uint4*>(stage)[k] = gtile[k];
+    uint8_t* gtile = p.layer_base + ((size_t)page * p.H + h) * p.phb + ((16 * T) % P) / 16 * (size_t)TB;
+    const int t_lo = lo - 16 * T, t_hi = hi - 16 * T;  // live tokens [t_lo, t_hi)
+    const bool partial = t_lo > 0 || t_hi < 16;
+    auto live = [&](int t) { return t >= t_lo && t < t_hi; };
+    if (partial) {  // the scale areas start as the pool's; live tokens overwrite theirs
+        for (int k = threadIdx.x; k < 2 * 16 * NB; k += kTileThreads)
+            scl[k / (16 * NB)][k % (16 * NB)] =
+                *reinterpret_cast<const uint16_t*>(gtile + (k < 16 * NB ? KS_OFF : VS_OFF) + 2 * (k % (16 * NB)));
         __syncthreads();
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int grp = lane % NB;
-    if constexpr (G <= 32) {
-        // every job's loads first (JPW x G/8 independent 16-byte loads per lane), then the math
-        uint4 w[JPW][G / 8];
-        bool live[JPW];
-        int tt[JPW], kvv[JPW];
-#pragma unroll
-        for (int q = 0; q < JPW; ++q) {
-            const int R = (warp * JPW + q) * RPJ + lane / NB;  // (kv, token) row of the tile
-            kvv[q] = R / 16;
-            tt[q] = R % 16;
-            const int pos = 16 * T + tt[q];
-            live[q] = warp * JPW + q < JOBS && pos >= lo && pos < hi;
-            if (live[q]) {
-                const uint4* src = reinterpret_cast<const uint4*>((kvv[q] ? p.v : p.k) +
-                                                                  ((size_t)(p.cu_rows[b] + pos - s) * p.H + h) * D + grp * G);
-#pragma unroll
-                for (int c = 0; c < G / 8; ++c) w[q][c] = __ldcs(src + c);
-            }
+
+    // ---- phase 1: rows into shared memory, group maxima, scales
+    for (int c = threadIdx.x; c < 2 * 16 * CPR; c += kTileThreads) {
+        const int kv = c / (16 * CPR), t = (c / CPR) % 16, q = c % CPR;
+        const bool on = live(t);
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (on) {
+            const __half* src = (kv ? p.v : p.k) + ((size_t)(p.cu_rows[b] + 16 * T + t - s) * p.H + h) * D;
+            w = __ldcs(reinterpret_cast<const uint4*>(src) + q);
         }
+        *reinterpret_cast<uint4*>(&rows[kv][t][16 * q]) = w;
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        __half2 m2 = __float2half2_rn(0.f);
 #pragma unroll
-        for (int q = 0; q < JPW; ++q) {
-            if (!live[q]) continue;
-            __half2 m2 = __float2half2_rn(0.f);
+        for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __half2*>(&ww[k])));
+        float amax = fmaxf(__low2float(m2), __high2float(m2));
 #pragma unroll
-            for (int c = 0; c < G / 8; ++c) {
-                const uint32_t ww[4] = {w[q][c].x, w[q][c].y, w[q][c].z, w[q][c].w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __half2*>(&ww[k])));
-            }
-            const float amax = fmaxf(__low2float(m2), __high2float(m2));
+        for (int off = 1; off < LPG; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        if (on && q % LPG == 0) {
+            const int grp = q / LPG;
             const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-#pragma unroll
-            for (int c = 0; c < G / 8; ++c) {
-                uint8_t qb[8];
-                quant8(w[q][c], id, qb);
-                put8(stage, D, NB, tt[q], kvv[q], grp * G + 8 * c, qb);
-            }
-            put_scale(stage, D, NB, tt[q], kvv[q], grp, d);
-        }
-    } else {
-        // row scale: lane = one (kv, token) row; an amax pass and a quantize pass over the row
-        const int R = warp * 32 + lane;
-        const int kv = R / 16, t = R % 16, pos = 16 * T + t;
-        if (R < 32 && pos >= lo && pos < hi) {
-            const uint4* src = reinterpret_cast<const uint4*>((kv ? p.v : p.k) +
-                                                              ((size_t)(p.cu_rows[b] + pos - s) * p.H + h) * D);
-            __half2 m2 = __float2half2_rn(0.f);
-#pragma unroll 4
-            for (int c = 0; c < D / 8; ++c) {
-                const uint4 x = src[c];
-                const uint32_t ww[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __half2*>(&ww[k])));
-            }
-            const float amax = fmaxf(__low2float(m2), __high2float(m2));
-            const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-#pragma unroll 4
-            for (int c = 0; c < D / 8; ++c) {
-                uint8_t qb[8];
-                quant8(src[c], id, qb);
-                put8(stage, D, NB, t, kv, 8 * c, qb);
-            }
-            put_scale(stage, D, NB, t, kv, 0, d);
+            inv[kv][t][grp] = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+            const int tig = (t % 8) / 2, j = (t & 1) * 2 + t / 8;
+            const int si = kv == 0 ? ((t % 8) * 2 + t / 8) * NB + grp : (tig * NB + grp) * 4 + j;
+            scl[kv][si] = __half_as_ushort(__float2half_rn(d));
         }
     }
     __syncthreads();
-    for (int k = threadIdx.x; k < TB / 16; k += kTileThreads) gtile[k] = reinterpret_cast<const uint4*>(stage)[k];
+
+    auto q8 = [](float x, float id) -> uint32_t {
+        return (uint32_t)excess128((int8_t)(int)roundf(__fmul_rn(x, id)));
+    };
+    // ---- phase 2a: K chunks (chunk kc = b32*32 + (t%8)*4 + r/8: dims 32*b32 + 8*(r/8) .. +7 of
+    // tokens t%8 (bytes 0-7) and t%8 + 8 (bytes 8-15))
+    for (int kc = threadIdx.x; kc < D * 16 / 16; kc += kTileThreads) {
+        const int b32 = kc / 32, t0 = (kc % 32) / 4, q4 = kc % 4;
+        const int d0 = 32 * b32 + 8 * q4, grp = d0 / G;
+        uint32_t out[4];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int t = t0 + 8 * half;
+            const uint4 w = *reinterpret_cast<const uint4*>(&rows[0][t][2 * d0]);
+            const float id = inv[0][t][grp];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+            uint32_t lo32 = 0, hi32 = 0;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const __half2 a = *reinterpret_cast<const __half2*>(&ww[k]);
+                const __half2 c2 = *reinterpret_cast<const __half2*>(&ww[k + 2]);
+                lo32 |= (q8(__low2float(a), id) | (q8(__high2float(a), id) << 8)) << (16 * k);
+                hi32 |= (q8(__low2float(c2), id) | (q8(__high2float(c2), id) << 8)) << (16 * k);
+            }
+            out[2 * half] = lo32;
+            out[2 * half + 1] = hi32;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(gtile + b32 * 512 + (t0 * 4 + q4) * 16);
+        uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
+        if (partial) {
+            const uint4 old = *dst;
+            if (!live(t0)) { o.x = old.x; o.y = old.y; }
+            if (!live(t0 + 8)) { o.z = old.z; o.w = old.w; }
+        }
+        *dst = o;
+    }
+    // ---- phase 2b: V chunks (chunk vc = M*32 + iim*4 + tig: word (m%2)*2 + ii/8 holds dim
+    // 16*(2M + m%2) + iim + 8*(ii/8) of tokens 2tig, 2tig+8, 2tig+1, 2tig+9 in bytes 0..3)
+    for (int vc = threadIdx.x; vc < D * 16 / 16; vc += kTileThreads) {
+        const int M = vc / 32, iim = (vc % 32) / 4, tig = vc % 4;
+        const int tok[4] = {2 * tig, 2 * tig + 8, 2 * tig + 1, 2 * tig + 9};
+        uint32_t out[4];
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+            const int dim = 16 * (2 * M + wd / 2) + iim + 8 * (wd % 2), grp = dim / G;
+            uint32_t word = 0;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const float x = __half2float(*reinterpret_cast<const __half*>(&rows[1][tok[jj]][2 * dim]));
+                word |= q8(x, inv[1][tok[jj]][grp]) << (8 * jj);
+            }
+            out[wd] = word;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(gtile + V_OFF + M * 512 + (iim * 4 + tig) * 16);
+        uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
+        if (partial) {
+            uint32_t keep = 0;  // bytes of tokens outside the chunk's live range
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+                if (!live(tok[jj])) keep |= 0xFFu << (8 * jj);
+            const uint4 old = *dst;
+            o.x = (o.x & ~keep) | (old.x & keep);
+            o.y = (o.y & ~keep) | (old.y & keep);
+            o.z = (o.z & ~keep) | (old.z & keep);
+            o.w = (o.w & ~keep) | (old.w & keep);
+        }
+        *dst = o;
+    }
+    // ---- phase 2c: the two scale areas (16 * NB f16 each, 16-byte aligned)
+    for (int k = threadIdx.x; k < 2 * 16 * NB * 2 / 16; k += kTileThreads) {
+        const int kv = k / (16 * NB * 2 / 16), i = k % (16 * NB * 2 / 16);
+        *reinterpret_cast<uint4*>(gtile + (kv ? VS_OFF : KS_OFF) + 16 * i) = reinterpret_cast<const uint4*>(scl[kv])[i];
+    }
 }
 
 template <int D, int NB, int TPP>
