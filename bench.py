@@ -33,6 +33,9 @@ import __graft_entry__ as graft  # noqa: E402
 graft.load_package()
 
 METRIC = "paged int8-KV decode attn tokens/s & KV GB/s (% HBM peak) at 1/2/4/8 B200"
+# attention options of every pool the bench builds (yf_attn_options; --schedule / --launch)
+POOL_OPTIONS = {}
+SCHEDULES = {"auto": 0, "chunked": 1, "persistent": 2}
 
 
 def peaks():
@@ -149,6 +152,7 @@ class Step:
         self.layers = layers_resident
         self.pool = yf.PagedKvPool(layers_resident, wl.n_pages, wl.n_kv_heads, wl.head_dim, wl.page_size,
                                    wl.group_size, device=device)
+        self.pool.set_options(**POOL_OPTIONS)
         gen = torch.Generator(device=self.dev)
         gen.manual_seed(wl.seed)
         bt = torch.from_numpy(wl.block_table).to(self.dev)
@@ -279,6 +283,7 @@ class ShardedStep:
         self.sd = S.ShardedLongDecode(sh, wl.n_q_heads, wl.n_kv_heads, wl.head_dim, pages, wl.page_size,
                                       wl.group_size, batch=1, device=device)
         self.pool = self.sd.pool
+        self.pool.set_options(**POOL_OPTIONS)
         gen = torch.Generator(device=self.dev)
         gen.manual_seed(wl.seed + 7919 * rank)
         self.bt = torch.arange(pages, dtype=torch.int32, device=self.dev).view(1, pages)
@@ -1031,11 +1036,16 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.5,
                     help="GPU time the timed passes of --steps steps must cover (median pass reported)")
     ap.add_argument("--no-long", action="store_true", help="N>1: skip the sharded decode_long leg")
+    ap.add_argument("--schedule", default="auto", choices=sorted(SCHEDULES),
+                    help="split-KV schedule of the pools (yf_attn_options.schedule), for A/B runs")
+    ap.add_argument("--cooperative", action="store_true",
+                    help="launch the persistent decode cooperatively (yf_attn_options.launch)")
     ap.add_argument("--layers", type=int, default=0,
                     help="mtp_verify only: stack this many layers instead of 36 (one launch per layer keeps "
                          "its shape; for profiling a launch with a few GB resident, not a bench line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    POOL_OPTIONS.update(schedule=SCHEDULES[args.schedule], launch=1 if args.cooperative else 0)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -150,8 +150,9 @@ YF_API int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear);
  * yf_attn_workspace_size, read (the library reads no environment variables).
  * A zero-filled struct is the default.  The engine's counterpart is its
  * command-line / config flags (src/cli.rs), fixed for the life of the pool. */
-#define YF_SCHED_AUTO 0        /* persistent decode schedule where it applies, else chunked split-KV */
+#define YF_SCHED_AUTO 0        /* cluster schedule for a few long units, persistent for many, else chunked */
 #define YF_SCHED_CHUNKED 1     /* always the chunked (unit x chunk grid) split-KV schedule */
+#define YF_SCHED_PERSISTENT 2  /* the persistent schedule wherever it applies (no cluster schedule) */
 #define YF_MERGE_IN_KERNEL 0   /* split partials merged inside the attention kernel */
 #define YF_MERGE_SEPARATE 1    /* chunked schedule: a separate combine launch merges the partials */
 #define YF_PREFILL_AUTO 0      /* tcgen05 prefill kernel where it applies (>= 128 rows per kv head) */

@@ -29,6 +29,7 @@ YF_DEV_SMEM_ALIGN = 32
 
 YF_SCHED_AUTO = 0
 YF_SCHED_CHUNKED = 1
+YF_SCHED_PERSISTENT = 2
 YF_MERGE_IN_KERNEL = 0
 YF_MERGE_SEPARATE = 1
 YF_PREFILL_AUTO = 0

@@ -1061,6 +1061,153 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
     }
 }
 
+// ---- schedule 3: few long units over thread-block clusters ----------------------------------
+//
+// For a handful of long units (the long-context decode, a small decode, one rank's shard) every
+// unit gets whole clusters of kClusterCtas CTAs; cluster lc of a unit streams tiles
+// [lc * tpc, (lc + 1) * tpc) of it, split evenly over its CTAs.  Each CTA merges its 4 warps into
+// a normalised partial in its own shared memory; after a cluster barrier, CTA rank r merges
+// column slice r of the unit's output over the cluster's CTAs by distributed shared-memory loads.
+// A unit held by one cluster writes its output there.  Otherwise each cluster writes its slices
+// as a partial and counts an arrival per slice; the CTA that arrives last for slice r merges the
+// unit's cluster partials of that slice from L2 and writes the output (its counter back to zero).
+// No CTA ever waits for another cluster, so the grid needs no co-residency beyond the cluster,
+// which the hardware schedules as one.
+
+template <int D>
+constexpr int cluster_part_off() {  // the CTA partial, after the 4-warp stash in the stage area
+    return ((2 * kWarps * 8 * 4 + kWarps * 8 * (D + 4) * 4) + 127) / 128 * 128;
+}
+
+template <int D, int NB, int TPP, int STAGES>
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads, 3)
+    decode_cluster_kernel(const SplitParams p) {
+    constexpr int NT = 1, RPC = 8, CL = kClusterCtas;
+    constexpr int TB = 32 * D + 64 * NB;
+    constexpr int DP = D + 4;
+    constexpr int COLS = RPC * (D / 4);  // float4 columns of a unit's output
+    constexpr int SLICE = COLS / CL;
+    static_assert(SLICE <= kThreads && COLS % CL == 0, "one column per thread in a slice");
+    static_assert(cluster_part_off<D>() + RPC * (D + 1) * 4 <= kWarps * STAGES * TB, "partial area");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* stages = smem + hdr_bytes<NB, NT>();
+    float* part_lse = reinterpret_cast<float*>(stages + cluster_part_off<D>());  // [RPC] base-2 lse
+    float* part_o = part_lse + RPC;                                               // [RPC][D] normalised
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = (int)cluster_rank();
+    const int cid = blockIdx.x / CL;
+    const int cpu = p.max_chunks, tpc = p.chunk_tiles;  // clusters per unit, tiles per cluster
+    const int uidx = cid / cpu, lc = cid % cpu;
+    const int b = uidx / p.H, h = uidx % p.H;
+    UnitGeom u;
+    unit_geom<TPP, RPC>(p, b, 0, u, lc == 0 && r == 0 && threadIdx.x == 0);
+    const int n_u = max(1, (u.n_tiles + tpc - 1) / tpc);  // clusters this unit uses
+    if (lc >= n_u) return;                               // the whole cluster leaves together
+    const int c0 = lc * tpc, c1 = min(c0 + tpc, u.n_tiles), len = max(c1 - c0, 0);
+    const int t0 = c0 + r * len / CL, t1 = c0 + (r + 1) * len / CL;
+
+    TileRing<TB, STAGES> ring;
+    ring.init(smem, stages, warp, lane);
+    WarpAcc<D, NT> acc;
+    uint4 qf[NT][D / 32];
+    int kvlen[NT][2], kv_min;
+    load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp));
+    acc.reset();
+    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, t1 - t0, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp),
+                                        acc, warp, lane, TreeCtx{});
+    stash_warp<D, NT>(stages, acc, warp, lane);
+    {  // the 4 warps into this CTA's partial
+        const float* mw = reinterpret_cast<const float*>(stages);
+        const float* lw = mw + kWarps * RPC;
+        const float* ow = lw + kWarps * RPC;
+        for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
+            const int row = e / (D / 4), d4 = (e % (D / 4)) * 4;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mw[w * RPC + row]);
+            float L = 0.f;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float mv = mw[w * RPC + row];
+                if (mv == -INFINITY) continue;
+                const float f = fast_exp2(mv - M);
+                L = fmaf(f, lw[w * RPC + row], L);
+                const float4 ov = *reinterpret_cast<const float4*>(&ow[(w * RPC + row) * DP + d4]);
+                o.x = fmaf(f, ov.x, o.x);
+                o.y = fmaf(f, ov.y, o.y);
+                o.z = fmaf(f, ov.z, o.z);
+                o.w = fmaf(f, ov.w, o.w);
+            }
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            *reinterpret_cast<float4*>(&part_o[row * D + d4]) = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+            if (d4 == 0) part_lse[row] = L > 0.f ? M + __log2f(L) : -INFINITY;
+        }
+    }
+    cluster_barrier();  // every CTA's partial is in its shared memory
+    // slice r of the columns, merged over the cluster's CTAs through distributed shared memory
+    const int col = r * SLICE + threadIdx.x;
+    const int row = col / (D / 4), d4 = (col % (D / 4)) * 4;
+    float m = -INFINITY, l = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (threadIdx.x < SLICE) {
+        float lv[CL];
+        float4 ov[CL];
+#pragma unroll
+        for (int q = 0; q < CL; ++q) {
+            lv[q] = ld_dsmem_f32(dsmem_addr(&part_lse[row], q));
+            ov[q] = ld_dsmem_f32x4(dsmem_addr(&part_o[row * D + d4], q));
+        }
+#pragma unroll
+        for (int q = 0; q < CL; ++q) merge_in(lv[q], ov[q], m, l, o);
+    }
+    cluster_barrier();  // no CTA leaves, or reuses its shared memory, while a peer still reads it
+    const bool live_row = threadIdx.x < SLICE && u.row_begin + row < u.rows_total;
+    if (n_u == 1) {
+        if (live_row) {
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
+                       l > 0.f ? m + __log2f(l) : -INFINITY);
+        }
+        return;
+    }
+    // this cluster's partial of slice r, then the slice's arrival
+    const size_t item = (size_t)uidx * cpu + lc;
+    if (threadIdx.x < SLICE) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __stcg(reinterpret_cast<float4*>(p.ws_o + (item * RPC + row) * D + d4),
+               make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv));
+        if (d4 == 0) __stcg(p.ws_lse + item * RPC + row, l > 0.f ? m + __log2f(l) : -INFINITY);
+    }
+    uint32_t* ctr = &p.counters[(size_t)uidx * CL + r];
+    if (!arrive_last(ctr, n_u, &s_last)) return;
+    if (live_row) {
+        float m2 = -INFINITY, l2 = 0.f;
+        float4 o2 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k0 = 0; k0 < n_u; k0 += 8) {
+            float lv[8];
+            float4 ov[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                lv[j] = -INFINITY;
+                ov[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k0 + j < n_u) {
+                    const size_t it = (size_t)uidx * cpu + k0 + j;
+                    lv[j] = __ldcg(p.ws_lse + it * RPC + row);
+                    ov[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (it * RPC + row) * D + d4));
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) merge_in(lv[j], ov[j], m2, l2, o2);
+        }
+        const float inv = l2 > 0.f ? 1.f / l2 : 0.f;
+        store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o2.x * inv, o2.y * inv, o2.z * inv, o2.w * inv),
+                   l2 > 0.f ? m2 + __log2f(l2) : -INFINITY);
+    }
+    if (threadIdx.x == 0) *ctr = 0;  // ready for the next call on this pool
+}
+
 // ---- schedule 2: a 3-D grid of (unit, chunk of tiles) ----------------------------------------
 
 template <int D, int NB, int NT, int TPP, int STAGES, bool TREE = false>
@@ -1146,6 +1293,19 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
     constexpr int SMEM = hdr_bytes<NB, NT, TREE>() + kWarps * STAGES * TB;
     const int dev = a.pool->desc.device;
     cudaError_t e;
+    if constexpr (!TREE && NT == 1) {
+        if (plan.cluster) {
+            auto kern = decode_cluster_kernel<D, NB, TPP, STAGES>;
+            static LaunchCache ccache;
+            const int rc = raise_smem_attr((const void*)kern, SMEM, dev, ccache);
+            if (rc) return rc;
+            const long long units = (long long)a.batch * a.pool->desc.n_kv_heads;
+            const long long ctas = units * plan.max_chunks * kClusterCtas;
+            kern<<<(unsigned)ctas, kThreads, SMEM, a.stream>>>(p);
+            e = cudaGetLastError();
+            return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_cluster launch");
+        }
+    }
     if (!TREE && plan.persistent) {
         auto kern = decode_persistent_kernel<D, NB, NT, TPP, STAGES>;
         static LaunchCache cache;
@@ -1248,7 +1408,7 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;
     if (plan.persistent && !p.counters) return fail(YF_E_UNSUPPORTED, "persistent decode needs the merge counters");
     if (plan.ws_bytes > 0) {
-        const size_t items = plan.persistent ? (size_t)plan.persistent_ctas * 2 : units * plan.max_chunks;
+        const size_t items = plan.persistent ? (size_t)plan.persistent_ctas * 2 : units * plan.max_chunks;  // cluster: units x clusters
         p.ws_o = static_cast<float*>(a.workspace);
         p.ws_lse = p.ws_o + items * plan.rows_per_cta * d.head_dim;
     } else {

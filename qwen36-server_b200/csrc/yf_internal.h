@@ -23,6 +23,9 @@ constexpr int kMaxGroupCounters = 4096;
 constexpr int kPersistentMaxBatch = 1024;
 // Upper bound of resident split-KV CTAs per SM (sizes the persistent schedule's workspace).
 constexpr int kMaxCtasPerSm = 4;
+// CTAs per thread-block cluster of the few-long-units decode schedule, and the most units it takes.
+constexpr int kClusterCtas = 8;
+constexpr int kClusterMaxUnits = 32;
 
 // Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).
 struct TileGeom {
@@ -103,6 +106,7 @@ struct SplitPlan {
     int stages;        // bulk-copy stages per warp
     bool fused_combine;  // the last CTA of a unit merges its partials (no combine launch)
     bool persistent;     // decode_persistent_kernel: equal (unit, tile) ranges per CTA
+    bool cluster;        // decode_cluster_kernel: max_chunks clusters of chunk_tiles tiles per unit
     int persistent_ctas;  // upper bound of its grid (the launch also caps it by occupancy)
     size_t ws_bytes;   // partial O + lse
 };

@@ -117,6 +117,21 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     p.persistent = !tree && o.schedule != YF_SCHED_CHUNKED && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
                    units <= kMaxCombineUnits && in_kernel_merge;
     if (p.persistent) p.fused_combine = true;
+    // A few long units (long-context decode, one rank's shard, a small decode): whole clusters of
+    // kClusterCtas CTAs per unit, at least 16 tiles per CTA and about two CTAs per SM in all.
+    p.cluster = p.persistent && o.schedule == YF_SCHED_AUTO && p.rows_per_cta == 8 && units <= kClusterMaxUnits &&
+                tiles > 0;
+    if (p.cluster) {
+        p.persistent = false;
+        const long long target = std::min((long long)pool->sm_count * 2, std::max<long long>(kClusterCtas, units * tiles / 16));
+        const long long cpu = std::max<long long>(1, target / (units * kClusterCtas));
+        p.max_chunks = (int)cpu;                         // clusters per unit
+        p.chunk_tiles = (int)((tiles + cpu - 1) / cpu);  // tiles per cluster
+        const size_t row_bytes_c = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
+        p.ws_bytes = cpu > 1 ? (size_t)units * cpu * row_bytes_c : 0;
+        p.persistent_ctas = 0;
+        return p;
+    }
     const size_t row_bytes = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
     if (p.persistent) {
         // at least 16 tiles (4 per warp) per CTA, at most kMaxCtasPerSm CTAs per SM
@@ -345,7 +360,7 @@ int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear) {
 
 static int check_options(const yf_attn_options* o) {
     if (!o) return fail(YF_E_INVALID, "options are null");
-    if (o->schedule != YF_SCHED_AUTO && o->schedule != YF_SCHED_CHUNKED)
+    if (o->schedule != YF_SCHED_AUTO && o->schedule != YF_SCHED_CHUNKED && o->schedule != YF_SCHED_PERSISTENT)
         return fail(YF_E_INVALID, "schedule %d unknown", o->schedule);
     if (o->chunk_tiles < 0) return fail(YF_E_INVALID, "chunk_tiles %d < 0", o->chunk_tiles);
     if (o->copy_stages != 0 && o->copy_stages != 3)

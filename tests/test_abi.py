@@ -104,18 +104,25 @@ def test_workspace_size_plan(yf):
     pool = yf.PagedKvPool(1, 4, 8, 128, device=None)
     L = yf.lib()
     row = 8 * 129 * 4   # one partial: rows_per_cta x (D + 1) floats
+    # few units: the cluster schedule, one cluster per unit for 8 units of 4 tiles (no partials)
+    assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 0
     # persistent decode: two partial slots per CTA, at least 16 tiles per CTA, at most 4 CTAs/SM
+    pool.set_options(schedule=_abi.YF_SCHED_PERSISTENT)
     assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 2 * 2 * row   # 32 tiles -> 2 CTAs
+    pool.set_options(schedule=_abi.YF_SCHED_AUTO)
     ws = L.yf_attn_workspace_size(pool.handle, 32, 16, 1, 32768)
-    assert ws == 148 * 4 * 2 * row
+    assert ws == 148 * 4 * 2 * row        # 128 units: persistent
     # past the persistent batch limit the chunked plan applies; short keys need no split
     assert L.yf_attn_workspace_size(pool.handle, 32, 2000, 1, 256) == 0
     assert L.yf_attn_workspace_size(pool.handle, 30, 16, 1, 32768) == 0   # Hq not a multiple of Hkv
     pool.close()
-    # few long units (one 131072-key entry, 2 kv heads, D 256): at most max(1.75 x 148, 128 per unit)
-    # = 259 CTAs instead of a full 4-per-SM wave
     long_pool = yf.PagedKvPool(1, 4, 2, 256, device=None)
     row256 = 8 * 257 * 4
+    # one 131072-key entry, 2 kv heads, D 256: 2 x 148 CTAs in clusters of 8 -> 18 clusters per
+    # unit, one partial per cluster
+    assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 2 * 18 * row256
+    # persistent: at most max(1.75 x 148, 128 per unit) = 259 CTAs instead of a full 4-per-SM wave
+    long_pool.set_options(schedule=_abi.YF_SCHED_PERSISTENT)
     assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 259 * 2 * row256
     long_pool.close()
 
@@ -128,7 +135,7 @@ def test_attention_options_are_explicit_and_validated(yf):
                               "prefill_kernel": 0, "wait_limit_us": 0, "launch": 0}
     pool.set_options(schedule=_abi.YF_SCHED_CHUNKED, chunk_tiles=8, wait_limit_us=20000)
     assert pool.options()["schedule"] == 1 and pool.options()["chunk_tiles"] == 8
-    for bad in ({"schedule": 2}, {"copy_stages": 2}, {"merge": 5}, {"prefill_kernel": -1},
+    for bad in ({"schedule": 3}, {"copy_stages": 2}, {"merge": 5}, {"prefill_kernel": -1},
                 {"chunk_tiles": -1}, {"wait_limit_us": 61_000_000}, {"launch": 2}):
         with pytest.raises(yf.YfError) as e:
             pool.set_options(**bad)

@@ -142,15 +142,39 @@ def test_workspace_and_argument_errors(yf, oracle, cuda):
     pool.close()
 
 
-def test_long_context_two_level_merge(yf, oracle, cuda):
-    """One slot, 2 kv heads, D 256 (the long-context decode shape) at 20000 keys: the persistent
-    schedule cuts each unit into ~80 pieces, merged in groups of 16 and then across groups."""
+@pytest.mark.parametrize("schedule", [0, 2])
+def test_long_context_split_merges(yf, oracle, cuda, schedule):
+    """One slot, 2 kv heads, D 256 (the long-context decode shape) at 20000 keys: the default
+    cluster schedule (clusters of 8 CTAs per kv head, merged through distributed shared memory,
+    then per column slice by the last cluster) and the persistent schedule (each unit cut into
+    ~100 pieces merged cooperatively) agree with the oracle, twice in a row."""
     wl = W.Workload("long", 16, 2, 256, ctx=[20000], q_rows=[1], seed=121)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=122)
+    pool.set_options(schedule=schedule)
     q = queries(wl, 123)
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(256))
     for _ in range(2):
         got = run_decode(yf, pool, wl, q, cuda)
         assert np.abs(got - ref).max() <= TOL
+    assert pool.status() == 0
+    pool.close()
+
+
+@pytest.mark.parametrize("ctx", [[1], [15, 16, 17], [0, 300, 5000, 1], [65, 1025, 40000, 7, 130, 2049, 0, 4096]])
+def test_cluster_schedule_ragged_few_units(yf, oracle, cuda, ctx):
+    """Few units of very different lengths (one to eight entries x 2 kv heads) on the cluster
+    schedule: short units use one cluster (output written by the cluster merge), long ones several
+    (merged per column slice by the last arrival); zero-length entries give zeros."""
+    n = len(ctx)
+    wl = W.Workload("fu", 16, 2, 256, ctx=ctx, q_rows=np.ones(n), seed=124 + n)
+    pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=125)
+    q = queries(wl, 126)
+    ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(256))
+    for _ in range(2):
+        got = run_decode(yf, pool, wl, q, cuda)
+        assert np.abs(got - ref).max() <= TOL, ctx
+    for b in range(n):
+        if ctx[b] == 0:
+            assert not got[b].any()
     assert pool.status() == 0
     pool.close()

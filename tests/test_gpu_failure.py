@@ -14,8 +14,9 @@ pytestmark = pytest.mark.gpu
 
 
 def test_merge_wait_times_out_and_pool_recovers(yf, oracle, cuda):
-    # one long entry, two kv heads: each kv head's unit is split over many CTAs of the persistent
-    # schedule, and the CTAs whose range ends inside it wait on its arrival counter
+    # one long entry, two kv heads on the persistent schedule: each kv head's unit is split over
+    # many CTAs, and the CTAs whose range ends inside it wait on its arrival counter (the default
+    # cluster schedule for so few units never waits)
     wl = W.Workload("to", 16, 2, 256, ctx=[20000], q_rows=[1], seed=141)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=142)
     q = queries(wl, 143)
@@ -23,7 +24,7 @@ def test_merge_wait_times_out_and_pool_recovers(yf, oracle, cuda):
     qd = torch.from_numpy(q).to(cuda)
     bt = torch.from_numpy(wl.block_table).to(cuda)
     scale = yf.default_scale(256)
-    pool.set_options(wait_limit_us=20000)   # 20 ms instead of 1 s
+    pool.set_options(wait_limit_us=20000, schedule=_abi.YF_SCHED_PERSISTENT)   # 20 ms instead of 1 s
     pool.plant_counter(0, 0xFFFF)          # unit (entry 0, kv head 0): the count never reaches its parts
     got = yf.dispatch_flash_decode_paged(qd, pool, 0, wl.cu_k, bt, scale).float().cpu().numpy()
     st = pool.status()                      # reads and clears; clearing a timeout resets the counters
