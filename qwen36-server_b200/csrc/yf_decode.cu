@@ -34,6 +34,7 @@
 // Calls on one pool must be stream-ordered (the counters belong to the pool).
 #include <algorithm>
 #include <cfloat>
+#include <mutex>
 
 #include "yf_device.cuh"
 #include "yf_internal.h"
@@ -1375,6 +1376,68 @@ template <int D, int NB, int NT>
 static int launch_tpp(const AttnArgs& a, const SplitPlan& plan, const SplitParams& p) {
     if (a.pool->desc.page_size == 16) return launch_st<D, NB, NT, 1>(a, plan, p);
     return launch_st<D, NB, NT, 4>(a, plan, p);
+}
+
+// ---- cluster capacity of decode_cluster_kernel ------------------------------------------------
+
+namespace {
+std::mutex g_cluster_mu;
+}
+
+template <int D, int NB, int TPP, int STAGES>
+static int cluster_capacity_t(int dev, int sm_count) {
+    static int cached[64] = {};
+    constexpr int TB = 32 * D + 64 * NB;
+    constexpr int SMEM = hdr_bytes<NB, 1>() + kWarps * STAGES * TB;
+    const int fallback = std::max(1, sm_count * 2 / kClusterCtas);
+    if (dev < 0 || dev >= 64) return fallback;
+    std::lock_guard<std::mutex> lock(g_cluster_mu);
+    if (cached[dev] > 0) return cached[dev];
+    auto kern = decode_cluster_kernel<D, NB, TPP, STAGES>;
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) return fallback;
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return fallback;
+    int n = 0;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kClusterCtas * 256);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = SMEM;
+        e = cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &cfg);
+    }
+    if (prev != dev) cudaSetDevice(prev);
+    if (e != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return fallback;
+    }
+    cached[dev] = n;
+    return n;
+}
+
+template <int D, int NB, int TPP>
+static int cluster_capacity_st(int dev, int sm, int stages) {
+    if (stages == 3) return cluster_capacity_t<D, NB, TPP, 3>(dev, sm);
+    if constexpr (D == 128)
+        return cluster_capacity_t<D, NB, TPP, 4>(dev, sm);
+    else
+        return cluster_capacity_t<D, NB, TPP, 2>(dev, sm);
+}
+
+int cluster_capacity(const yf_pool* pool, int stages) {
+    const yf_pool_desc& d = pool->desc;
+    const int dev = pool->base ? d.device : -1;
+    const bool rs = d.group_size == d.head_dim, p16 = d.page_size == 16;
+    if (d.head_dim == 128) {
+        if (rs) return p16 ? cluster_capacity_st<128, 1, 1>(dev, pool->sm_count, stages)
+                           : cluster_capacity_st<128, 1, 4>(dev, pool->sm_count, stages);
+        return p16 ? cluster_capacity_st<128, 4, 1>(dev, pool->sm_count, stages)
+                   : cluster_capacity_st<128, 4, 4>(dev, pool->sm_count, stages);
+    }
+    if (rs) return p16 ? cluster_capacity_st<256, 1, 1>(dev, pool->sm_count, stages)
+                       : cluster_capacity_st<256, 1, 4>(dev, pool->sm_count, stages);
+    return p16 ? cluster_capacity_st<256, 8, 1>(dev, pool->sm_count, stages)
+               : cluster_capacity_st<256, 8, 4>(dev, pool->sm_count, stages);
 }
 
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {

@@ -24,7 +24,7 @@ constexpr int kPersistentMaxBatch = 1024;
 // Upper bound of resident split-KV CTAs per SM (sizes the persistent schedule's workspace).
 constexpr int kMaxCtasPerSm = 4;
 // CTAs per thread-block cluster of the few-long-units decode schedule, and the most units it takes.
-constexpr int kClusterCtas = 8;
+constexpr int kClusterCtas = 4;
 constexpr int kClusterMaxUnits = 32;
 
 // Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).
@@ -143,6 +143,9 @@ struct AttnArgs {
 
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan);
+// Clusters of the few-long-units decode kernel that fit on the pool's device at once (one wave),
+// for a ring of `stages` copy stages (cached per device; an estimate for a host-only pool).
+int cluster_capacity(const yf_pool* pool, int stages);
 
 // Snapshot records: the CRC combine operators of the pool's record shape (yf_snapshot.cu).
 void init_record_ops(yf_pool* pool);

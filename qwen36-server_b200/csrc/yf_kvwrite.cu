@@ -136,15 +136,26 @@ __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const Writ
         __syncthreads();
     }
 
-    // ---- phase 1: rows into shared memory, group maxima, scales
-    for (int c = threadIdx.x; c < 2 * 16 * CPR; c += kTileThreads) {
+    // ---- phase 1: rows into shared memory, group maxima, scales.  All of the thread's loads are
+    // issued before the first is used.
+    constexpr int ITER = 2 * 16 * CPR / kTileThreads;
+    static_assert((2 * 16 * CPR) % kTileThreads == 0, "whole iterations");
+    uint4 wv[ITER];
+#pragma unroll
+    for (int i = 0; i < ITER; ++i) {
+        const int c = threadIdx.x + i * kTileThreads;
         const int kv = c / (16 * CPR), t = (c / CPR) % 16, q = c % CPR;
-        const bool on = live(t);
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (on) {
+        wv[i] = make_uint4(0, 0, 0, 0);
+        if (live(t)) {
             const __half* src = (kv ? p.v : p.k) + ((size_t)(p.cu_rows[b] + 16 * T + t - s) * p.H + h) * D;
-            w = __ldcs(reinterpret_cast<const uint4*>(src) + q);
+            wv[i] = __ldcs(reinterpret_cast<const uint4*>(src) + q);
         }
+    }
+#pragma unroll
+    for (int i = 0; i < ITER; ++i) {
+        const int c = threadIdx.x + i * kTileThreads;
+        const int kv = c / (16 * CPR), t = (c / CPR) % 16, q = c % CPR;
+        const uint4 w = wv[i];
         *reinterpret_cast<uint4*>(&rows[kv][t][16 * q]) = w;
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
         __half2 m2 = __float2half2_rn(0.f);
@@ -153,7 +164,7 @@ __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const Writ
         float amax = fmaxf(__low2float(m2), __high2float(m2));
 #pragma unroll
         for (int off = 1; off < LPG; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        if (on && q % LPG == 0) {
+        if (live(t) && q % LPG == 0) {
             const int grp = q / LPG;
             const float d = __fdiv_rn(amax, 127.0f);
             inv[kv][t][grp] = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
@@ -164,8 +175,13 @@ __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const Writ
     }
     __syncthreads();
 
+    // roundf(y) for |y| < 2^23 as trunc(y + copysign(0.5 - 2^-25, y)) with a round-to-nearest
+    // add: below .5 the sum stays under the next integer, from .5 up it reaches it (|y| <= 127
+    // here); the same value as roundf, in three instructions
     auto q8 = [](float x, float id) -> uint32_t {
-        return (uint32_t)excess128((int8_t)(int)roundf(__fmul_rn(x, id)));
+        const float y = __fmul_rn(x, id);
+        const int q = __float2int_rz(__fadd_rn(y, copysignf(0.49999997f, y)));
+        return (uint32_t)(q + 128) & 0xFFu;
     };
     // ---- phase 2a: K chunks (chunk kc = b32*32 + (t%8)*4 + r/8: dims 32*b32 + 8*(r/8) .. +7 of
     // tokens t%8 (bytes 0-7) and t%8 + 8 (bytes 8-15))
@@ -204,15 +220,19 @@ __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const Writ
     for (int vc = threadIdx.x; vc < D * 16 / 16; vc += kTileThreads) {
         const int M = vc / 32, iim = (vc % 32) / 4, tig = vc % 4;
         const int tok[4] = {2 * tig, 2 * tig + 8, 2 * tig + 1, 2 * tig + 9};
+        const int grp = 32 * M / G;  // the chunk's dims lie in one 32-dim block, so in one group
+        float id[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) id[jj] = inv[1][tok[jj]][grp];
         uint32_t out[4];
 #pragma unroll
         for (int wd = 0; wd < 4; ++wd) {
-            const int dim = 16 * (2 * M + wd / 2) + iim + 8 * (wd % 2), grp = dim / G;
+            const int dim = 16 * (2 * M + wd / 2) + iim + 8 * (wd % 2);
             uint32_t word = 0;
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 const float x = __half2float(*reinterpret_cast<const __half*>(&rows[1][tok[jj]][2 * dim]));
-                word |= q8(x, inv[1][tok[jj]][grp]) << (8 * jj);
+                word |= q8(x, id[jj]) << (8 * jj);
             }
             out[wd] = word;
         }
