@@ -24,7 +24,7 @@ constexpr int kPersistentMaxBatch = 1024;
 // Upper bound of resident split-KV CTAs per SM (sizes the persistent schedule's workspace).
 constexpr int kMaxCtasPerSm = 4;
 // CTAs per thread-block cluster of the few-long-units decode schedule, and the most units it takes.
-constexpr int kClusterCtas = 4;
+constexpr int kClusterCtas = 8;
 constexpr int kClusterMaxUnits = 32;
 
 // Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).

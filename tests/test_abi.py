@@ -118,9 +118,9 @@ def test_workspace_size_plan(yf):
     pool.close()
     long_pool = yf.PagedKvPool(1, 4, 2, 256, device=None)
     row256 = 8 * 257 * 4
-    # one 131072-key entry, 2 kv heads, D 256: clusters of 4, one wave (the host-only estimate: 2 x 148 / 4 = 74 clusters) -> 37 clusters per
-    # unit, one partial per cluster
-    assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 2 * 37 * row256
+    # one 131072-key entry, 2 kv heads, D 256: clusters of 8 CTAs, one wave of them (on a host-only
+    # pool the estimate 2 x 148 / 8 = 37 clusters) -> 18 clusters per unit, one partial each
+    assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 2 * 18 * row256
     # persistent: at most max(1.75 x 148, 128 per unit) = 259 CTAs instead of a full 4-per-SM wave
     long_pool.set_options(schedule=_abi.YF_SCHED_PERSISTENT)
     assert L.yf_attn_workspace_size(long_pool.handle, 16, 1, 1, 131072) == 259 * 2 * row256
