@@ -1065,131 +1065,19 @@ __global__ void __launch_bounds__(kThreads, min_ctas<D, NT>()) decode_persistent
 // ---- schedule 3: few long units over thread-block clusters ----------------------------------
 //
 // For a handful of long units (the long-context decode, a small decode, one rank's shard) every
-// unit gets whole clusters of kClusterCtas CTAs (max_chunks of them), sized so that the grid is
-// one wave of clusters.  The unit's tiles are handed out one at a time by a dispenser (an atomic
-// counter per unit): a warp that streams faster takes more tiles, so the unit's CTAs finish
-// together whether their SM hosts two CTAs or three.  After a cluster barrier, CTA rank r merges
-// column slice r of the unit's output over the cluster's warps (their stashed state) by
-// distributed shared-memory loads.  A unit held by one cluster writes its output there.
-// Otherwise each cluster writes its slices as a partial and counts an arrival per slice; the CTA
-// that arrives last for slice r merges the unit's cluster partials of that slice from L2 and
-// writes the output.  No CTA ever waits for another cluster, so the grid needs no co-residency
-// beyond the cluster, which the hardware schedules as one.
+// unit gets whole clusters of kClusterCtas CTAs; cluster lc of a unit streams tiles
+// [lc * tpc, (lc + 1) * tpc) of it, split evenly over its CTAs.  Each CTA merges its 4 warps into
+// a normalised partial in its own shared memory; after a cluster barrier, CTA rank r merges
+// column slice r of the unit's output over the cluster's CTAs by distributed shared-memory loads.
+// A unit held by one cluster writes its output there.  Otherwise each cluster writes its slices
+// as a partial and counts an arrival per slice; the CTA that arrives last for slice r merges the
+// unit's cluster partials of that slice from L2 and writes the output (its counter back to zero).
+// No CTA ever waits for another cluster, so the grid needs no co-residency beyond the cluster,
+// which the hardware schedules as one.
 
-// Tile indices of a warp's ring stages (the dispensed stream), after the barriers and flags.
-constexpr int kTileIdOff = 160;
-static_assert(kTileIdOff >= kWarps * 4 * 9 && kTileIdOff + kWarps * 4 * 4 <= kHdrBytes, "header layout");
-
-// Streams the unit's tiles this warp takes from *disp until the unit's n_tiles are handed out.
-// Lane 0 runs a two-step pipeline so that no latency sits on the issue path: the atomic that
-// takes tile k+2 and the page-id load of tile k+1 are in flight while tile k's copy is issued.
-// The first take is STAGES + 1 tiles at once (their page ids loaded together).
-template <int D, int NB, int TPP, int STAGES>
-__device__ __forceinline__ void stream_dispensed(const SplitParams& p, TileRing<32 * D + 64 * NB, STAGES>& ring,
-                                                 int* tile_id, int b, int h, int n_tiles, uint32_t* disp,
-                                                 const uint4 (&qf)[1][D / 32], const int (&kvlen)[1][2], int kv_min,
-                                                 WarpAcc<D, 1>& a, int lane) {
-    constexpr int TB = 32 * D + 64 * NB;
-    const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
-    const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
-    const long long page_stride = p.phb * p.H;
-    // lane 0's pipeline: t1 / p1 = the next tile to issue and its page id, g = the pending take
-    int t1 = -1, g = n_tiles, issued = 0;
-    uint32_t p1 = 0;
-    bool ended = false;
-    auto issue_slot = [&](int slot, int t, uint32_t page) {  // lane 0; t < 0 ends the stream
-        tile_id[slot] = t;
-        if (t < 0) {
-            ring.flag[slot] = 0;
-            mbar_arrive(&ring.bar[slot]);
-            return;
-        }
-        if (page < (uint32_t)p.n_pages) {
-            ring.flag[slot] = 1;
-            mbar_arrive_expect_tx(&ring.bar[slot], TB);
-            bulk_g2s(ring.stage + slot * TB, head_base + (size_t)page * page_stride + (t % TPP) * TB, TB, &ring.bar[slot]);
-        } else {
-            ring.flag[slot] = 0;
-            atomicOr(p.status, YF_DEV_BAD_PAGE);
-            mbar_arrive(&ring.bar[slot]);
-        }
-    };
-    auto step = [&]() {  // lane 0: issue the pipeline's tile into the next slot, advance the pipeline
-        if (ended) return;
-        issue_slot((ring.base + issued) % STAGES, t1, p1);
-        ++issued;
-        if (t1 < 0) {
-            ended = true;
-            return;
-        }
-        t1 = g < n_tiles ? g : -1;
-        p1 = t1 >= 0 ? __ldg(btrow + t1 / TPP) : 0u;
-        g = t1 >= 0 ? (int)atomicAdd(disp, 1u) : n_tiles;
-    };
-    if (lane == 0) {
-        const int g0 = (int)atomicAdd(disp, (uint32_t)(STAGES + 1));
-        uint32_t pg[STAGES + 1];
-#pragma unroll
-        for (int s = 0; s <= STAGES; ++s) pg[s] = g0 + s < n_tiles ? __ldg(btrow + (g0 + s) / TPP) : 0u;
-        g = g0 + STAGES < n_tiles ? (int)atomicAdd(disp, 1u) : n_tiles;
-#pragma unroll
-        for (int s = 0; s < STAGES; ++s) {
-            if (ended) break;
-            const int t = g0 + s < n_tiles ? g0 + s : -1;
-            issue_slot((ring.base + issued) % STAGES, t, pg[s]);
-            ++issued;
-            ended = t < 0;
-        }
-        t1 = g0 + STAGES < n_tiles ? g0 + STAGES : -1;
-        p1 = pg[STAGES];
-    }
-    __syncwarp();
-    int done = 0;
-    bool ok = true;
-    for (int i = 0;; ++i) {
-        const int pos = ring.base + i;
-        const int slot = pos % STAGES;
-        if (!__all_sync(0xffffffffu, mbar_wait(&ring.bar[slot], (uint32_t)(pos / STAGES) & 1u, p.wait_ns))) {
-            if (lane == 0) atomicOr(p.status, YF_DEV_TIMEOUT);
-            ok = false;
-            break;
-        }
-        done = i + 1;
-        const int t = tile_id[slot];
-        if (t < 0) break;  // the end marker: every earlier tile is consumed
-        if (ring.flag[slot])
-            tile_math<D, NB, 1, false>(ring.stage + slot * TB, t, qf, kvlen, kv_min, nullptr, p.scale_log2, a, lane,
-                                       TreeCtx{});
-        __syncwarp();
-        if (lane == 0) step();
-    }
-    if (!ok) {  // wait (bounded) for the copies still in flight
-        const int n_issued = __shfl_sync(0xffffffffu, issued, 0);
-        for (int i = done; i < n_issued; ++i)
-            (void)mbar_wait(&ring.bar[(ring.base + i) % STAGES], (uint32_t)((ring.base + i) / STAGES) & 1u, p.wait_ns);
-    }
-    __syncwarp();
-}
-
-// Online merge of one part given as (base-2 running max mv, sum lv, unnormalised O ov) into
-// (M, L, O) with O unnormalised against M.
-__device__ __forceinline__ void merge_raw(float mv, float lv, float4 ov, float& M, float& L, float4& O) {
-    if (mv == -INFINITY) return;
-    if (mv > M) {
-        const float f = M == -INFINITY ? 0.f : fast_exp2(M - mv);
-        L *= f;
-        O.x *= f;
-        O.y *= f;
-        O.z *= f;
-        O.w *= f;
-        M = mv;
-    }
-    const float w = fast_exp2(mv - M);
-    L = fmaf(w, lv, L);
-    O.x = fmaf(w, ov.x, O.x);
-    O.y = fmaf(w, ov.y, O.y);
-    O.z = fmaf(w, ov.z, O.z);
-    O.w = fmaf(w, ov.w, O.w);
+template <int D>
+constexpr int cluster_part_off() {  // the CTA partial, after the 4-warp stash in the stage area
+    return ((2 * kWarps * 8 * 4 + kWarps * 8 * (D + 4) * 4) + 127) / 128 * 128;
 }
 
 template <int D, int NB, int TPP, int STAGES>
@@ -1200,87 +1088,109 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads,
     constexpr int DP = D + 4;
     constexpr int COLS = RPC * (D / 4);  // float4 columns of a unit's output
     constexpr int SLICE = COLS / CL;
-    constexpr int PB = 16;               // partials loaded together by the final merge
     static_assert(SLICE <= kThreads && COLS % CL == 0, "one column per thread in a slice");
+    static_assert(cluster_part_off<D>() + RPC * (D + 1) * 4 <= kWarps * STAGES * TB, "partial area");
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem + hdr_bytes<NB, NT>();
-    int* tile_id = reinterpret_cast<int*>(smem + kTileIdOff);
+    float* part_lse = reinterpret_cast<float*>(stages + cluster_part_off<D>());  // [RPC] base-2 lse
+    float* part_o = part_lse + RPC;                                               // [RPC][D] normalised
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = (int)cluster_rank();
     const int cid = blockIdx.x / CL;
-    const int cpu = p.max_chunks;  // clusters per unit
+    const int cpu = p.max_chunks, tpc = p.chunk_tiles;  // clusters per unit, tiles per cluster
     const int uidx = cid / cpu, lc = cid % cpu;
     const int b = uidx / p.H, h = uidx % p.H;
     UnitGeom u;
     unit_geom<TPP, RPC>(p, b, 0, u, lc == 0 && r == 0 && threadIdx.x == 0);
-    // a unit uses at most one cluster per chunk_tiles of its tiles (at least one, for its output)
-    const int n_u = min(cpu, max(1, (u.n_tiles + p.chunk_tiles - 1) / p.chunk_tiles));
-    if (lc >= n_u) return;  // the whole cluster leaves together
-    uint32_t* disp = &p.counters[kMaxCombineUnits + uidx];
+    const int n_u = max(1, (u.n_tiles + tpc - 1) / tpc);  // clusters this unit uses
+    if (lc >= n_u) return;                               // the whole cluster leaves together
+    const int c0 = lc * tpc, c1 = min(c0 + tpc, u.n_tiles), len = max(c1 - c0, 0);
+    const int t0 = c0 + r * len / CL, t1 = c0 + (r + 1) * len / CL;
 
     TileRing<TB, STAGES> ring;
     ring.init(smem, stages, warp, lane);
     WarpAcc<D, NT> acc;
     uint4 qf[NT][D / 32];
     int kvlen[NT][2], kv_min;
-    load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, nullptr);
+    load_unit_q<D, NT, NB>(p, u, h, lane, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp));
     acc.reset();
-    stream_dispensed<D, NB, TPP, STAGES>(p, ring, tile_id + warp * STAGES, b, h, u.n_tiles, disp, qf, kvlen, kv_min,
-                                         acc, lane);
-    stash_warp<D, NT>(stages, acc, warp, lane);  // (m, l, O) of every warp in shared memory
-    cluster_barrier();  // every CTA's warps are stashed
-    // slice r of the columns, merged over the cluster's CTA x warp parts by distributed
-    // shared-memory loads
-    const float* mw = reinterpret_cast<const float*>(stages);
-    const float* lw = mw + kWarps * RPC;
-    const float* ow = lw + kWarps * RPC;
+    stream_unit<D, NB, NT, TPP, STAGES>(p, ring, b, h, t0, t1 - t0, qf, kvlen, kv_min, kbias_area<NB, NT>(smem, warp),
+                                        acc, warp, lane, TreeCtx{});
+    stash_warp<D, NT>(stages, acc, warp, lane);
+    {  // the 4 warps into this CTA's partial
+        const float* mw = reinterpret_cast<const float*>(stages);
+        const float* lw = mw + kWarps * RPC;
+        const float* ow = lw + kWarps * RPC;
+        for (int e = threadIdx.x; e < RPC * (D / 4); e += kThreads) {
+            const int row = e / (D / 4), d4 = (e % (D / 4)) * 4;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mw[w * RPC + row]);
+            float L = 0.f;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float mv = mw[w * RPC + row];
+                if (mv == -INFINITY) continue;
+                const float f = fast_exp2(mv - M);
+                L = fmaf(f, lw[w * RPC + row], L);
+                const float4 ov = *reinterpret_cast<const float4*>(&ow[(w * RPC + row) * DP + d4]);
+                o.x = fmaf(f, ov.x, o.x);
+                o.y = fmaf(f, ov.y, o.y);
+                o.z = fmaf(f, ov.z, o.z);
+                o.w = fmaf(f, ov.w, o.w);
+            }
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            *reinterpret_cast<float4*>(&part_o[row * D + d4]) = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+            if (d4 == 0) part_lse[row] = L > 0.f ? M + __log2f(L) : -INFINITY;
+        }
+    }
+    cluster_barrier();  // every CTA's partial is in its shared memory
+    // slice r of the columns, merged over the cluster's CTAs through distributed shared memory
     const int col = r * SLICE + threadIdx.x;
     const int row = col / (D / 4), d4 = (col % (D / 4)) * 4;
-    float M = -INFINITY, L = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = -INFINITY, l = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     if (threadIdx.x < SLICE) {
+        float lv[CL];
+        float4 ov[CL];
 #pragma unroll
-        for (int q0 = 0; q0 < CL; q0 += 2) {
-            float mv[2 * kWarps], lv[2 * kWarps];
-            float4 ov[2 * kWarps];
-#pragma unroll
-            for (int j = 0; j < 2 * kWarps; ++j) {
-                const int q = q0 + j / kWarps, w = j % kWarps;
-                mv[j] = ld_dsmem_f32(dsmem_addr(&mw[w * RPC + row], q));
-                lv[j] = ld_dsmem_f32(dsmem_addr(&lw[w * RPC + row], q));
-                ov[j] = ld_dsmem_f32x4(dsmem_addr(&ow[(w * RPC + row) * DP + d4], q));
-            }
-#pragma unroll
-            for (int j = 0; j < 2 * kWarps; ++j) merge_raw(mv[j], lv[j], ov[j], M, L, O);
+        for (int q = 0; q < CL; ++q) {
+            lv[q] = ld_dsmem_f32(dsmem_addr(&part_lse[row], q));
+            ov[q] = ld_dsmem_f32x4(dsmem_addr(&part_o[row * D + d4], q));
         }
+#pragma unroll
+        for (int q = 0; q < CL; ++q) merge_in(lv[q], ov[q], m, l, o);
     }
     cluster_barrier();  // no CTA leaves, or reuses its shared memory, while a peer still reads it
     const bool live_row = threadIdx.x < SLICE && u.row_begin + row < u.rows_total;
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const float4 on = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-    const float lse = L > 0.f ? M + __log2f(L) : -INFINITY;
     if (n_u == 1) {
-        if (live_row) store_row4(p, u, h, u.row_begin + row, d4, D, on, lse);
-        if (r == 0 && threadIdx.x == 0) *disp = 0;  // every warp of the unit is done taking tiles
+        if (live_row) {
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
+                       l > 0.f ? m + __log2f(l) : -INFINITY);
+        }
         return;
     }
     // this cluster's partial of slice r, then the slice's arrival
     const size_t item = (size_t)uidx * cpu + lc;
     if (threadIdx.x < SLICE) {
-        __stcg(reinterpret_cast<float4*>(p.ws_o + (item * RPC + row) * D + d4), on);
-        if (d4 == 0) __stcg(p.ws_lse + item * RPC + row, lse);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __stcg(reinterpret_cast<float4*>(p.ws_o + (item * RPC + row) * D + d4),
+               make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv));
+        if (d4 == 0) __stcg(p.ws_lse + item * RPC + row, l > 0.f ? m + __log2f(l) : -INFINITY);
     }
     uint32_t* ctr = &p.counters[(size_t)uidx * CL + r];
     if (!arrive_last(ctr, n_u, &s_last)) return;
     if (live_row) {
         float m2 = -INFINITY, l2 = 0.f;
         float4 o2 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k0 = 0; k0 < n_u; k0 += PB) {
-            float lv[PB];
-            float4 ov[PB];
+        for (int k0 = 0; k0 < n_u; k0 += 16) {
+            float lv[16];
+            float4 ov[16];
 #pragma unroll
-            for (int j = 0; j < PB; ++j) {
+            for (int j = 0; j < 16; ++j) {
                 lv[j] = -INFINITY;
                 ov[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (k0 + j < n_u) {
@@ -1290,16 +1200,13 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads,
                 }
             }
 #pragma unroll
-            for (int j = 0; j < PB; ++j) merge_in(lv[j], ov[j], m2, l2, o2);
+            for (int j = 0; j < 16; ++j) merge_in(lv[j], ov[j], m2, l2, o2);
         }
-        const float inv2 = l2 > 0.f ? 1.f / l2 : 0.f;
-        store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o2.x * inv2, o2.y * inv2, o2.z * inv2, o2.w * inv2),
+        const float inv = l2 > 0.f ? 1.f / l2 : 0.f;
+        store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o2.x * inv, o2.y * inv, o2.z * inv, o2.w * inv),
                    l2 > 0.f ? m2 + __log2f(l2) : -INFINITY);
     }
-    if (threadIdx.x == 0) {
-        *ctr = 0;                   // ready for the next call on this pool
-        if (r == 0) *disp = 0;      // every cluster of the unit has arrived: its warps are done
-    }
+    if (threadIdx.x == 0) *ctr = 0;  // ready for the next call on this pool
 }
 
 // ---- schedule 2: a 3-D grid of (unit, chunk of tiles) ----------------------------------------

@@ -118,15 +118,15 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
                    units <= kMaxCombineUnits && in_kernel_merge;
     if (p.persistent) p.fused_combine = true;
     // A few long units (long-context decode, one rank's shard, a small decode): whole clusters of
-    // kClusterCtas CTAs per unit, at least 16 tiles per CTA and up to three CTAs per SM in all
-    // (the split-KV tile math needs ~12 warps per SM to keep up with HBM).
+    // kClusterCtas CTAs per unit, at least 16 tiles per CTA and about two CTAs per SM in all (a
+    // third CTA per SM measured slower: more partials to merge, uneven CTAs per SM).
     p.cluster = p.persistent && o.schedule == YF_SCHED_AUTO && p.rows_per_cta == 8 && units <= kClusterMaxUnits &&
                 tiles > 0;
     if (p.cluster) {
         p.persistent = false;
         // one wave of clusters: cluster placement is per GPC, so the device's cluster capacity,
         // not SMs x CTAs per SM, bounds the grid (a partial second wave doubles the time)
-        const long long target = std::min((long long)pool->sm_count * 3, std::max<long long>(kClusterCtas, units * tiles / 16));
+        const long long target = std::min((long long)pool->sm_count * 2, std::max<long long>(kClusterCtas, units * tiles / 16));
         const long long cap = cluster_capacity(pool, p.stages);
         const long long cpu = std::max<long long>(1, std::min(target / (units * kClusterCtas), cap / units));
         p.max_chunks = (int)cpu;                         // clusters per unit
