@@ -157,6 +157,8 @@ YF_API int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear);
 #define YF_MERGE_SEPARATE 1    /* chunked schedule: a separate combine launch merges the partials */
 #define YF_PREFILL_AUTO 0      /* tcgen05 prefill kernel where it applies (>= 128 rows per kv head) */
 #define YF_PREFILL_SPLITKV 1   /* every query block on the split-KV kernel */
+#define YF_VERIFY_AUTO 0       /* tcgen05 verify kernel for 2..32 query rows per kv head (D 128, groups of 32) */
+#define YF_VERIFY_SPLITKV 1    /* verify blocks on the split-KV (mma.sync) kernel */
 /* The persistent decode's CTAs wait for one another's split partials, so all of them must be
  * resident at once.  Its grid never exceeds one resident wave, so against other kernels that
  * finish by themselves (other streams, other pools) a plain launch completes; only kernels that
@@ -173,7 +175,8 @@ typedef struct yf_attn_options {
     int32_t prefill_kernel;  /* YF_PREFILL_* */
     uint32_t wait_limit_us;  /* bound of every in-kernel wait (copies, merges); 0 = 1 000 000 (1 s) */
     int32_t launch;          /* YF_LAUNCH_*: how the persistent decode is launched */
-    int32_t reserved[9];     /* zero */
+    int32_t verify_kernel;   /* YF_VERIFY_* */
+    int32_t reserved[8];     /* zero */
 } yf_attn_options;
 /* Replaces the pool's options (validated: YF_E_INVALID for an unknown value).  Not
  * stream-ordered: set them between calls, not while the pool's kernels run. */

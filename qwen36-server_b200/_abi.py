@@ -35,6 +35,8 @@ YF_MERGE_SEPARATE = 1
 YF_PREFILL_AUTO = 0
 YF_PREFILL_SPLITKV = 1
 YF_LAUNCH_PLAIN = 0
+YF_VERIFY_AUTO = 0
+YF_VERIFY_SPLITKV = 1
 YF_LAUNCH_COOPERATIVE = 1
 YF_POOL_COUNTERS = 65536 + 4096
 YF_REC_REJECTED = 0
@@ -68,7 +70,7 @@ class AttnOptions(ctypes.Structure):
     _fields_ = [
         ("schedule", ctypes.c_int32), ("chunk_tiles", ctypes.c_int32), ("copy_stages", ctypes.c_int32),
         ("merge", ctypes.c_int32), ("prefill_kernel", ctypes.c_int32), ("wait_limit_us", ctypes.c_uint32),
-        ("launch", ctypes.c_int32), ("reserved", ctypes.c_int32 * 9),
+        ("launch", ctypes.c_int32), ("verify_kernel", ctypes.c_int32), ("reserved", ctypes.c_int32 * 8),
     ]
 
 

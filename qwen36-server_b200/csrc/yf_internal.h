@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "yfattn.h"
@@ -149,6 +150,18 @@ int cluster_capacity(const yf_pool* pool, int stages);
 
 // Snapshot records: the CRC combine operators of the pool's record shape (yf_snapshot.cu).
 void init_record_ops(yf_pool* pool);
+
+// Tensor-core (tcgen05) MTP / tree verify for query blocks of 2..32 rows per kv head
+// (yf_verify_tc.cu): keys as the MMA's M, split over CTAs in chunks of key tiles.
+struct VerifyPlan {
+    int rows;          // N of the MMAs: 16 or 32 query rows per unit
+    int chunk_tiles;   // 128-key tiles per CTA
+    int max_chunks;
+    size_t ws_bytes;   // chunk partials (O + lse), 0 with one chunk per unit
+};
+bool verify_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q, bool tree);
+VerifyPlan plan_verify(const yf_pool* pool, int n_q_heads, int batch, int max_seqlen_q, int max_seqlen_k);
+int launch_verify_tc(const AttnArgs& a, const VerifyPlan& plan);
 
 // Tensor-core (tcgen05) causal prefill for query blocks of >= 128 rows per kv head
 // (yf_prefill_tc.cu); needs no workspace.

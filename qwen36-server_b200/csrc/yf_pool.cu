@@ -376,6 +376,8 @@ static int check_options(const yf_attn_options* o) {
     if (o->wait_limit_us > 60u * 1000000u) return fail(YF_E_INVALID, "wait_limit_us above 60 s");
     if (o->launch != YF_LAUNCH_PLAIN && o->launch != YF_LAUNCH_COOPERATIVE)
         return fail(YF_E_INVALID, "launch %d unknown", o->launch);
+    if (o->verify_kernel != YF_VERIFY_AUTO && o->verify_kernel != YF_VERIFY_SPLITKV)
+        return fail(YF_E_INVALID, "verify_kernel %d unknown", o->verify_kernel);
     for (int32_t r : o->reserved)
         if (r) return fail(YF_E_INVALID, "reserved option fields must be zero");
     return YF_OK;
@@ -471,10 +473,13 @@ static int check_attn(const yf_pool* pool, int32_t layer, const void* q, int32_t
 size_t yf_attn_workspace_size(const yf_pool* pool, int32_t hq, int32_t batch, int32_t max_q, int32_t max_k) {
     if (!pool || batch <= 0 || hq < pool->desc.n_kv_heads || hq % pool->desc.n_kv_heads) return 0;
     if (max_q > kMaxTreeRowsHost && prefill_tc_applies(pool, hq, max_q)) return 0;
-    // query blocks a tree verify can take: room for both schedules
-    const size_t ws = plan_split(pool, hq, batch, max_q, max_k, false).ws_bytes;
+    // query blocks a causal or a tree verify can take: room for every schedule that may run
+    size_t ws = plan_split(pool, hq, batch, max_q, max_k, false).ws_bytes;
     if (max_q <= 1 || max_q > kMaxTreeRowsHost) return ws;
-    return std::max(ws, plan_split(pool, hq, batch, max_q, max_k, true).ws_bytes);
+    ws = std::max(ws, plan_split(pool, hq, batch, max_q, max_k, true).ws_bytes);
+    if (verify_tc_applies(pool, hq, max_q, false) || verify_tc_applies(pool, hq, max_q, true))
+        ws = std::max(ws, plan_verify(pool, hq, batch, max_q, max_k).ws_bytes);
+    return ws;
 }
 
 static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_q,
@@ -486,9 +491,12 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     if (rc || batch == 0) return rc;
     if (part_o && (!part_lse || !aligned(part_lse, 4))) return fail(YF_E_INVALID, "lse output null or misaligned");
     const bool tc = !part_o && !trie && cu_q && prefill_tc_applies(pool, hq, max_q);
+    const bool vtc = !tc && !part_o && cu_q && verify_tc_applies(pool, hq, max_q, trie != nullptr);
     const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k, trie != nullptr);
-    if (!tc && plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
-        return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", plan.ws_bytes,
+    const VerifyPlan vplan = vtc ? plan_verify(pool, hq, batch, max_q, max_k) : VerifyPlan{};
+    const size_t need = tc ? 0 : (vtc ? vplan.ws_bytes : plan.ws_bytes);
+    if (need > 0 && (!ws || ws_bytes < need || !aligned(ws, 16)))
+        return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", need,
                     ws ? ws_bytes : (size_t)0);
     AttnArgs a;
     a.pool = pool;
@@ -511,6 +519,7 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     a.part_lse = part_lse;
     a.trie = trie;
     if (tc) return launch_prefill_tc(a);
+    if (vtc) return launch_verify_tc(a, vplan);
     return launch_splitkv(a, plan);
 }
 

@@ -132,11 +132,13 @@ def test_attention_options_are_explicit_and_validated(yf):
     are refused and leave the options unchanged, and the workspace query follows the schedule."""
     pool = yf.PagedKvPool(1, 4096, 8, 128, device=None)
     assert pool.options() == {"schedule": 0, "chunk_tiles": 0, "copy_stages": 0, "merge": 0,
-                              "prefill_kernel": 0, "wait_limit_us": 0, "launch": 0}
+                              "prefill_kernel": 0, "wait_limit_us": 0, "launch": 0,
+                              "verify_kernel": 0}
     pool.set_options(schedule=_abi.YF_SCHED_CHUNKED, chunk_tiles=8, wait_limit_us=20000)
     assert pool.options()["schedule"] == 1 and pool.options()["chunk_tiles"] == 8
     for bad in ({"schedule": 3}, {"copy_stages": 2}, {"merge": 5}, {"prefill_kernel": -1},
-                {"chunk_tiles": -1}, {"wait_limit_us": 61_000_000}, {"launch": 2}):
+                {"chunk_tiles": -1}, {"wait_limit_us": 61_000_000}, {"launch": 2},
+                {"verify_kernel": 2}):
         with pytest.raises(yf.YfError) as e:
             pool.set_options(**bad)
         assert e.value.code == _abi.YF_E_INVALID, bad
