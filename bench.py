@@ -1038,6 +1038,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="N>1: skip the sharded decode_long leg")
     ap.add_argument("--schedule", default="auto", choices=sorted(SCHEDULES),
                     help="split-KV schedule of the pools (yf_attn_options.schedule), for A/B runs")
+    ap.add_argument("--verify-kernel", default="auto", choices=["auto", "tcgen05"],
+                    help="verify blocks on the split-KV kernel (auto) or the tcgen05 kernel (yf_attn_options.verify_kernel)")
     ap.add_argument("--cooperative", action="store_true",
                     help="launch the persistent decode cooperatively (yf_attn_options.launch)")
     ap.add_argument("--layers", type=int, default=0,
@@ -1045,7 +1047,8 @@ def main():
                          "its shape; for profiling a launch with a few GB resident, not a bench line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    POOL_OPTIONS.update(schedule=SCHEDULES[args.schedule], launch=1 if args.cooperative else 0)
+    POOL_OPTIONS.update(schedule=SCHEDULES[args.schedule], launch=1 if args.cooperative else 0,
+                        verify_kernel=1 if args.verify_kernel == "tcgen05" else 0)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

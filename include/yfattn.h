@@ -157,8 +157,8 @@ YF_API int yf_pool_status(yf_pool* pool, uint32_t* out_bits, int clear);
 #define YF_MERGE_SEPARATE 1    /* chunked schedule: a separate combine launch merges the partials */
 #define YF_PREFILL_AUTO 0      /* tcgen05 prefill kernel where it applies (>= 128 rows per kv head) */
 #define YF_PREFILL_SPLITKV 1   /* every query block on the split-KV kernel */
-#define YF_VERIFY_AUTO 0       /* tcgen05 verify kernel for 2..32 query rows per kv head (D 128, groups of 32) */
-#define YF_VERIFY_SPLITKV 1    /* verify blocks on the split-KV (mma.sync) kernel */
+#define YF_VERIFY_AUTO 0       /* verify blocks on the split-KV kernel (measured faster at <= 32 rows per kv head) */
+#define YF_VERIFY_TCGEN05 1    /* verify blocks of 2..32 rows per kv head (D 128, groups of 32) on the tcgen05 kernel */
 /* The persistent decode's CTAs wait for one another's split partials, so all of them must be
  * resident at once.  Its grid never exceeds one resident wave, so against other kernels that
  * finish by themselves (other streams, other pools) a plain launch completes; only kernels that

@@ -36,7 +36,7 @@ YF_PREFILL_AUTO = 0
 YF_PREFILL_SPLITKV = 1
 YF_LAUNCH_PLAIN = 0
 YF_VERIFY_AUTO = 0
-YF_VERIFY_SPLITKV = 1
+YF_VERIFY_TCGEN05 = 1
 YF_LAUNCH_COOPERATIVE = 1
 YF_POOL_COUNTERS = 65536 + 4096
 YF_REC_REJECTED = 0

@@ -376,7 +376,7 @@ static int check_options(const yf_attn_options* o) {
     if (o->wait_limit_us > 60u * 1000000u) return fail(YF_E_INVALID, "wait_limit_us above 60 s");
     if (o->launch != YF_LAUNCH_PLAIN && o->launch != YF_LAUNCH_COOPERATIVE)
         return fail(YF_E_INVALID, "launch %d unknown", o->launch);
-    if (o->verify_kernel != YF_VERIFY_AUTO && o->verify_kernel != YF_VERIFY_SPLITKV)
+    if (o->verify_kernel != YF_VERIFY_AUTO && o->verify_kernel != YF_VERIFY_TCGEN05)
         return fail(YF_E_INVALID, "verify_kernel %d unknown", o->verify_kernel);
     for (int32_t r : o->reserved)
         if (r) return fail(YF_E_INVALID, "reserved option fields must be zero");

@@ -47,6 +47,7 @@ constexpr int kVtBlock = kVtWarps * 32;
 constexpr int kVtCtl = 8, kVtCopy = 9;
 constexpr float kVtRescale = 8.0f;           // lazy rescale threshold (base 2)
 constexpr int kVtMaxTree = 64;               // draft rows of a tree entry (64-bit ancestor masks)
+constexpr int kVtMaxChunkTiles = 64;         // key tiles of one CTA (its page ids live in shared memory)
 
 // Shared-memory map (bytes from a 1024-aligned base) for N query rows per unit.
 template <int N>
@@ -59,7 +60,8 @@ struct VtMap {
     static constexpr int MISC = RAW + 2 * kVtPoolTiles * kVtRawPitch;
     static constexpr int ANC = MISC + 512;                      // [64] ancestor masks (tree)
     static constexpr int RED = ANC + kVtMaxTree * 8;            // [4 warps][N] row scratch
-    static constexpr int ALLOC = RED + 4 * N * 4;
+    static constexpr int PGS = RED + 4 * N * 4;                 // [64 key tiles x 8] page ids of the chunk
+    static constexpr int ALLOC = PGS + kVtMaxChunkTiles * kVtPoolTiles * 4;
     static_assert(ALLOC <= 232448, "shared memory");
 };
 
@@ -171,6 +173,7 @@ __global__ void __launch_bounds__(kVtBlock, 1) verify_tc_kernel(const VerifyPara
     int* s_last = reinterpret_cast<int*>(base + Map::MISC + 284);
     unsigned long long* anc = reinterpret_cast<unsigned long long*>(base + Map::ANC);
     float* red = reinterpret_cast<float*>(base + Map::RED);
+    uint32_t* pgs = reinterpret_cast<uint32_t*>(base + Map::PGS);  // page id of every pool tile of the chunk
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -241,9 +244,15 @@ __global__ void __launch_bounds__(kVtBlock, 1) verify_tc_kernel(const VerifyPara
                 sts128(sbase + Map::Q + sw128_off(r, cc, N), live ? __ldg(qp + cc) : make_uint4(0, 0, 0, 0));
         }
         fence_proxy_async_smem();
-        // every page this CTA reads exists (the common case skips per-key page checks)
-        for (int pt = kt0 * kVtPoolTiles + tid; pt < min((kt0 + n) * kVtPoolTiles, pt_total); pt += 128)
-            if (__ldg(btrow + pt / p.tpp) >= (uint32_t)p.n_pages) bad = 1;
+        // the page id of every pool tile of the chunk, read once: the copy warp then issues each
+        // key tile's copies without a dependent global load; every page the CTA reads exists in
+        // the common case, which skips per-key page checks
+        for (int i = tid; i < n * kVtPoolTiles; i += 128) {
+            const int pt = kt0 * kVtPoolTiles + i;
+            const uint32_t pg = pt < pt_total ? __ldg(btrow + pt / p.tpp) : (uint32_t)p.n_pages;
+            pgs[i] = pg;
+            if (pt < pt_total && pg >= (uint32_t)p.n_pages) bad = 1;
+        }
         if constexpr (TREE) {
             // ancestor masks of the entry's draft nodes from their subtree ranges (clamped to the
             // block; a range outside it flags YF_DEV_BAD_ROWS)
@@ -319,21 +328,11 @@ __global__ void __launch_bounds__(kVtBlock, 1) verify_tc_kernel(const VerifyPara
     } else if (warp == kVtCopy) {
         // ================= copies: the 8 pool tiles of a key tile into the raw ring =================
         if (lane == 0) {
-            uint32_t page[kVtPoolTiles];
-            auto fetch_pages = [&](int kt) {
-#pragma unroll
-                for (int j = 0; j < kVtPoolTiles; ++j) {
-                    const int pt = kt * kVtPoolTiles + j;
-                    page[j] = pt < pt_total ? __ldg(btrow + pt / p.tpp) : (uint32_t)p.n_pages;
-                }
-            };
-            if (n > 0) fetch_pages(kt0);
             for (int i = 0; i < n; ++i) {
                 const int kt = kt0 + i, slot = i & 1;
                 uint32_t cur[kVtPoolTiles];
 #pragma unroll
-                for (int j = 0; j < kVtPoolTiles; ++j) cur[j] = page[j];
-                if (i + 1 < n) fetch_pages(kt + 1);  // in flight while this stage waits
+                for (int j = 0; j < kVtPoolTiles; ++j) cur[j] = pgs[i * kVtPoolTiles + j];
                 if (i >= 2 && !vt_wait(&bars->raw_free[slot], (i >> 1) - 1, s_abort, p.status, p.wait_ns)) break;
                 uint8_t* dst = base + Map::RAW + slot * kVtPoolTiles * kVtRawPitch;
                 uint32_t bytes = 0;
@@ -459,7 +458,7 @@ __global__ void __launch_bounds__(kVtBlock, 1) verify_tc_kernel(const VerifyPara
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->s_free[i & 1]);
             bool key_live = key < Tk;
-            if (!pages_ok && key_live) key_live = __ldg(btrow + (key >> 4) / p.tpp) < (uint32_t)p.n_pages;
+            if (!pages_ok && key_live) key_live = pgs[i * kVtPoolTiles + (tid >> 4)] < (uint32_t)p.n_pages;
             bool need = false;
             // draft row j = r / G sees keys < kv0 + j + 1; rows past the unit's R see none
             const int kq = key - kv0;  // >= 0 only for draft keys
@@ -623,7 +622,7 @@ int launch_t(const AttnArgs& a, const VerifyParams& p, int max_chunks) {
 }  // namespace
 
 bool verify_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q, bool tree) {
-    if (pool->opts.verify_kernel == YF_VERIFY_SPLITKV) return false;
+    if (pool->opts.verify_kernel != YF_VERIFY_TCGEN05) return false;
     const yf_pool_desc& d = pool->desc;
     const int G = n_q_heads / d.n_kv_heads;
     const int rows = G * max_seqlen_q;
@@ -640,7 +639,7 @@ VerifyPlan plan_verify(const yf_pool* pool, int n_q_heads, int batch, int max_se
     // 16 to 64 key tiles per CTA: enough CTAs for ~8 waves over the SMs, few enough that the
     // per-CTA set-up and the merge stay small against the stream
     long long ct = (units * max_kt + (long long)pool->sm_count * 8 - 1) / ((long long)pool->sm_count * 8);
-    ct = std::max<long long>(16, std::min<long long>(64, ct));
+    ct = std::max<long long>(16, std::min<long long>(kVtMaxChunkTiles, ct));
     v.chunk_tiles = (int)ct;
     v.max_chunks = std::max(1, (max_kt + v.chunk_tiles - 1) / v.chunk_tiles);
     v.ws_bytes = v.max_chunks > 1 ? (size_t)units * v.max_chunks * v.rows * (kVtD + 1) * sizeof(float) : 0;

@@ -1,5 +1,6 @@
-"""The tcgen05 verify kernel (keys as the MMA's M, N = 16 or 32 query rows per kv head) against
-the oracle, and against the split-KV verify kernel on the same inputs."""
+"""The tcgen05 verify kernel (keys as the MMA's M, N = 16 or 32 query rows per kv head; the pool
+option YF_VERIFY_TCGEN05) against the oracle, and against the default split-KV verify kernel on
+the same inputs."""
 import numpy as np
 import pytest
 import torch
@@ -29,6 +30,7 @@ def test_verify_tc_ragged_lengths(yf, oracle, cuda, drafts, P):
     ctx = np.array([drafts, 100, 127, 128, 129, 3000, 9000, 20001])
     wl = W.Workload("vt", 32, 8, 128, ctx=ctx, q_rows=[drafts] * len(ctx), page_size=P, seed=301 + drafts)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=302)
+    pool.set_options(verify_kernel=_abi.YF_VERIFY_TCGEN05)
     q = queries(wl, 303)
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128))
     got = verify(yf, pool, wl, q, cuda)
@@ -37,9 +39,8 @@ def test_verify_tc_ragged_lengths(yf, oracle, cuda, drafts, P):
     assert err <= TOL, err
     again = verify(yf, pool, wl, q, cuda)
     assert np.array_equal(got, again)
-    pool.set_options(verify_kernel=_abi.YF_VERIFY_SPLITKV)
-    alt = verify(yf, pool, wl, q, cuda)
     pool.set_options(verify_kernel=_abi.YF_VERIFY_AUTO)
+    alt = verify(yf, pool, wl, q, cuda)
     assert np.abs(alt - ref).max() <= TOL
     assert pool.status() == 0
     pool.close()
@@ -50,6 +51,7 @@ def test_verify_tc_bad_page_and_short_entries(yf, oracle, cuda):
     committed keys (every key a draft) attend causally among their drafts only."""
     wl = W.Workload("vb", 32, 8, 128, ctx=[4, 300, 1000], q_rows=[4, 4, 4], seed=311)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=312)
+    pool.set_options(verify_kernel=_abi.YF_VERIFY_TCGEN05)
     q = queries(wl, 313)
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128))
     assert np.abs(verify(yf, pool, wl, q, cuda) - ref).max() <= TOL
@@ -72,6 +74,7 @@ def test_verify_tc_tree(yf, oracle, cuda):
     trie = np.concatenate([W.random_trie(rng, 8) for _ in ctx])
     wl = W.Workload("vtt", 32, 8, 128, ctx=ctx, q_rows=[8] * 4, seed=322, trie=trie)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=323)
+    pool.set_options(verify_kernel=_abi.YF_VERIFY_TCGEN05)
     q = queries(wl, 324)
     got = verify(yf, pool, wl, q, cuda, trie=trie)
     ref = oracle.np_attn_tree(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128), trie)
