@@ -49,8 +49,9 @@ def peaks():
 
 def dominant_kernel(config: str) -> str:
     """The kernel that dominates one attention call of the workload."""
-    return {"prefill_chunk": "prefill_tc_kernel", "tree_verify": "splitkv_kernel",
-            "attn_prep": "attn_prep_kernel", "snapshot_records": "records_kernel"}.get(config, "decode_persistent_kernel")
+    return {"prefill_chunk": "prefill_tc_kernel", "tree_verify": "splitkv_kernel", "decode_long": "decode_cluster_kernel",
+            "decode_small": "decode_cluster_kernel", "attn_prep": "attn_prep_kernel",
+            "snapshot_records": "records_kernel"}.get(config, "decode_persistent_kernel")
 
 
 def profile_traffic(config: str):
@@ -135,6 +136,25 @@ class ClockSampler:
 # GPU arm
 
 
+def packed(tensors, dev):
+    """One device buffer holding a step's input tensors back to back (256-byte aligned) and views
+    of it in their shapes and dtypes: the step's inputs then arrive in one host-to-device copy, as
+    an engine stages a step's q / k / v rows and lengths in one pinned buffer."""
+    import torch
+
+    offs, off = [], 0
+    for t in tensors:
+        offs.append(off)
+        off += -(-t.numel() * t.element_size() // 256) * 256
+    buf = torch.zeros(off, dtype=torch.uint8, device=dev)
+    views = []
+    for t, o in zip(tensors, offs):
+        v = buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+        v.copy_(t)
+        views.append(v)
+    return buf, views
+
+
 class Step:
     """One workload resident on one GPU, with pre-bound C-ABI calls for the timed loop."""
 
@@ -179,6 +199,8 @@ class Step:
         self.cu_k = i32(wl.cu_k)
         self.cu_q = i32(wl.cu_q)
         self.start = i32(wl.prefix)
+        self.inputs, (self.q, self.k_new, self.v_new, self.start, self.cu_k) = packed(
+            [self.q, self.k_new, self.v_new, self.start, self.cu_k], self.dev)
         self.trie = None if wl.trie is None else i32(wl.trie)
         self.decode = bool((wl.q_rows == 1).all()) and self.trie is None
         self.max_q = int(wl.q_rows.max())
@@ -302,6 +324,8 @@ class ShardedStep:
         self.out = self.sd.out
         self.start = torch.tensor([n - 1], dtype=torch.int32, device=self.dev)
         self.cu_k = torch.tensor([0, n], dtype=torch.int32, device=self.dev)
+        self.inputs, (self.q, self.k_new, self.v_new, self.start, self.cu_k) = packed(
+            [self.q, self.k_new, self.v_new, self.start, self.cu_k], self.dev)
         self.n = n
         self.scale = yf.default_scale(wl.head_dim)
         self.ws_bytes = self.pool.workspace_size(self.sd.hq, 1, 1, max(n, 1))
@@ -455,17 +479,16 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize()
         attn_ms = sum(a.elapsed_time(b) for a, b in evs) / n_ev / wl.n_layers
 
-        # end to end through the public API with host buffers: H2D of the step's inputs, D2H of
-        # the output, every step
-        pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
-        h_in = [(pin(t), t) for t in (step.q, step.k_new, step.v_new, step.start, step.cu_k)]
+        # end to end through the public API with host buffers: the step's inputs (q, the new K/V
+        # rows, positions, lengths) staged in one pinned buffer and copied in, the output read
+        # back, every step
+        h_in = torch.empty(step.inputs.shape, dtype=torch.uint8, pin_memory=True).copy_(step.inputs.cpu())
         h_out = torch.empty(step.out.shape, dtype=step.out.dtype, pin_memory=True)
-        bytes_in = sum(h.numel() * h.element_size() for h, _ in h_in)
+        bytes_in = h_in.numel()
         bytes_out = h_out.numel() * h_out.element_size()
 
         def e2e_step():
-            for h, d in h_in:
-                d.copy_(h, non_blocking=True)
+            step.inputs.copy_(h_in, non_blocking=True)
             run_step()
             h_out.copy_(step.out, non_blocking=True)
 
