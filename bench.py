@@ -35,6 +35,9 @@ graft.load_package()
 METRIC = "paged int8-KV decode attn tokens/s & KV GB/s (% HBM peak) at 1/2/4/8 B200"
 # attention options of every pool the bench builds (yf_attn_options; --schedule / --launch)
 POOL_OPTIONS = {}
+# how the sharded decode's partials reach every rank: "p2p" (push/combine kernels over NVLink
+# peer memory) or "nccl" (all-gather, then yf_attn_combine)
+TRANSPORT = {"kind": "p2p"}
 SCHEDULES = {"auto": 0, "chunked": 1, "persistent": 2}
 
 
@@ -282,8 +285,9 @@ class Step:
 
 class ShardedStep:
     """decode_long on `world` GPUs: this rank's kv head and key range of the one sequence
-    (qwen36_server_b200.sharding), partial decode -> NCCL all-gather -> LSE combine per step.
-    Strong scaling: every rank works on the same token."""
+    (qwen36_server_b200.sharding), partial decode -> exchange of the partials (peer-memory push
+    or NCCL all-gather) -> LSE combine per step.  Strong scaling: every rank works on the same
+    token."""
 
     def __init__(self, wl, device: int, rank: int, world: int):
         import torch
@@ -302,8 +306,10 @@ class ShardedStep:
         self.shard = sh = S.long_context_plan(world, wl.n_kv_heads, ctx, wl.page_size)[rank]
         n = sh.k1 - sh.k0
         pages = max(1, -(-n // wl.page_size))
+        self.world = world
+        self.transport = TRANSPORT["kind"]
         self.sd = S.ShardedLongDecode(sh, wl.n_q_heads, wl.n_kv_heads, wl.head_dim, pages, wl.page_size,
-                                      wl.group_size, batch=1, device=device)
+                                      wl.group_size, batch=1, device=device, transport=self.transport)
         self.pool = self.sd.pool
         self.pool.set_options(**POOL_OPTIONS)
         gen = torch.Generator(device=self.dev)
@@ -344,9 +350,12 @@ class ShardedStep:
         self.sd.partial(self.q_local, self.cu_k, self.bt, self.scale, max(self.n, 1))
 
     def capture(self):
-        """CUDA graphs of one step (NCCL all-gather included) and of the partial alone, after a
-        warm step has created the NCCL communicator and the workspace."""
+        """CUDA graphs of one step (the exchange included) and of the partial alone, after a
+        warm step has created the NCCL communicator and the workspace.  The ranks meet first:
+        a peer-memory combine waits (bounded) for every rank's push of the same step."""
         torch = self.torch
+        if self.world > 1:
+            torch.distributed.barrier()
         with torch.cuda.stream(self.stream):
             self.run()
         self.stream.synchronize()
@@ -358,13 +367,22 @@ class ShardedStep:
         self.stream.synchronize()
 
     def release(self):
-        """Drops the graphs (the step's holds an NCCL call: gone before the process group)."""
+        """Drops the graphs (the step's may hold an NCCL call: gone before the process group)."""
         self.g_step = self.g_attn = None
 
+    def status(self) -> int:
+        """The pool's device status bits, with the exchange's (a combine wait that ran out)."""
+        st = self.pool.status()
+        if self.sd.peer is not None:
+            st |= self.sd.peer.status()
+        return st
+
     def launches_per_step(self) -> int:
-        """KV write (owner only) + partial decode + one combine per head group (the all-gather
-        is NCCL's kernel, the q slice a torch copy)."""
-        return (1 if self.owner else 0) + 1 + self.shard.n_head_groups
+        """KV write (owner only) + partial decode + the exchange: push + combine kernels (p2p),
+        or one combine per head group (nccl: the all-gather is NCCL's kernel).  The q slice is a
+        torch copy."""
+        ex = 2 if self.transport == "p2p" else self.shard.n_head_groups
+        return (1 if self.owner else 0) + 1 + ex
 
 
 def make_workload(name: str, rank: int, layers: int = 0):
@@ -381,7 +399,7 @@ def partition(wl_full, world: int, rank: int):
     """This rank's share of the workload at N GPUs, and how the job is split:
     - "slots": independent entries bin-packed by context over the GPUs (LPT); the same job at
       every N (strong scaling), no collective on the data path;
-    - "sharded": the one long sequence split by kv head x key range (partials all-gathered);
+    - "sharded": the one long sequence split by kv head x key range (partials exchanged);
     - "replica": a workload with fewer entries than GPUs runs whole on every GPU (weak scaling)."""
     from qwen36_server_b200 import sharding as S
     from qwen36_server_b200 import workloads as W
@@ -451,7 +469,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     if args.no_graph:
         run_step, run_attn = step.run, step.run_attn
     else:
-        step.capture()  # the sharded step's graph holds its NCCL all-gather
+        step.capture()  # the sharded step's graph holds its exchange (push + combine, or NCCL's all-gather)
         run_step, run_attn = step.g_step.replay, step.g_attn.replay
 
     def barrier():
@@ -503,7 +521,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms, attn_ms = t.tolist()
-    status = step.pool.status()
+    status = step.status() if sharded else step.pool.status()
 
     if mode == "replica":
         tokens = step.T * world
@@ -531,7 +549,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
         parallelism = (f"slots LPT-packed by context over {world} GPUs (same {wl_full.batch} slots at every N, "
                        "no collective on the data path)")
     elif sharded:
-        parallelism = f"kv-head x sequence sharded x{world} (partials all-gathered over NCCL, LSE combine)"
+        how = ("partials pushed over NVLink peer memory, LSE combine" if TRANSPORT["kind"] == "p2p"
+               else "partials all-gathered over NCCL, LSE combine")
+        parallelism = f"kv-head x sequence sharded x{world} ({how})"
     elif mode == "replica":
         parallelism = f"replicas x{world} (fewer entries than GPUs: each GPU runs the whole workload)"
     else:
@@ -561,7 +581,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
             else "pool fits in L2 (small workload)",
             "parallelism": parallelism,
             "launch": "direct C-ABI calls" if args.no_graph else (
-                "CUDA graph replay of the step (partial, NCCL all-gather, combine)" if sharded
+                "CUDA graph replay of the step (partial, exchange of the partials, combine)" if sharded
                 else "CUDA graph replay of the step's C-ABI calls"),
             "timing": f"median of {passes} passes of {args.steps} steps (>= {args.min_seconds} s of GPU time), "
                       "CUDA events on the launching stream, max over ranks",
@@ -593,8 +613,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
 
 
 def long_sharded_leg(args, rank: int, world: int, local_rank: int) -> dict:
-    """The 131072-key decode at the same N: kv head x key-range shards, partial decode, NCCL
-    all-gather of the packed partials, LSE combine; replayed as one CUDA graph per rank."""
+    """The 131072-key decode at the same N: kv head x key-range shards, partial decode, exchange
+    of the packed partials (peer-memory push, or NCCL all-gather), LSE combine; replayed as one
+    CUDA graph per rank."""
     import torch
     import torch.distributed as dist
 
@@ -623,16 +644,20 @@ def long_sharded_leg(args, rank: int, world: int, local_rank: int) -> dict:
     t = torch.tensor([ms, part_ms], dtype=torch.float64, device=step.dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, part_ms = t.tolist()
-    status = step.pool.status()
+    status = step.status()
     step.release()
     hbm, _, _ = peaks()
     shard_bytes = wl.kv_bytes(1) // world
+    if step.transport == "p2p":
+        limiter = ("the peer-memory push of the packed partials (a few KB stored over NVLink) and the "
+                   "combine's wait for every rank's flag, on top of the shard's partial decode")
+    else:
+        limiter = ("the NCCL all-gather of the packed partials plus the combine launch (latency, a few KB "
+                   "moved) on top of the shard's partial decode")
     return {"workload": describe(wl), "ms_per_step": ms, "tokens_per_s": 1.0 / (ms * 1e-3),
             "partial_ms": part_ms, "partial_hbm_frac": shard_bytes / (part_ms * 1e-3) / 1e9 / hbm,
-            "exchange_and_combine_ms": ms - part_ms, "passes": passes,
-            "limiter": "the NCCL all-gather of the packed partials plus the combine launch (latency, a few KB "
-                       "moved) on top of the shard's partial decode",
-            "parallelism": f"kv-head x sequence sharded x{world}", "device_status": status}
+            "exchange_and_combine_ms": ms - part_ms, "passes": passes, "transport": step.transport,
+            "limiter": limiter, "parallelism": f"kv-head x sequence sharded x{world}", "device_status": status}
 
 
 def describe(wl) -> str:
@@ -1065,11 +1090,14 @@ def main():
                     help="verify blocks on the split-KV kernel (auto) or the tcgen05 kernel (yf_attn_options.verify_kernel)")
     ap.add_argument("--cooperative", action="store_true",
                     help="launch the persistent decode cooperatively (yf_attn_options.launch)")
+    ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1 sharded decode: partials pushed over NVLink peer memory (p2p) or all-gathered by NCCL")
     ap.add_argument("--layers", type=int, default=0,
                     help="mtp_verify only: stack this many layers instead of 36 (one launch per layer keeps "
                          "its shape; for profiling a launch with a few GB resident, not a bench line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    TRANSPORT["kind"] = args.transport
     POOL_OPTIONS.update(schedule=SCHEDULES[args.schedule], launch=1 if args.cooperative else 0,
                         verify_kernel=1 if args.verify_kernel == "tcgen05" else 0)
     rank = int(os.environ.get("RANK", "0"))

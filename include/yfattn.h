@@ -334,6 +334,41 @@ YF_API int yf_attn_combine(const float* d_o_parts, int64_t o_part_stride, const 
                            int64_t lse_part_stride, int32_t n_parts, int32_t rows, int32_t head_dim, void* d_out,
                            void* stream);
 
+/* ---- partial exchange over NVLink peer memory ---------------------------------
+ * Replaces, for the kv-head x key-range sharded long decode, the all-gather of the packed
+ * partials plus yf_attn_combine (both stand in for flash_fwd_splitkv_combine_kernel across
+ * GPUs; same citation): every rank owns an exchange area in its own HBM that the other ranks
+ * map once (CUDA IPC, plain peer mappings).  A step is yf_exchange_push (this rank's partial
+ * stored into slot `rank` of every rank's area, then a release flag in each) followed, later
+ * in the same stream, by yf_exchange_combine (a bounded acquire wait on every rank's flag in
+ * the own area, then the LSE merge in place into f16 output).  The reference has no
+ * counterpart: its decode runs on one GPU.  Each rank's partial is slot_floats f32, 16-byte
+ * aligned: O f32 [rows][head_dim] at offset 0 and lse f32 [rows] at lse_offset.  A wait that
+ * runs past the limit (default 1 s) writes nothing and sets YF_DEV_TIMEOUT in the exchange's
+ * status. */
+typedef struct yf_exchange yf_exchange;
+#define YF_EXCHANGE_HANDLE_BYTES 64
+YF_API int yf_exchange_create(int32_t device, int32_t rank, int32_t world, int64_t slot_floats,
+                              yf_exchange** out);
+YF_API int yf_exchange_destroy(yf_exchange* ex);
+/* The IPC handle (YF_EXCHANGE_HANDLE_BYTES bytes) of this rank's area, to hand to the others. */
+YF_API int yf_exchange_handle(const yf_exchange* ex, void* out_handle);
+/* Maps rank `peer`'s area (its handle) into this process. */
+YF_API int yf_exchange_open_peer(yf_exchange* ex, int32_t peer, const void* handle);
+/* Same-process, same-device peer (tests that emulate ranks on one GPU). */
+YF_API int yf_exchange_attach(yf_exchange* ex, int32_t peer, const yf_exchange* other);
+/* 0 restores the default limit of one second. */
+YF_API int yf_exchange_set_wait_limit(yf_exchange* ex, uint32_t wait_limit_us);
+YF_API int yf_exchange_push(yf_exchange* ex, const float* d_partial, void* stream);
+/* Ranks s * n_head_groups + g (s < n_seq) hold head group g's key ranges; row i = b * hq + j of
+ * a partial is output row b * n_q_heads + g * hq + j, n_q_heads = hq * n_head_groups; d_out f16
+ * [rows / hq][n_q_heads][head_dim], 8-byte aligned. */
+YF_API int yf_exchange_combine(yf_exchange* ex, int32_t n_head_groups, int32_t n_seq, int32_t rows, int32_t hq,
+                               int32_t n_q_heads, int32_t head_dim, int64_t lse_offset, void* d_out,
+                               void* stream);
+/* Synchronizes the device, reads the status bits (YF_DEV_TIMEOUT) and clears them if asked. */
+YF_API int yf_exchange_status(yf_exchange* ex, uint32_t* out_bits, int clear);
+
 /* ---- prefix snapshot export / restore ----------------------------------------
  * Byte copies of whole pages (all KV heads, one layer) with their scales and
  * no requantization, as StateSnapshot::to_host / to_device do for the int8

@@ -42,6 +42,7 @@ YF_POOL_COUNTERS = 65536 + 4096
 YF_REC_REJECTED = 0
 YF_REC_RESTORED = 1
 YF_REC_MISMATCH = 2
+YF_EXCHANGE_HANDLE_BYTES = 64
 
 ERROR_NAMES = {
     YF_E_INVALID: "YF_E_INVALID", YF_E_UNSUPPORTED: "YF_E_UNSUPPORTED", YF_E_NOMEM: "YF_E_NOMEM",
@@ -116,6 +117,15 @@ SIGNATURES = {
     "yf_pool_record_bytes": (_sz, [_vp]),
     "yf_pool_export_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "yf_pool_import_records": (_ci, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "yf_exchange_create": (_ci, [_i32, _i32, _i32, ctypes.c_int64, ctypes.POINTER(_vp)]),
+    "yf_exchange_destroy": (_ci, [_vp]),
+    "yf_exchange_handle": (_ci, [_vp, _vp]),
+    "yf_exchange_open_peer": (_ci, [_vp, _i32, _vp]),
+    "yf_exchange_attach": (_ci, [_vp, _i32, _vp]),
+    "yf_exchange_set_wait_limit": (_ci, [_vp, _u32]),
+    "yf_exchange_push": (_ci, [_vp, _vp, _vp]),
+    "yf_exchange_combine": (_ci, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_int64, _vp, _vp]),
+    "yf_exchange_status": (_ci, [_vp, ctypes.POINTER(_u32), _ci]),
     "yf_pool_export_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "yf_pool_restore_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
 }

@@ -15,15 +15,24 @@ NVLink), and yf_attn_combine merges the key ranges of each head group in place i
 gathered buffer.  This replaces the reference's single-GPU split-KV + combine
 (flash_fwd_splitkv_combine_kernel, docs/plans/2026-09-16-prefil-parity-fa2-and-mmq.md:104-107)
 for a sequence spread over GPUs; partitions with independent slots need no such exchange.
+
+The "p2p" transport (PeerExchange) replaces that all-gather and combine with two kernels of
+libyfattn.so over NVLink peer memory: a push that stores this rank's partial straight into
+every rank's exchange area and raises a release flag there, and a combine that waits (bounded)
+for every rank's flag in its own area and merges in place.  No collective library call remains
+on the data path; the areas are mapped once with CUDA IPC when the decode is built.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import List
 
 import torch
 
+from . import _abi
 from . import paged_attn as pa
+from ._abi import call, lib
 
 
 def lpt_partition(costs, n_bins: int) -> List[List[int]]:
@@ -107,6 +116,98 @@ def gather_packed(local: torch.Tensor, gathered: torch.Tensor, world: int, group
         gathered.copy_(local)
 
 
+class PeerExchange:
+    """One rank's end of the NVLink partial exchange (yf_exchange_* of libyfattn.so).
+
+    Every rank's partial is ``slot_floats`` f32 (packed_floats: O then lse).  ``connect`` maps
+    all ranks' areas into each other over a process group (their IPC handles travel through
+    one all-gather at set-up); ``emulated`` builds ``world`` exchanges on one GPU attached to
+    each other, for tests that run every rank's push and then every rank's combine."""
+
+    def __init__(self, rank: int, world: int, slot_floats: int, device: int = 0, wait_limit_us: int = 0):
+        if slot_floats % 4:
+            raise ValueError("slot_floats must be a multiple of 4")
+        self.rank, self.world, self.slot_floats = rank, world, slot_floats
+        self.device = torch.device("cuda", device)
+        h = ctypes.c_void_p()
+        call("yf_exchange_create", device, rank, world, slot_floats, ctypes.byref(h))
+        self._h = h
+        if wait_limit_us:
+            call("yf_exchange_set_wait_limit", self._h, wait_limit_us)
+
+    def handle(self) -> bytes:
+        buf = (ctypes.c_uint8 * _abi.YF_EXCHANGE_HANDLE_BYTES)()
+        call("yf_exchange_handle", self._h, buf)
+        return bytes(buf)
+
+    def open_peer(self, peer: int, handle: bytes) -> None:
+        buf = (ctypes.c_uint8 * _abi.YF_EXCHANGE_HANDLE_BYTES).from_buffer_copy(handle)
+        call("yf_exchange_open_peer", self._h, peer, buf)
+
+    def attach(self, peer: int, other: "PeerExchange") -> None:
+        call("yf_exchange_attach", self._h, peer, other._h)
+
+    def set_wait_limit(self, wait_limit_us: int) -> None:
+        call("yf_exchange_set_wait_limit", self._h, wait_limit_us)
+
+    def push(self, local: torch.Tensor) -> None:
+        if local.dtype != torch.float32 or local.numel() < self.slot_floats or not local.is_contiguous():
+            raise ValueError("local partial must be contiguous f32 of at least slot_floats")
+        call("yf_exchange_push", self._h, ctypes.c_void_p(local.data_ptr()), pa._stream(self.device))
+
+    def combine(self, out: torch.Tensor, n_head_groups: int, n_seq: int, rows: int, hq: int, n_q_heads: int,
+                head_dim: int, lse_offset: int) -> torch.Tensor:
+        if out.dtype != torch.float16 or out.numel() < rows // hq * n_q_heads * head_dim:
+            raise ValueError("out must be f16 [rows / hq, n_q_heads, head_dim]")
+        call("yf_exchange_combine", self._h, n_head_groups, n_seq, rows, hq, n_q_heads, head_dim, lse_offset,
+             ctypes.c_void_p(out.data_ptr()), pa._stream(self.device))
+        return out
+
+    def status(self, clear: bool = False) -> int:
+        v = ctypes.c_uint32()
+        call("yf_exchange_status", self._h, ctypes.byref(v), int(clear))
+        return v.value
+
+    @classmethod
+    def connect(cls, rank: int, world: int, slot_floats: int, device: int = 0, group=None,
+                wait_limit_us: int = 0) -> "PeerExchange":
+        """Creates this rank's exchange and maps every other rank's area (collective call)."""
+        ex = cls(rank, world, slot_floats, device, wait_limit_us)
+        if world > 1:
+            nb = _abi.YF_EXCHANGE_HANDLE_BYTES
+            backend = torch.distributed.get_backend(group)
+            where = ex.device if backend == "nccl" else torch.device("cpu")
+            mine = torch.tensor(list(ex.handle()), dtype=torch.uint8, device=where)
+            every = torch.empty(world * nb, dtype=torch.uint8, device=where)
+            torch.distributed.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy().tobytes()
+            for r in range(world):
+                if r != rank:
+                    ex.open_peer(r, every[r * nb:(r + 1) * nb])
+            torch.distributed.barrier(group=group)
+        return ex
+
+    @classmethod
+    def emulated(cls, world: int, slot_floats: int, device: int = 0, wait_limit_us: int = 0):
+        xs = [cls(r, world, slot_floats, device, wait_limit_us) for r in range(world)]
+        for a in xs:
+            for b in xs:
+                if a is not b:
+                    a.attach(b.rank, b)
+        return xs
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().yf_exchange_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ShardedLongDecode:
     """One rank's share of a sharded decode (batch entries, all of one length split alike).
 
@@ -115,7 +216,7 @@ class ShardedLongDecode:
 
     def __init__(self, shard: LongShard, n_q_heads: int, n_kv_heads: int, head_dim: int, n_pages: int,
                  page_size: int = 16, group_size: int = 32, batch: int = 1, device: int = 0,
-                 process_group=None):
+                 process_group=None, transport: str = "nccl", peer_exchange: "PeerExchange" = None):
         if n_q_heads % n_kv_heads:
             raise ValueError("n_q_heads must be a multiple of n_kv_heads")
         self.shard, self.batch, self.D = shard, batch, head_dim
@@ -137,6 +238,14 @@ class ShardedLongDecode:
         # workspace for the shard's whole key range, so a context that grows step by step never
         # outgrows it (partial() still re-checks against the call's own max_seqlen_k)
         self.ws = self._workspace(max(shard.k1 - shard.k0, 1))
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport {transport!r}: 'nccl' or 'p2p'")
+        self.transport = transport
+        self.peer = peer_exchange
+        if transport == "p2p" and self.peer is None:
+            self.peer = PeerExchange.connect(shard.rank, shard.world, blk, device, process_group)
+        if self.peer is not None and self.peer.slot_floats != blk:
+            raise ValueError("peer exchange slot size differs from the packed partial")
 
     def q_slice(self, q: torch.Tensor) -> torch.Tensor:
         """This rank's q heads of a full q [B, Hq, D]."""
@@ -154,9 +263,16 @@ class ShardedLongDecode:
                                          o_part=self.o_part, lse_part=self.lse_part, workspace=self.ws)
 
     def exchange(self):
-        gather_packed(self.local, self.gathered, self.shard.world, self.group)
+        if self.transport == "p2p":
+            self.peer.push(self.local)
+        else:
+            gather_packed(self.local, self.gathered, self.shard.world, self.group)
 
     def combine(self) -> torch.Tensor:
+        if self.transport == "p2p":
+            rows = self.batch * self.hq
+            return self.peer.combine(self.out, self.shard.n_head_groups, self.shard.n_seq, rows, self.hq, self.Hq,
+                                     self.D, rows * self.D)
         flat = self.out.view(self.batch * self.Hq, self.D)
         for g, (oo, lo, stride, n_parts, rows) in enumerate(combine_views(self.shard, self.batch, self.hq, self.D)):
             # one head group: its rows are contiguous in the output when B == 1 or there is one group
@@ -169,7 +285,7 @@ class ShardedLongDecode:
         return self.out
 
     def step(self, q_local: torch.Tensor, cu_k, table, scale: float, max_seqlen_k: int) -> torch.Tensor:
-        """Partial over this shard, all-gather, combine: the full f16 output [B, Hq, D] on every rank."""
+        """Partial over this shard, exchange, combine: the full f16 output [B, Hq, D] on every rank."""
         self.partial(q_local, cu_k, table, scale, max_seqlen_k)
         self.exchange()
         return self.combine()

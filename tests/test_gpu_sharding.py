@@ -69,10 +69,13 @@ def test_decode_partial_matches_oracle(yf, oracle, cuda):
     pool.close()
 
 
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_sharded_long_decode_emulated(yf, oracle, cuda, world):
+def test_sharded_long_decode_emulated(yf, oracle, cuda, world, transport):
     """The decode_long shape (Hq 16 x D 256, Hkv 2) over 20000 keys split as world ranks would
-    split it: every rank's combined output equals the unsharded decode and the oracle."""
+    split it: every rank's combined output equals the unsharded decode and the oracle.  "nccl"
+    stands the all-gather in with copies; "p2p" runs the peer exchange's push of every rank,
+    then every rank's combine."""
     ctx, Hq, H, D = 20000, 16, 2, 256
     rng = np.random.default_rng(90 + world)
     k = W.kv_rows_np(rng, ctx, H, D, 0.0)
@@ -94,11 +97,14 @@ def test_sharded_long_decode_emulated(yf, oracle, cuda, world):
     ref = oracle.c_attn(desc, img, 0, q, np.array([0, 1]), np.array([0, ctx]), wl.block_table, scale)
 
     plan = S.long_context_plan(world, H, ctx)
+    xs = S.PeerExchange.emulated(world, S.packed_floats(1, Hq // plan[0].n_head_groups, D)) \
+        if transport == "p2p" else [None] * world
     ranks = []
     for sh in plan:
         n = sh.k1 - sh.k0
         pages = max(1, -(-n // 16))
-        r = S.ShardedLongDecode(sh, Hq, H, D, n_pages=pages, device=0)
+        r = S.ShardedLongDecode(sh, Hq, H, D, n_pages=pages, device=0, transport=transport,
+                                peer_exchange=xs[sh.rank])
         bt = torch.arange(pages, dtype=torch.int32, device=cuda).view(1, pages)
         if n:
             ks = kd[sh.k0:sh.k1, sh.kv_head0:sh.kv_head0 + sh.kv_heads].contiguous()
@@ -106,13 +112,22 @@ def test_sharded_long_decode_emulated(yf, oracle, cuda, world):
             yf.launch_append_multi(r.pool, 0, ks, vs, [0, n], [0], bt)
         r.partial(r.q_slice(qd), [0, n], bt, scale, max_seqlen_k=max(n, 1))
         ranks.append(r)
-    gathered = torch.cat([r.local for r in ranks])
+    if transport == "p2p":
+        for r in ranks:
+            r.exchange()
+    else:
+        gathered = torch.cat([r.local for r in ranks])
+        for r in ranks:
+            r.gathered.copy_(gathered)
     for r in ranks:
-        r.gathered.copy_(gathered)
         got = r.combine().float().cpu().numpy()
         assert np.abs(got - ref_gpu).max() <= TOL, r.shard
         assert np.abs(got - ref).max() <= TOL, r.shard
         assert r.pool.status() == 0
     for r in ranks:
         r.pool.close()
+    for x in xs:
+        if x is not None:
+            assert x.status() == 0
+            x.close()
     full_pool.close()
