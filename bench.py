@@ -332,6 +332,11 @@ class ShardedStep:
         self.cu_k = torch.tensor([0, n], dtype=torch.int32, device=self.dev)
         self.inputs, (self.q, self.k_new, self.v_new, self.start, self.cu_k) = packed(
             [self.q, self.k_new, self.v_new, self.start, self.cu_k], self.dev)
+        # one entry: this rank's q heads are a contiguous run of q, read in place
+        h0 = sh.kv_head0 * self.sd.G
+        self.q_view = self.q[:, h0:h0 + self.sd.hq] if self.q.shape[0] == 1 else None
+        if self.q_view is not None:
+            self.q_local = self.q_view
         self.n = n
         self.scale = yf.default_scale(wl.head_dim)
         self.ws_bytes = self.pool.workspace_size(self.sd.hq, 1, 1, max(n, 1))
@@ -342,8 +347,9 @@ class ShardedStep:
     def run(self):
         if self.owner:
             self.yf.kv_append_paged(self.pool, 0, self.k_new, self.v_new, self.start, self.bt)
-        h0 = self.shard.kv_head0 * self.sd.G
-        self.q_local.copy_(self.q[:, h0:h0 + self.sd.hq])
+        if self.q_view is None:  # several entries: this rank's heads are strided in q
+            h0 = self.shard.kv_head0 * self.sd.G
+            self.q_local.copy_(self.q[:, h0:h0 + self.sd.hq])
         self.sd.step(self.q_local, self.cu_k, self.bt, self.scale, max(self.n, 1))
 
     def run_attn(self):
@@ -378,9 +384,11 @@ class ShardedStep:
         return st
 
     def launches_per_step(self) -> int:
-        """KV write (owner only) + partial decode + the exchange: push + combine kernels (p2p),
-        or one combine per head group (nccl: the all-gather is NCCL's kernel).  The q slice is a
-        torch copy."""
+        """KV write (owner only) + the shard's decode with the exchange fused in (p2p: one
+        launch), or partial decode + one combine per head group (nccl: the all-gather is NCCL's
+        kernel).  A q slice of several entries is a torch copy."""
+        if self.transport == "p2p" and self.sd.fused:
+            return (1 if self.owner else 0) + 1
         ex = 2 if self.transport == "p2p" else self.shard.n_head_groups
         return (1 if self.owner else 0) + 1 + ex
 

@@ -366,6 +366,20 @@ YF_API int yf_exchange_push(yf_exchange* ex, const float* d_partial, void* strea
 YF_API int yf_exchange_combine(yf_exchange* ex, int32_t n_head_groups, int32_t n_seq, int32_t rows, int32_t hq,
                                int32_t n_q_heads, int32_t head_dim, int64_t lse_offset, void* d_out,
                                void* stream);
+/* One whole step of the sharded decode in one launch where the cluster decode schedule takes it:
+ * this rank's partial over its pool (as yf_attn_decode_partial; q [batch][hq][head_dim], the
+ * workspace of yf_attn_workspace_size(pool, hq, batch, 1, max_seqlen_k)) is stored straight into
+ * every rank's area as (value, step) words, and every CTA that stored a slice polls the same rows
+ * of every rank's partial in its own area (bounded) and merges them into d_out (the arithmetic of
+ * yf_exchange_combine; 16-byte aligned).  Other
+ * schedules run decode_partial, push and combine (three launches, same result).  The slot must
+ * hold batch * hq * (head_dim + 1) floats.  For ranks on separate devices: an exchange with
+ * attached same-device peers returns YF_E_UNSUPPORTED (those ranks would wait on one another). */
+YF_API int yf_exchange_decode(yf_exchange* ex, yf_pool* pool, int32_t layer, const void* d_q, int32_t hq,
+                              const uint32_t* d_cu_k, const uint32_t* d_block_table, int32_t max_blocks,
+                              int32_t batch, int32_t max_seqlen_k, float scale, int32_t n_head_groups, int32_t n_seq,
+                              int32_t n_q_heads, void* d_out, void* d_workspace, size_t workspace_bytes,
+                              void* stream);
 /* Synchronizes the device, reads the status bits (YF_DEV_TIMEOUT) and clears them if asked. */
 YF_API int yf_exchange_status(yf_exchange* ex, uint32_t* out_bits, int clear);
 

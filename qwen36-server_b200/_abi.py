@@ -125,6 +125,8 @@ SIGNATURES = {
     "yf_exchange_set_wait_limit": (_ci, [_vp, _u32]),
     "yf_exchange_push": (_ci, [_vp, _vp, _vp]),
     "yf_exchange_combine": (_ci, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_int64, _vp, _vp]),
+    "yf_exchange_decode": (_ci, [_vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _vp,
+                                 _vp, _sz, _vp]),
     "yf_exchange_status": (_ci, [_vp, ctypes.POINTER(_u32), _ci]),
     "yf_pool_export_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "yf_pool_restore_pages": (_ci, [_vp, _i32, _i32, _vp, _vp, _vp]),

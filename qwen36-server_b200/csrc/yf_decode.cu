@@ -38,6 +38,7 @@
 
 #include "yf_device.cuh"
 #include "yf_internal.h"
+#include "yf_xchg.cuh"
 
 namespace yf {
 
@@ -90,6 +91,7 @@ struct SplitParams {
     uint32_t* status;
     const int2* trie;    // tree verify: inclusive subtree range of every draft row, or null
     uint64_t wait_ns;    // bound of every wait (copies, merge arrivals)
+    XFuse x;             // fused partial exchange (cluster schedule), x.peers null when off
 };
 
 // Tree verify: the draft rows of an entry are the nodes of a token trie in depth-first order;
@@ -153,6 +155,94 @@ __device__ __forceinline__ void store_row4(const SplitParams& p, const UnitGeom&
         pk.y = pack_h2(v.z, v.w);
         *reinterpret_cast<uint2*>(p.out + off + d4) = pk;
     }
+}
+
+// Final output of a cluster-decode row slice: store_row4, or with the fused exchange on, the
+// f32 O and natural-log lse as (value, xstep) words into slot `rank` of word buffer xstep & 1 of
+// every rank's area (the partial layout of part_o / part_lse, lse rows at x.lse_off).
+__device__ __forceinline__ void store_out4(const SplitParams& p, const UnitGeom& u, int h, int row, int d4, int D,
+                                           float4 v, float lse2, uint32_t xstep) {
+    if (!p.x.peers) {
+        store_row4(p, u, h, row, d4, D, v, lse2);
+        return;
+    }
+    const size_t off = row_offset(p, u, h, row, D);
+    const unsigned long long lse = ll_word(lse2 * 0.6931471805599453f, xstep);
+    const unsigned long long w0 = ll_word(v.x, xstep), w1 = ll_word(v.y, xstep), w2 = ll_word(v.z, xstep),
+                             w3 = ll_word(v.w, xstep);
+    const long long slot0 = ((long long)(xstep & 1u) * p.x.world + p.x.rank) * p.x.slot_floats;
+    for (int k = 0; k < p.x.world; ++k) {
+        unsigned long long* wd = reinterpret_cast<unsigned long long*>(p.x.peers[k] + p.x.words_off) + slot0;
+        st_ll2(wd + off + d4, w0, w1);
+        st_ll2(wd + off + d4 + 2, w2, w3);
+        if (d4 == 0) st_ll1(wd + p.x.lse_off + off / D, lse);
+    }
+}
+
+// The fused exchange's merge, by the CTA that stored output row `row` (of unit u) of this rank's
+// partial: the same partial row of every rank arrives in the own area's word buffer xstep & 1
+// (polled, bounded by x.wait_ns); head group g's output row merges ranks s * n_hg + g, s < n_seq,
+// with xmerge4's arithmetic.  One thread per (head group, float4 column).  A wait that runs out
+// sets YF_DEV_TIMEOUT in the area's status word and leaves the element unwritten.
+template <int D>
+__device__ __forceinline__ void exchange_merge_row(const SplitParams& p, const UnitGeom& u, int h, int row,
+                                                   uint32_t xstep) {
+    const XFuse& x = p.x;
+    constexpr int d4n = D / 4;
+    const size_t pr = row_offset(p, u, h, row, D) / D;  // partial row
+    const unsigned long long* wd = reinterpret_cast<const unsigned long long*>(x.local + x.words_off) +
+                                   (long long)(xstep & 1u) * x.world * x.slot_floats;
+    const uint64_t t0 = globaltimer_ns();
+    for (int e = threadIdx.x; e < x.n_hg * d4n; e += kThreads) {
+        const int g = e / d4n, c = e % d4n;
+        float lv[kXMaxSeq];
+        bool ok = true;
+        float M = -INFINITY;
+        for (int s = 0; s < x.n_seq && ok; ++s) {
+            ok = ll_wait1(wd + (long long)(s * x.n_hg + g) * x.slot_floats + x.lse_off + pr, xstep, t0, x.wait_ns, lv[s]);
+            M = fmaxf(M, lv[s]);
+        }
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < x.n_seq && ok; ++s) {
+            float4 v;
+            const unsigned long long* src = wd + (long long)(s * x.n_hg + g) * x.slot_floats + pr * D + 4 * c;
+            ok = ll_wait2(src, xstep, t0, x.wait_ns, v.x, v.y) && ll_wait2(src + 2, xstep, t0, x.wait_ns, v.z, v.w);
+            if (!ok || M == -INFINITY || lv[s] == -INFINITY) continue;
+            const float w = fast_exp2((lv[s] - M) * 1.4426950408889634f);
+            L += w;
+            acc.x = fmaf(w, v.x, acc.x);
+            acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z);
+            acc.w = fmaf(w, v.w, acc.w);
+        }
+        if (!ok) {
+            atomicOr(xmeta(x.local, x.flags_off) + x.world + 1, YF_DEV_TIMEOUT);
+            continue;
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        const int b = (int)(pr / x.hq), j = (int)(pr % x.hq);
+        uint2 pk;
+        pk.x = pack_h2(acc.x * inv, acc.y * inv);
+        pk.y = pack_h2(acc.z * inv, acc.w * inv);
+        reinterpret_cast<uint2*>(x.out + ((size_t)b * x.n_q_heads + (size_t)g * x.hq + j) * D)[c] = pk;
+    }
+}
+
+// After this CTA's slice stores (all threads): merges each live row of slice r and records the
+// slice's step.
+template <int D, int RPC, int CL>
+__device__ __forceinline__ void exchange_finish(const SplitParams& p, const UnitGeom& u, int h, int r, int si,
+                                                uint32_t xstep) {
+    constexpr int RS = RPC / CL;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < RS; ++i) {
+        const int row = u.row_begin + r * RS + i;
+        if (row < u.rows_total) exchange_merge_row<D>(p, u, h, row, xstep);
+    }
+    if (threadIdx.x == 0)
+        reinterpret_cast<uint32_t*>(p.x.local + p.x.sstep_off)[si] = xstep;  // this slice's step, for the next call
 }
 
 // mma.sync m16n8k16 f16 x f16 -> f32, D = A B + C (C may differ from D).
@@ -1080,8 +1170,85 @@ constexpr int cluster_part_off() {  // the CTA partial, after the 4-warp stash i
     return ((2 * kWarps * 8 * 4 + kWarps * 8 * (D + 4) * 4) + 127) / 128 * 128;
 }
 
+// The last arrival's merge of slice r (RPC / CL rows) over the unit's n cluster partials, workspace
+// items item0 .. item0 + n - 1.  Weights first: warp j < RS takes row j's n lse values, their max
+// and w_k = 2^(lse_k - max) (0 for a part without keys) into shared memory, with their sum reduced
+// in a fixed lane order.  Then every thread adds w_k o_k of its column over parts k = ph, ph + TPC,
+// ... (TPC threads per column), with the loads of an unrolled run of parts in flight together,
+// and the TPC shares are added in phase order.  `area` is the CTA's stage area (free again once
+// the cluster's reads of this CTA's partial are over).
+template <int D, int RPC, int CL>
+__device__ __forceinline__ void last_merge(const SplitParams& p, const UnitGeom& u, int h, int r, int n,
+                                           size_t item0, uint8_t* area, uint32_t xstep) {
+    constexpr int C4 = D / 4;               // float4 columns of a row
+    constexpr int SLICE = RPC * C4 / CL;    // float4 columns of a slice
+    constexpr int RS = RPC / CL;            // rows of a slice
+    constexpr int TPC = kThreads / SLICE;   // threads per column
+    static_assert(RPC % CL == 0 && RS <= kWarps && kThreads % SLICE == 0, "slice geometry");
+    float* wts = reinterpret_cast<float*>(area);                 // [n][RS]
+    float* rowm = wts + kClusterMaxParts * RS;                   // [RS] max lse
+    float* rowl = rowm + 4;                                      // [RS] sum of weights
+    float4* share = reinterpret_cast<float4*>(rowl + 4);         // [kThreads]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = r * RS;
+    if (warp < RS) {
+        float M = -INFINITY;
+        for (int k = lane; k < n; k += 32) {
+            const float lv = __ldcg(p.ws_lse + (item0 + k) * RPC + row0 + warp);
+            wts[k * RS + warp] = lv;
+            M = fmaxf(M, lv);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.f;
+        for (int k = lane; k < n; k += 32) {
+            const float lv = wts[k * RS + warp];
+            const float w = lv == -INFINITY ? 0.f : fast_exp2(lv - M);
+            wts[k * RS + warp] = w;
+            L += w;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (lane == 0) {
+            rowm[warp] = M;
+            rowl[warp] = L;
+        }
+    }
+    __syncthreads();
+    const int c = threadIdx.x % SLICE, ph = threadIdx.x / SLICE;
+    const int col = r * SLICE + c, row = col / C4, d4 = (col % C4) * 4, rr = row - row0;
+    const float4* src = reinterpret_cast<const float4*>(p.ws_o) + (item0 * RPC + row) * C4 + col % C4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int k = ph; k < n; k += TPC) {
+        const float w = wts[k * RS + rr];
+        const float4 v = __ldcg(src + (size_t)k * RPC * C4);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+    }
+    if constexpr (TPC > 1) {
+        share[threadIdx.x] = acc;
+        __syncthreads();
+    }
+    if (ph == 0 && u.row_begin + row < u.rows_total) {
+#pragma unroll
+        for (int q = 1; q < TPC; ++q) {
+            const float4 v = share[q * SLICE + c];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float L = rowl[rr], inv = L > 0.f ? 1.f / L : 0.f;
+        store_out4(p, u, h, u.row_begin + row, d4, D, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv),
+                   L > 0.f ? rowm[rr] + __log2f(L) : -INFINITY, xstep);
+    }
+}
+
 template <int D, int NB, int TPP, int STAGES>
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads, 3)
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads, 2)  // 2 per SM: kClusterSmemFloor
     decode_cluster_kernel(const SplitParams p) {
     constexpr int NT = 1, RPC = 8, CL = kClusterCtas;
     constexpr int TB = 32 * D + 64 * NB;
@@ -1165,12 +1332,16 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads,
     }
     cluster_barrier();  // no CTA leaves, or reuses its shared memory, while a peer still reads it
     const bool live_row = threadIdx.x < SLICE && u.row_begin + row < u.rows_total;
+    // fused exchange: this slice's step (its previous call's + 1; only this CTA role touches it)
+    const int xsi = uidx * CL + r;
+    const uint32_t xstep = p.x.peers ? reinterpret_cast<const uint32_t*>(p.x.local + p.x.sstep_off)[xsi] + 1u : 0u;
     if (n_u == 1) {
         if (live_row) {
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
-                       l > 0.f ? m + __log2f(l) : -INFINITY);
+            store_out4(p, u, h, u.row_begin + row, d4, D, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
+                       l > 0.f ? m + __log2f(l) : -INFINITY, xstep);
         }
+        if (p.x.peers) exchange_finish<D, RPC, CL>(p, u, h, r, xsi, xstep);
         return;
     }
     // this cluster's partial of slice r, then the slice's arrival
@@ -1183,30 +1354,9 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads,
     }
     uint32_t* ctr = &p.counters[(size_t)uidx * CL + r];
     if (!arrive_last(ctr, n_u, &s_last)) return;
-    if (live_row) {
-        float m2 = -INFINITY, l2 = 0.f;
-        float4 o2 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k0 = 0; k0 < n_u; k0 += 16) {
-            float lv[16];
-            float4 ov[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                lv[j] = -INFINITY;
-                ov[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k0 + j < n_u) {
-                    const size_t it = (size_t)uidx * cpu + k0 + j;
-                    lv[j] = __ldcg(p.ws_lse + it * RPC + row);
-                    ov[j] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (it * RPC + row) * D + d4));
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) merge_in(lv[j], ov[j], m2, l2, o2);
-        }
-        const float inv = l2 > 0.f ? 1.f / l2 : 0.f;
-        store_row4(p, u, h, u.row_begin + row, d4, D, make_float4(o2.x * inv, o2.y * inv, o2.z * inv, o2.w * inv),
-                   l2 > 0.f ? m2 + __log2f(l2) : -INFINITY);
-    }
+    last_merge<D, RPC, CL>(p, u, h, r, n_u, (size_t)uidx * cpu, stages, xstep);
     if (threadIdx.x == 0) *ctr = 0;  // ready for the next call on this pool
+    if (p.x.peers) exchange_finish<D, RPC, CL>(p, u, h, r, xsi, xstep);
 }
 
 // ---- schedule 2: a 3-D grid of (unit, chunk of tiles) ----------------------------------------
@@ -1298,11 +1448,12 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
         if (plan.cluster) {
             auto kern = decode_cluster_kernel<D, NB, TPP, STAGES>;
             static LaunchCache ccache;
-            const int rc = raise_smem_attr((const void*)kern, SMEM, dev, ccache);
+            constexpr int SMEM_C = SMEM > kClusterSmemFloor ? SMEM : kClusterSmemFloor;
+            const int rc = raise_smem_attr((const void*)kern, SMEM_C, dev, ccache);
             if (rc) return rc;
             const long long units = (long long)a.batch * a.pool->desc.n_kv_heads;
             const long long ctas = units * plan.max_chunks * kClusterCtas;
-            kern<<<(unsigned)ctas, kThreads, SMEM, a.stream>>>(p);
+            kern<<<(unsigned)ctas, kThreads, SMEM_C, a.stream>>>(p);
             e = cudaGetLastError();
             return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_cluster launch");
         }
@@ -1388,7 +1539,8 @@ template <int D, int NB, int TPP, int STAGES>
 static int cluster_capacity_t(int dev, int sm_count) {
     static int cached[64] = {};
     constexpr int TB = 32 * D + 64 * NB;
-    constexpr int SMEM = hdr_bytes<NB, 1>() + kWarps * STAGES * TB;
+    constexpr int SMEM0 = hdr_bytes<NB, 1>() + kWarps * STAGES * TB;
+    constexpr int SMEM = SMEM0 > kClusterSmemFloor ? SMEM0 : kClusterSmemFloor;  // as launched
     const int fallback = std::max(1, sm_count * 2 / kClusterCtas);
     if (dev < 0 || dev >= 64) return fallback;
     std::lock_guard<std::mutex> lock(g_cluster_mu);
@@ -1466,6 +1618,8 @@ int launch_splitkv(const AttnArgs& a, const SplitPlan& plan) {
     p.status = a.pool->d_status;
     p.trie = reinterpret_cast<const int2*>(a.trie);
     p.wait_ns = wait_limit_ns(a.pool);
+    p.x = a.xf ? *a.xf : XFuse{};
+    if (p.x.peers && !plan.cluster) return fail(YF_E_UNSUPPORTED, "the fused exchange needs the cluster schedule");
     if (p.trie && plan.persistent) return fail(YF_E_UNSUPPORTED, "tree verify needs the chunked schedule");
     const size_t units = (size_t)a.batch * d.n_kv_heads * plan.n_row_groups;
     p.counters = (plan.fused_combine && units <= (size_t)kMaxCombineUnits) ? a.pool->d_counters : nullptr;

@@ -3,16 +3,20 @@
 // The sharded long-context decode (kv head x key range per GPU) ends every step with each rank's
 // packed partial [O f32 rows*D | lse f32 rows] needed on every rank.  Instead of a collective
 // library call, every rank owns an exchange area in its own memory, mapped into the other ranks'
-// address spaces once at set-up (CUDA IPC, plain peer mappings):
-//   [2 buffers][world slots][slot_floats] f32 | [world] u32 flags | u32 epoch | u32 status
-// Step s (the push kernel's epoch + 1): the push kernel stores this rank's partial into slot
-// `rank` of buffer s & 1 in every rank's area with plain stores over NVLink, fences at system
-// scope, and stores s into flag `rank` of every area (release).  The combine kernel, later in the
-// same stream, waits (bounded by the exchange's wait limit) until every flag in its own area has
-// reached s (acquire), then merges the head groups' parts in place into f16 output, as
-// yf_attn_combine does.  Two buffers are enough: a rank can push step s+1 only after its combine
-// of step s, which needed every rank's push of step s, and each rank pushes s+1 only after its
-// own combine of s -- so nobody overwrites a buffer that another rank still reads.
+// address spaces once at set-up (CUDA IPC, plain peer mappings); yf_xchg.cuh gives its layout.
+// Step s (epoch + 1): this rank's partial is stored into slot `rank` of buffer s & 1 in every
+// rank's area with plain stores over NVLink, fenced at system scope, and s is stored into flag
+// `rank` of every area (release).  The merge waits (bounded by the exchange's wait limit) until
+// every flag of its own area has reached s (acquire), then merges the head groups' parts in place
+// into f16 output, as yf_attn_combine does.  Two buffers are enough: a rank writes step s+1 only
+// after its merge of step s, which needed every rank's step-s partial, and each rank writes s+1
+// only after its own merge of s -- so nobody overwrites a buffer that another rank still reads.
+//
+// Two ways to run a step: yf_exchange_push then yf_exchange_combine (two kernels after the
+// caller's yf_attn_decode_partial; ranks can be emulated on one GPU, every push before every
+// combine), or yf_exchange_decode, where the cluster decode kernel itself stores the partial into
+// the areas, raises the flags and merges in its last CTA: one launch per step, for ranks on
+// separate GPUs only (on one GPU the ranks' kernels would wait on one another).
 // Replaces the all-gather + flash_fwd_splitkv_combine_kernel pair
 // (docs/plans/2026-09-16-prefil-parity-fa2-and-mmq.md:104-107) across GPUs.
 #include <cuda_fp16.h>
@@ -23,6 +27,7 @@
 
 #include "yf_device.cuh"
 #include "yf_internal.h"
+#include "yf_xchg.cuh"
 
 struct yf_exchange {
     int device = -1;
@@ -31,10 +36,14 @@ struct yf_exchange {
     long long slot_floats = 0;
     uint8_t* area = nullptr;        // this rank's area (cudaMalloc)
     size_t area_bytes = 0;
-    size_t flags_off = 0;           // byte offset of the flags, then epoch, then status
+    size_t flags_off = 0;           // byte offset of the meta words (flags, epoch, status)
+    size_t sstep_off = 0;           // byte offset of the fused path's slice step counts
+    size_t words_off = 0;           // byte offset of the fused path's (value, step) word buffers
     unsigned long long* d_peers = nullptr;  // device array: every rank's area base (own included)
     std::vector<unsigned long long> peers;  // host copy
     std::vector<void*> opened;      // IPC mappings to close
+    bool emulated = false;          // a peer area attached in this process on the same device
+    float* staging = nullptr;       // the partial of the unfused yf_exchange_decode path
     uint64_t wait_ns = 1000000000ull;
 };
 
@@ -42,15 +51,6 @@ namespace yf {
 namespace {
 
 constexpr int kXThreads = 256;
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 struct XParams {
     const unsigned long long* peers;  // area bases
@@ -60,85 +60,36 @@ struct XParams {
     uint8_t* local;
 };
 
-__device__ __forceinline__ float* slot_of(unsigned long long area, int buf, int world, long long slot_floats, int r) {
-    return reinterpret_cast<float*>(area) + ((long long)buf * world + r) * slot_floats;
-}
-
 // One block: this rank's partial into slot `rank` of every area, then its flag in every area.
 __global__ void __launch_bounds__(kXThreads) push_kernel(const XParams x, const float4* __restrict__ src) {
-    uint32_t* meta = reinterpret_cast<uint32_t*>(x.local + x.flags_off);
+    uint32_t* meta = xmeta(x.local, x.flags_off);
     const uint32_t step = meta[x.world] + 1u;  // epoch + 1
-    const int buf = (int)(step & 1u);
     const long long n4 = x.slot_floats / 4;
     for (int k = 0; k < x.world; ++k) {
-        float4* dst = reinterpret_cast<float4*>(slot_of(x.peers[k], buf, x.world, x.slot_floats, x.rank));
+        float4* dst = reinterpret_cast<float4*>(xslot(x.peers[k], step, x.world, x.slot_floats, x.rank));
         for (long long i = threadIdx.x; i < n4; i += kXThreads) dst[i] = __ldg(src + i);
     }
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int k = 0; k < x.world; ++k)
-            st_release_sys(reinterpret_cast<uint32_t*>(x.peers[k] + x.flags_off) + x.rank, step);
+        xraise(x.peers, x.world, x.rank, x.flags_off, step);
         meta[x.world] = step;  // the step the combine waits for
     }
 }
 
-// Waits for every rank's flag of the current step, then merges: one thread per (head group,
-// row, 4 dims); head group g's parts are ranks s * n_hg + g, s < n_seq; O of a part at offset 0
-// of its slot, lse at o_floats; row i = b * hq + j goes to output row b * Hq + g * hq + j.
+// Waits (one thread per block) for every rank's flag of the current step, then merges: one
+// thread per (head group, row, 4 dims), as xmerge4 describes.
 __global__ void __launch_bounds__(kXThreads) exchange_combine_kernel(const XParams x, int n_hg, int n_seq, int rows,
-                                                                     int hq, int Hq, int d4n, long long o_floats,
+                                                                     int hq, int Hq, int d4n, long long lse_off,
                                                                      uint64_t wait_ns, __half* __restrict__ out) {
-    uint32_t* meta = reinterpret_cast<uint32_t*>(x.local + x.flags_off);
+    uint32_t* meta = xmeta(x.local, x.flags_off);
     __shared__ int s_ok;
     const uint32_t step = meta[x.world];
-    if (threadIdx.x == 0) {
-        bool ok = true;
-        const uint64_t t0 = globaltimer_ns();
-        for (int k = 0; k < x.world && ok; ++k) {
-            for (uint32_t it = 0;; ++it) {
-                if ((int)(ld_acquire_sys(meta + k) - step) >= 0) break;
-                if ((it & 31u) == 31u && globaltimer_ns() - t0 > wait_ns) {
-                    ok = false;
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-        if (!ok) atomicOr(meta + x.world + 1, YF_DEV_TIMEOUT);
-        s_ok = ok;
-    }
+    if (threadIdx.x == 0) s_ok = xwait(meta, x.world, step, wait_ns);
     __syncthreads();
     const int e = blockIdx.x * kXThreads + threadIdx.x;
     if (!s_ok || e >= n_hg * rows * d4n) return;
-    const int g = e / (rows * d4n), r = (e / d4n) % rows, c = e % d4n;
-    const int buf = (int)(step & 1u);
-    const unsigned long long base = reinterpret_cast<unsigned long long>(x.local);
-    float M = -INFINITY;
-    for (int s = 0; s < n_seq; ++s)
-        M = fmaxf(M, __ldcg(slot_of(base, buf, x.world, x.slot_floats, s * n_hg + g) + o_floats + r));
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (M != -INFINITY) {
-        for (int s = 0; s < n_seq; ++s) {
-            const float* sl = slot_of(base, buf, x.world, x.slot_floats, s * n_hg + g);
-            const float lv = __ldcg(sl + o_floats + r);
-            if (lv == -INFINITY) continue;
-            const float w = fast_exp2((lv - M) * 1.4426950408889634f);
-            L += w;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(sl) + (size_t)r * d4n + c);
-            acc.x = fmaf(w, v.x, acc.x);
-            acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z);
-            acc.w = fmaf(w, v.w, acc.w);
-        }
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int b = r / hq, j = r % hq;
-    uint2 pk;
-    pk.x = pack_h2(acc.x * inv, acc.y * inv);
-    pk.y = pack_h2(acc.z * inv, acc.w * inv);
-    reinterpret_cast<uint2*>(out + ((size_t)b * Hq + (size_t)g * hq + j) * (size_t)(4 * d4n))[c] = pk;
+    xmerge4(x.local, step, x.world, x.slot_floats, lse_off, n_hg, n_seq, rows, hq, Hq, d4n, e, out);
 }
 
 XParams params_of(const yf_exchange* ex) {
@@ -183,7 +134,9 @@ int yf_exchange_create(int32_t device, int32_t rank, int32_t world, int64_t slot
     ex->world = world;
     ex->slot_floats = slot_floats;
     ex->flags_off = (size_t)2 * world * slot_floats * sizeof(float);
-    ex->area_bytes = ex->flags_off + ((size_t)(world + 2) * sizeof(uint32_t) + 255) / 256 * 256;
+    ex->sstep_off = ex->flags_off + ((size_t)(world + 2) * sizeof(uint32_t) + 255) / 256 * 256;
+    ex->words_off = ex->sstep_off + ((size_t)kXMaxSlices * sizeof(uint32_t) + 255) / 256 * 256;
+    ex->area_bytes = ex->words_off + (size_t)2 * world * slot_floats * sizeof(unsigned long long);
     cudaError_t e = cudaSetDevice(device);
     if (e == cudaSuccess) e = cudaMalloc(&ex->area, ex->area_bytes);
     if (e == cudaSuccess) e = cudaMemset(ex->area, 0, ex->area_bytes);
@@ -192,6 +145,13 @@ int yf_exchange_create(int32_t device, int32_t rank, int32_t world, int64_t slot
         if (ex->area) cudaFree(ex->area);
         delete ex;
         return cuda_fail(e, "exchange area");
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&ex->staging, (size_t)slot_floats * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaFree(ex->area);
+        cudaFree(ex->d_peers);
+        delete ex;
+        return cuda_fail(e, "exchange staging");
     }
     ex->peers.assign(world, 0ull);
     ex->peers[rank] = reinterpret_cast<unsigned long long>(ex->area);
@@ -210,6 +170,7 @@ int yf_exchange_destroy(yf_exchange* ex) {
     if (!ex) return YF_OK;
     cudaSetDevice(ex->device);
     for (void* p : ex->opened) cudaIpcCloseMemHandle(p);
+    if (ex->staging) cudaFree(ex->staging);
     cudaFree(ex->area);
     cudaFree(ex->d_peers);
     delete ex;
@@ -248,6 +209,7 @@ int yf_exchange_attach(yf_exchange* ex, int32_t peer, const yf_exchange* other) 
         return fail(YF_E_INVALID, "peer %d does not match the other exchange", peer);
     if (other->device != ex->device) return fail(YF_E_UNSUPPORTED, "attach needs both areas on one device");
     ex->peers[peer] = reinterpret_cast<unsigned long long>(other->area);
+    ex->emulated = true;
     return sync_peers(ex);
 }
 
@@ -286,6 +248,55 @@ int yf_exchange_combine(yf_exchange* ex, int32_t n_head_groups, int32_t n_seq, i
         static_cast<__half*>(d_out));
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? YF_OK : cuda_fail(e, "exchange combine launch");
+}
+
+int yf_exchange_decode(yf_exchange* ex, yf_pool* pool, int32_t layer, const void* d_q, int32_t hq,
+                       const uint32_t* d_cu_k, const uint32_t* d_block_table, int32_t max_blocks, int32_t batch,
+                       int32_t max_seqlen_k, float scale, int32_t n_head_groups, int32_t n_seq, int32_t n_q_heads,
+                       void* d_out, void* d_workspace, size_t workspace_bytes, void* stream) {
+    if (!ex || !pool) return fail(YF_E_INVALID, "null argument");
+    if (n_head_groups < 1 || n_seq < 1 || (long long)n_head_groups * n_seq != ex->world)
+        return fail(YF_E_INVALID, "n_head_groups %d x n_seq %d != world %d", n_head_groups, n_seq, ex->world);
+    if (hq < 1 || n_q_heads != hq * n_head_groups)
+        return fail(YF_E_INVALID, "n_q_heads %d != hq %d x n_head_groups %d", n_q_heads, hq, n_head_groups);
+    if (ex->world > 1 && ex->emulated)
+        return fail(YF_E_UNSUPPORTED, "ranks attached on one device: run yf_exchange_push and yf_exchange_combine");
+    for (int k = 0; k < ex->world; ++k)
+        if (!ex->peers[k]) return fail(YF_E_STATE, "rank %d's area is not mapped", k);
+    if (pool->desc.device != ex->device) return fail(YF_E_INVALID, "pool and exchange on different devices");
+    const int D = pool->desc.head_dim;
+    const long long rows = (long long)batch * hq;
+    if (batch < 1 || rows * (D + 1) > ex->slot_floats)
+        return fail(YF_E_INVALID, "batch %d x hq %d x (head_dim + 1) exceeds the slot of %lld floats", batch, hq,
+                    ex->slot_floats);
+    XFuse xf;
+    xf.peers = ex->d_peers;
+    xf.local = ex->area;
+    xf.rank = ex->rank;
+    xf.world = ex->world;
+    xf.slot_floats = ex->slot_floats;
+    xf.lse_off = rows * D;
+    xf.flags_off = ex->flags_off;
+    xf.sstep_off = ex->sstep_off;
+    xf.words_off = ex->words_off;
+    xf.n_hg = n_head_groups;
+    xf.n_seq = n_seq;
+    xf.hq = hq;
+    xf.n_q_heads = n_q_heads;
+    xf.rows = (int)rows;
+    xf.out = static_cast<__half*>(d_out);
+    xf.wait_ns = ex->wait_ns;
+    bool fused = false;
+    int rc = decode_exchange(pool, layer, d_q, hq, d_cu_k, d_block_table, max_blocks, batch, max_seqlen_k, scale, xf,
+                             d_workspace, workspace_bytes, stream, &fused);
+    if (rc || fused) return rc;
+    // another schedule took the call: the partial into the staging slot, then push and combine
+    rc = yf_attn_decode_partial(pool, layer, d_q, hq, d_cu_k, d_block_table, max_blocks, batch, max_seqlen_k, scale,
+                                ex->staging, ex->staging + rows * D, d_workspace, workspace_bytes, stream);
+    if (!rc) rc = yf_exchange_push(ex, ex->staging, stream);
+    if (!rc)
+        rc = yf_exchange_combine(ex, n_head_groups, n_seq, (int32_t)rows, hq, n_q_heads, D, rows * D, d_out, stream);
+    return rc;
 }
 
 int yf_exchange_status(yf_exchange* ex, uint32_t* out_bits, int clear) {

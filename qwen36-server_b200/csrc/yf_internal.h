@@ -27,6 +27,11 @@ constexpr int kMaxCtasPerSm = 4;
 // CTAs per thread-block cluster of the few-long-units decode schedule, and the most units it takes.
 constexpr int kClusterCtas = 8;
 constexpr int kClusterMaxUnits = 32;
+// Dynamic shared memory floor of that schedule's CTAs: above a third of an SM's 228 KB, so no SM
+// hosts three of them while others host one (CTAs of equal work then stream at equal rates).
+constexpr int kClusterSmemFloor = 80 * 1024;
+// Most cluster partials of one unit (sizes the last merge's weight table in shared memory).
+constexpr int kClusterMaxParts = 256;
 
 // Byte offsets of the four areas of a 16-token tile (see yf_pool_tile_offset).
 struct TileGeom {
@@ -117,6 +122,27 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
 // draft rows per entry of a tree verify (a 64-bit ancestor mask per row in the kernel)
 constexpr int kMaxTreeRowsHost = 64;
 
+// The exchange of a sharded decode's partial, fused into the cluster decode kernel
+// (yf_exchange_decode): every CTA that finishes an output slice of this rank's partial stores it
+// as 64-bit (value, step) words into slot `rank` of word buffer step & 1 in every rank's area,
+// then polls the same rows of every rank's slot in its own area and merges them into f16 `out`.
+// Shared-memory floats are not needed; the bounds below keep the per-thread state small.
+constexpr int kXMaxSlices = 256;  // output slices of one call (units x cluster CTAs)
+constexpr int kXMaxSeq = 8;       // key ranges merged per head group
+struct XFuse {
+    const unsigned long long* peers = nullptr;  // device array: every rank's area base (null: off)
+    uint8_t* local = nullptr;                   // this rank's area
+    int rank = 0, world = 1;
+    long long slot_floats = 0;  // words per rank slot (the float slot's layout)
+    long long lse_off = 0;      // words: the lse rows inside a slot
+    size_t flags_off = 0;       // bytes: the meta words (status at world + 1)
+    size_t sstep_off = 0;       // bytes: u32 [kXMaxSlices] step count of every output slice
+    size_t words_off = 0;       // bytes: u64 [2][world][slot_floats] word buffers
+    int n_hg = 1, n_seq = 1, hq = 1, n_q_heads = 1, rows = 1;
+    __half* out = nullptr;  // f16 [rows / hq][n_q_heads][head_dim]
+    uint64_t wait_ns = 0;
+};
+
 struct AttnArgs {
     const yf_pool* pool;
     int layer;
@@ -140,10 +166,17 @@ struct AttnArgs {
     float* part_lse = nullptr;
     // tree verify: int32 [total_q][2] inclusive subtree range of every draft row, or null
     const int32_t* trie = nullptr;
+    // fused partial exchange (cluster schedule only), or null
+    const XFuse* xf = nullptr;
 };
 
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan);
+// A sharded decode's partial with the exchange fused in (yf_pool.cu): *fused = false and nothing
+// launched when the cluster schedule does not take this call.
+int decode_exchange(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_k, const uint32_t* bt,
+                    int32_t max_blocks, int32_t batch, int32_t max_k, float scale, const XFuse& xf, void* ws,
+                    size_t ws_bytes, void* stream, bool* fused);
 // Clusters of the few-long-units decode kernel that fit on the pool's device at once (one wave),
 // for a ring of `stages` copy stages (cached per device; an estimate for a host-only pool).
 int cluster_capacity(const yf_pool* pool, int stages);

@@ -128,7 +128,8 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
         // not SMs x CTAs per SM, bounds the grid (a partial second wave doubles the time)
         const long long target = std::min((long long)pool->sm_count * 2, std::max<long long>(kClusterCtas, units * tiles / 16));
         const long long cap = cluster_capacity(pool, p.stages);
-        const long long cpu = std::max<long long>(1, std::min(target / (units * kClusterCtas), cap / units));
+        const long long cpu = std::max<long long>(
+            1, std::min<long long>(std::min(target / (units * kClusterCtas), cap / units), kClusterMaxParts));
         p.max_chunks = (int)cpu;                         // clusters per unit
         p.chunk_tiles = (int)((tiles + cpu - 1) / cpu);  // tiles per cluster
         const size_t row_bytes_c = p.rows_per_cta * (pool->desc.head_dim + 1) * sizeof(float);
@@ -560,3 +561,43 @@ int yf_attn_verify_tree(yf_pool* pool, int32_t layer, const void* q, int32_t hq,
 }
 
 }  // extern "C"
+
+namespace yf {
+
+int decode_exchange(yf_pool* pool, int32_t layer, const void* q, int32_t hq, const uint32_t* cu_k, const uint32_t* bt,
+                    int32_t max_blocks, int32_t batch, int32_t max_k, float scale, const XFuse& xf, void* ws,
+                    size_t ws_bytes, void* stream, bool* fused) {
+    *fused = false;
+    const int rc = check_attn(pool, layer, q, hq, cu_k, bt, max_blocks, batch, 1, max_k, scale, xf.out);
+    if (rc || batch == 0) return rc;
+    const SplitPlan plan = plan_split(pool, hq, batch, 1, max_k, false);
+    if (!plan.cluster || (long long)batch * pool->desc.n_kv_heads * kClusterCtas > kXMaxSlices ||
+        xf.n_seq > kXMaxSeq)
+        return YF_OK;
+    if (plan.ws_bytes > 0 && (!ws || ws_bytes < plan.ws_bytes || !aligned(ws, 16)))
+        return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", plan.ws_bytes,
+                    ws ? ws_bytes : (size_t)0);
+    AttnArgs a;
+    a.pool = pool;
+    a.layer = layer;
+    a.q = static_cast<const __half*>(q);
+    a.n_q_heads = hq;
+    a.cu_q = nullptr;
+    a.cu_k = cu_k;
+    a.block_table = bt;
+    a.max_blocks = max_blocks;
+    a.batch = batch;
+    a.max_seqlen_q = 1;
+    a.max_seqlen_k = max_k;
+    a.scale = scale;
+    a.out = nullptr;
+    a.workspace = ws;
+    a.workspace_bytes = ws_bytes;
+    a.stream = static_cast<cudaStream_t>(stream);
+    a.xf = &xf;
+    *fused = true;
+    return launch_splitkv(a, plan);
+}
+
+}  // namespace yf
+

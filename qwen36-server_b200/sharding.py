@@ -163,6 +163,22 @@ class PeerExchange:
              ctypes.c_void_p(out.data_ptr()), pa._stream(self.device))
         return out
 
+    def decode(self, pool, q: torch.Tensor, cu_k, table, scale: float, max_seqlen_k: int, n_head_groups: int,
+               n_seq: int, n_q_heads: int, out: torch.Tensor, workspace: torch.Tensor, layer: int = 0) -> torch.Tensor:
+        """The whole sharded step (yf_exchange_decode): this rank's partial over `pool` stored into
+        every rank's area, then every rank's partial merged into ``out`` [B, n_q_heads, D] f16 --
+        one launch where the cluster decode schedule applies.  Ranks on separate GPUs only."""
+        batch, hq = int(q.shape[0]), int(q.shape[1])
+        if out.dtype != torch.float16 or out.numel() < batch * n_q_heads * q.shape[-1]:
+            raise ValueError("out must be f16 [B, n_q_heads, D]")
+        cu = pa._i32(cu_k, self.device)
+        bt = pa._i32(table, self.device)
+        call("yf_exchange_decode", self._h, pool.handle, layer, ctypes.c_void_p(q.data_ptr()), hq,
+             ctypes.c_void_p(cu.data_ptr()), ctypes.c_void_p(bt.data_ptr()), bt.shape[1], batch, max_seqlen_k,
+             ctypes.c_float(scale), n_head_groups, n_seq, n_q_heads, ctypes.c_void_p(out.data_ptr()),
+             ctypes.c_void_p(workspace.data_ptr()), workspace.numel(), pa._stream(self.device))
+        return out
+
     def status(self, clear: bool = False) -> int:
         v = ctypes.c_uint32()
         call("yf_exchange_status", self._h, ctypes.byref(v), int(clear))
@@ -194,7 +210,10 @@ class PeerExchange:
             for b in xs:
                 if a is not b:
                     a.attach(b.rank, b)
+            a.is_emulated = world > 1
         return xs
+
+    is_emulated = False
 
     def close(self) -> None:
         if getattr(self, "_h", None) is not None and self._h.value:
@@ -262,6 +281,11 @@ class ShardedLongDecode:
         pa.dispatch_flash_decode_partial(q_local, self.pool, 0, cu_k, table, scale, max_seqlen_k=max_seqlen_k,
                                          o_part=self.o_part, lse_part=self.lse_part, workspace=self.ws)
 
+    @property
+    def fused(self) -> bool:
+        """The whole step is one yf_exchange_decode (p2p between ranks on separate GPUs)."""
+        return self.transport == "p2p" and not self.peer.is_emulated
+
     def exchange(self):
         if self.transport == "p2p":
             self.peer.push(self.local)
@@ -285,7 +309,13 @@ class ShardedLongDecode:
         return self.out
 
     def step(self, q_local: torch.Tensor, cu_k, table, scale: float, max_seqlen_k: int) -> torch.Tensor:
-        """Partial over this shard, exchange, combine: the full f16 output [B, Hq, D] on every rank."""
+        """Partial over this shard, exchange, combine: the full f16 output [B, Hq, D] on every rank
+        (with the p2p transport between GPUs, one fused launch)."""
+        if self.fused:
+            if self.pool.workspace_size(self.hq, self.batch, 1, max_seqlen_k) > self.ws.numel():
+                self.ws = self._workspace(max_seqlen_k)
+            return self.peer.decode(self.pool, q_local, cu_k, table, scale, max_seqlen_k, self.shard.n_head_groups,
+                                    self.shard.n_seq, self.Hq, self.out, self.ws)
         self.partial(q_local, cu_k, table, scale, max_seqlen_k)
         self.exchange()
         return self.combine()

@@ -118,3 +118,64 @@ def test_exchange_rejects_bad_arguments(yf, cuda):
         x.attach(1, y)
     y.close()
     x.close()
+
+
+def _long_shard_data(yf, oracle, cuda, ctx, Hq, H, D, batch, seed):
+    """K/V of `batch` entries of ctx keys, the unsharded GPU decode of them, and q."""
+    rng = np.random.default_rng(seed)
+    from qwen36_server_b200 import workloads as W
+    wl = W.Workload("xd", Hq, H, D, ctx=[ctx] * batch, q_rows=[1] * batch, seed=seed)
+    pool = yf.PagedKvPool(1, wl.n_pages, H, D, 16, 32, device=0)
+    bt = torch.from_numpy(wl.block_table).to(cuda)
+    ks, vs = [], []
+    for b in range(batch):
+        k = torch.from_numpy(W.kv_rows_np(rng, ctx, H, D, 0.0)).to(cuda)
+        v = torch.from_numpy(W.kv_rows_np(rng, ctx, H, D, 0.0)).to(cuda)
+        yf.launch_append_multi(pool, 0, k, v, [0, ctx], [0], bt[b:b + 1])
+        ks.append(k)
+        vs.append(v)
+    q = torch.from_numpy(rng.standard_normal((batch, Hq, D)).astype(np.float16)).to(cuda)
+    return wl, pool, bt, ks, vs, q
+
+
+@pytest.mark.parametrize("batch,schedule", [(1, _abi.YF_SCHED_AUTO), (3, _abi.YF_SCHED_AUTO),
+                                            (1, _abi.YF_SCHED_CHUNKED)])
+def test_exchange_decode_world1(yf, oracle, cuda, batch, schedule):
+    """yf_exchange_decode with one rank: the cluster kernel stores its partial into the area,
+    raises its own flag and merges in its last CTA (the fused launch), or with the chunked
+    schedule the partial + push + combine fallback; either equals the plain decode, over steps
+    that alternate the two buffers."""
+    ctx, Hq, H, D = 9000, 16, 2, 256
+    wl, pool, bt, _, _, q = _long_shard_data(yf, oracle, cuda, ctx, Hq, H, D, batch, 501 + batch)
+    pool.set_options(schedule=schedule)
+    scale = yf.default_scale(D)
+    cu = torch.tensor([i * ctx for i in range(batch + 1)], dtype=torch.int32, device=cuda)
+    ref = yf.dispatch_flash_decode_paged(q, pool, 0, cu, bt, scale).float().cpu().numpy()
+    x = S.PeerExchange(0, 1, S.packed_floats(batch, Hq, D), device=0)
+    ws = torch.empty(max(pool.workspace_size(Hq, batch, 1, ctx), 16), dtype=torch.uint8, device=cuda)
+    out = torch.full((batch, Hq, D), float("nan"), dtype=torch.float16, device=cuda)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        x.decode(pool, q, cu, bt, scale, ctx, 1, 1, Hq, out, ws)
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        assert np.abs(got - ref).max() <= 2e-3
+    assert x.status() == 0 and pool.status() == 0
+    x.close()
+    pool.close()
+
+
+def test_exchange_decode_refuses_emulated_ranks(yf, cuda):
+    """Ranks attached on one GPU would wait on one another inside one launch: refused."""
+    blk = S.packed_floats(1, 8, 256)
+    xs = S.PeerExchange.emulated(2, blk, device=0)
+    pool = yf.PagedKvPool(1, 8, 1, 256, 16, 32, device=0)
+    q = torch.zeros((1, 8, 256), dtype=torch.float16, device=cuda)
+    out = torch.empty((1, 16, 256), dtype=torch.float16, device=cuda)
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device=cuda)
+    with pytest.raises(_abi.YfError) as e:
+        xs[0].decode(pool, q, [0, 16], torch.zeros((1, 1), dtype=torch.int32, device=cuda), 0.1, 16, 2, 1, 16, out, ws)
+    assert e.value.code == _abi.YF_E_UNSUPPORTED
+    for x in xs:
+        x.close()
+    pool.close()
