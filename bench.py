@@ -52,7 +52,8 @@ def peaks():
 
 def dominant_kernel(config: str) -> str:
     """The kernel that dominates one attention call of the workload."""
-    return {"prefill_chunk": "prefill_tc_kernel", "tree_verify": "splitkv_kernel", "decode_long": "decode_cluster_kernel",
+    return {"prefill_chunk": "prefill_tc_kernel", "prefill_rowscale": "prefill_tc_kernel",
+            "prefill_d256": "splitkv_kernel", "tree_verify": "splitkv_kernel", "decode_long": "decode_cluster_kernel",
             "decode_small": "decode_cluster_kernel", "attn_prep": "attn_prep_kernel",
             "snapshot_records": "records_kernel"}.get(config, "decode_persistent_kernel")
 
@@ -539,7 +540,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     hbm, tflops, peak_kind = peaks()
     alg_bytes_attn = wl.kv_bytes(1) // (world if sharded else 1)
     achieved_gbs = alg_bytes_attn / (attn_ms * 1e-3) / 1e9
-    if wl.name == "prefill_chunk":
+    if wl.name.startswith("prefill"):
         roof = {"bound": "tensor", "achieved": wl.attn_flops() / wl.n_layers / (attn_ms * 1e-3) / 1e12,
                 "peak": tflops, "unit": "TFLOP/s"}
     else:
@@ -1081,8 +1082,8 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="decode_batch",
-                    choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "mtp_verify",
-                             "tree_verify", "attn_prep", "snapshot_records"])
+                    choices=["decode_small", "decode_batch", "decode_long", "prefill_chunk", "prefill_rowscale",
+                             "prefill_d256", "mtp_verify", "tree_verify", "attn_prep", "snapshot_records"])
     ap.add_argument("--impl", default="yfattn", choices=["yfattn", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every call directly instead of replaying a CUDA graph")

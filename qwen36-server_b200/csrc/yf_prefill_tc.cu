@@ -31,6 +31,8 @@
 //   * warp 13, copies (one lane): bulk copies of this CTA's 64-key half of each key tile (K+V
 //     int8 and scales, one 4352-byte block per 16-token tile), page ids read one half ahead.
 // At the end thread r reads row r of O_i and writes out[row] / l[row].
+// Pools with 32-dim scale groups (4352-byte tiles) and with one scale per row (4160-byte tiles,
+// the engine's own int8 pool format) are both read; only the dequant's scale indexing differs.
 #include <cstdint>
 #include <cstdlib>
 
@@ -48,7 +50,10 @@ constexpr int kPfD = 128;         // head dim (K of S, N of PV)
 constexpr int kPfTmemCols = 512;
 constexpr float kPfRescale = 8.0f;  // lazy rescale threshold (base 2), as in the decode kernels
 
-constexpr int kRawTileBytes = 4352;   // one 16-token pool tile, D=128, group 32
+// one 16-token pool tile at D=128: 4352 B with 32-dim scale groups (NB = 4), 4160 B with one
+// scale per row (NB = 1)
+template <int NB>
+constexpr int raw_tile_bytes() { return 32 * 128 + 64 * NB; }
 constexpr int kRawPitch = 4368;       // staged tiles 16 B apart modulo 128 B: spreads banks
 constexpr int kRawHalf = 4 * kRawPitch;  // 64 keys
 
@@ -179,7 +184,10 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, int use, volatile int*
     return false;
 }
 
+template <int NB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill_tc_kernel(const PrefillParams p) {
+    constexpr int kRawTileBytes = raw_tile_bytes<NB>();
+    static_assert(kRawTileBytes <= kRawPitch && kRawTileBytes % 16 == 0, "staged tile");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = smem_raw;
     const uint32_t sbase = smem_u32(smem_raw);
@@ -407,9 +415,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                 if (s_valid[slot * 4 + jt]) {
                     const uint4 kw = lds128(T + dw * 512 + (kg * 4 + ktig) * 16);
                     // K scales [token%8][token/8][group]
-                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2) * 4 + dw));
+                    // (the warp's 32 dims are scale group dw, or the row's one group)
+                    const int sg = NB == 1 ? 0 : dw;
+                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2) * NB + sg));
                     const uint16_t s1 =
-                        *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2 + 1) * 4 + dw));
+                        *reinterpret_cast<const uint16_t*>(T + 16 * kPfD + 2 * ((kg * 2 + 1) * NB + sg));
                     const uint32_t d0 = (uint32_t)s0 | ((uint32_t)s0 << 16), d1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
                     const uint32_t x0 = kw.x, x1 = kw.y, z0 = kw.z, z1 = kw.w;
                     o0 = make_uint4(dq2(x0, 0, d0), dq2(x0, 1, d0), dq2(x1, 0, d0), dq2(x1, 1, d0));
@@ -441,10 +451,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
             uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
             if (vvalid) {
                 // V scales [tig][group][j]: pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
-                const uint8_t* vsc = TV + 32 * kPfD + 128 + dw * 8;
+                const uint8_t* vsc = TV + 32 * kPfD + 32 * NB + (NB == 1 ? 0 : dw) * 8;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const uint2 pr = lds64(vsc + q * 32);
+                    const uint2 pr = lds64(vsc + q * 8 * NB);
                     sp[q] = __byte_perm(pr.x, pr.y, 0x5410);
                     sp[4 + q] = __byte_perm(pr.x, pr.y, 0x7632);
                 }
@@ -457,7 +467,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfBlock, 1) prefill
                 const int m = d >> 4, gp = d & 7;
                 uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
                 if (vvalid) {
-                    const uint8_t* vb = TV + 16 * kPfD + 128 + (m >> 1) * 512 + ((m & 1) * 2 + vdh) * 4;
+                    const uint8_t* vb = TV + 16 * kPfD + 32 * NB + (m >> 1) * 512 + ((m & 1) * 2 + vdh) * 4;
                     uint32_t wv[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) wv[q] = lds32(vb + (gp * 4 + q) * 16);
@@ -595,7 +605,8 @@ bool prefill_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q) {
     if (pool->opts.prefill_kernel == YF_PREFILL_SPLITKV) return false;
     const yf_pool_desc& d = pool->desc;
     const int G = n_q_heads / d.n_kv_heads;
-    return d.head_dim == kPfD && d.group_size == 32 && kPfRows % G == 0 && (long long)G * max_seqlen_q >= kPfRows;
+    return d.head_dim == kPfD && (d.group_size == 32 || d.group_size == d.head_dim) && kPfRows % G == 0 &&
+           (long long)G * max_seqlen_q >= kPfRows;
 }
 
 int launch_prefill_tc(const AttnArgs& a) {
@@ -618,14 +629,19 @@ int launch_prefill_tc(const AttnArgs& a) {
     p.out = a.out;
     p.status = a.pool->d_status;
     p.wait_ns = wait_limit_ns(a.pool);
-    static LaunchCache cache;
-    const int rc = raise_smem_attr((const void*)prefill_tc_kernel, kSmAlloc, d.device, cache);
+    const bool row_scale = d.group_size == d.head_dim;
+    static LaunchCache cache4, cache1;
+    const void* kern = row_scale ? (const void*)prefill_tc_kernel<1> : (const void*)prefill_tc_kernel<4>;
+    const int rc = raise_smem_attr(kern, kSmAlloc, d.device, row_scale ? cache1 : cache4);
     if (rc) return rc;
     const int ppb = kPfTiles * kPfRows / p.G;
     const long long blocks = (a.max_seqlen_q + ppb - 1) / ppb;
     const dim3 grid((unsigned)((blocks + 1) / 2 * 2), d.n_kv_heads, a.batch);  // clusters of 2 along x
     if (grid.x > 0x7fffffffu) return fail(YF_E_UNSUPPORTED, "too many query rows");
-    prefill_tc_kernel<<<grid, kPfBlock, kSmAlloc, a.stream>>>(p);
+    if (row_scale)
+        prefill_tc_kernel<1><<<grid, kPfBlock, kSmAlloc, a.stream>>>(p);
+    else
+        prefill_tc_kernel<4><<<grid, kPfBlock, kSmAlloc, a.stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? YF_OK : cuda_fail(e, "prefill_tc launch");
 }

@@ -137,6 +137,17 @@ def prefill_chunk(seed: int = 4, batch: int = 4, prefix: int = 8192, chunk: int 
     return Workload("prefill_chunk", 32, 8, 128, ctx=[prefix + chunk] * batch, q_rows=[chunk] * batch, seed=seed)
 
 
+def prefill_rowscale(seed: int = 4, batch: int = 4, prefix: int = 8192, chunk: int = 2048) -> Workload:
+    """prefill_chunk's shape over the pool format with one scale per row (group = head_dim)."""
+    return Workload("prefill_rowscale", 32, 8, 128, ctx=[prefix + chunk] * batch, q_rows=[chunk] * batch,
+                    group_size=128, seed=seed)
+
+
+def prefill_d256(seed: int = 4, batch: int = 4, prefix: int = 8192, chunk: int = 2048) -> Workload:
+    """A chunked prefill at decode_long's head shape (Hq 16 x D 256, Hkv 2)."""
+    return Workload("prefill_d256", 16, 2, 256, ctx=[prefix + chunk] * batch, q_rows=[chunk] * batch, seed=seed)
+
+
 def mtp_verify(seed: int = 5, n_slots: int = 64, drafts: int = 4, n_layers: int = 36) -> Workload:
     rng = np.random.default_rng(seed)
     ctx = rng.integers(4096, 65536, size=n_slots, endpoint=True)
@@ -169,6 +180,8 @@ CONFIGS = {
     "decode_batch": decode_batch,
     "decode_long": decode_long,
     "prefill_chunk": prefill_chunk,
+    "prefill_rowscale": prefill_rowscale,
+    "prefill_d256": prefill_d256,
     "mtp_verify": mtp_verify,
     "tree_verify": tree_verify,
 }

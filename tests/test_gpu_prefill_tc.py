@@ -58,3 +58,36 @@ def test_prefill_chunk_config_full_size(yf, oracle, cuda):
             assert np.abs(got[rows] - ref).max() <= TOL, (b, start)
     assert pool.status() == 0
     pool.close()
+
+
+@pytest.mark.parametrize("P", [16, 64])
+def test_prefill_tc_row_scale(yf, oracle, cuda, P):
+    """The pool format with one scale per row (group = head_dim, the reference's own int8 pool):
+    the tensor-core kernel reads the 4160-byte tiles and their per-row scales.  Ragged entries as
+    above, 16- and 64-token pages, against the oracle and the split-KV kernel."""
+    wl = W.Workload("pfr", 32, 8, 128, ctx=[300, 1257, 192, 6, 3000], q_rows=[300, 257, 128, 1, 700],
+                    group_size=128, page_size=P, seed=151)
+    pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=152)
+    q = queries(wl, 153)
+    got = run_prefill(yf, pool, wl, q, cuda)
+    ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(128))
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= TOL
+    alt = run_prefill(yf, pool, wl, q, cuda, tc=False)
+    assert np.abs(got - alt).max() <= TOL
+    assert pool.status() == 0
+    pool.close()
+
+
+def test_prefill_d256_against_oracle(yf, oracle, cuda):
+    """Causal chunked prefill at D 256 (Hq 16, Hkv 2: decode_long's head shape), which the
+    split-KV kernel serves: ragged chunks over prefixes against the oracle."""
+    wl = W.Workload("pf256", 16, 2, 256, ctx=[300, 2257, 129, 1], q_rows=[300, 257, 128, 1], seed=161)
+    pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=162)
+    q = queries(wl, 163)
+    got = run_prefill(yf, pool, wl, q, cuda)
+    ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(256))
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= TOL
+    assert pool.status() == 0
+    pool.close()
