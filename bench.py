@@ -53,7 +53,7 @@ def peaks():
 def dominant_kernel(config: str) -> str:
     """The kernel that dominates one attention call of the workload."""
     return {"prefill_chunk": "prefill_tc_kernel", "prefill_rowscale": "prefill_tc_kernel",
-            "prefill_d256": "splitkv_kernel", "tree_verify": "splitkv_kernel", "decode_long": "decode_cluster_kernel",
+            "prefill_d256": "prefill_tc256_kernel", "tree_verify": "splitkv_kernel", "decode_long": "decode_cluster_kernel",
             "decode_small": "decode_cluster_kernel", "attn_prep": "attn_prep_kernel",
             "snapshot_records": "records_kernel"}.get(config, "decode_persistent_kernel")
 

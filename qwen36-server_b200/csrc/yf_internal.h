@@ -200,5 +200,8 @@ int launch_verify_tc(const AttnArgs& a, const VerifyPlan& plan);
 // (yf_prefill_tc.cu); needs no workspace.
 bool prefill_tc_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q);
 int launch_prefill_tc(const AttnArgs& a);
+// The D=256 tcgen05 prefill (yf_prefill_tc256.cu).
+bool prefill_tc256_applies(const yf_pool* pool, int n_q_heads, int max_seqlen_q);
+int launch_prefill_tc256(const AttnArgs& a);
 
 }  // namespace yf

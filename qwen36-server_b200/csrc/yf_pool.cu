@@ -473,7 +473,8 @@ static int check_attn(const yf_pool* pool, int32_t layer, const void* q, int32_t
 
 size_t yf_attn_workspace_size(const yf_pool* pool, int32_t hq, int32_t batch, int32_t max_q, int32_t max_k) {
     if (!pool || batch <= 0 || hq < pool->desc.n_kv_heads || hq % pool->desc.n_kv_heads) return 0;
-    if (max_q > kMaxTreeRowsHost && prefill_tc_applies(pool, hq, max_q)) return 0;
+    if (max_q > kMaxTreeRowsHost && (prefill_tc_applies(pool, hq, max_q) || prefill_tc256_applies(pool, hq, max_q)))
+        return 0;
     // query blocks a causal or a tree verify can take: room for every schedule that may run
     size_t ws = plan_split(pool, hq, batch, max_q, max_k, false).ws_bytes;
     if (max_q <= 1 || max_q > kMaxTreeRowsHost) return ws;
@@ -492,10 +493,11 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     if (rc || batch == 0) return rc;
     if (part_o && (!part_lse || !aligned(part_lse, 4))) return fail(YF_E_INVALID, "lse output null or misaligned");
     const bool tc = !part_o && !trie && cu_q && prefill_tc_applies(pool, hq, max_q);
-    const bool vtc = !tc && !part_o && cu_q && verify_tc_applies(pool, hq, max_q, trie != nullptr);
+    const bool tc256 = !part_o && !trie && cu_q && prefill_tc256_applies(pool, hq, max_q);
+    const bool vtc = !tc && !tc256 && !part_o && cu_q && verify_tc_applies(pool, hq, max_q, trie != nullptr);
     const SplitPlan plan = plan_split(pool, hq, batch, max_q, max_k, trie != nullptr);
     const VerifyPlan vplan = vtc ? plan_verify(pool, hq, batch, max_q, max_k) : VerifyPlan{};
-    const size_t need = tc ? 0 : (vtc ? vplan.ws_bytes : plan.ws_bytes);
+    const size_t need = (tc || tc256) ? 0 : (vtc ? vplan.ws_bytes : plan.ws_bytes);
     if (need > 0 && (!ws || ws_bytes < need || !aligned(ws, 16)))
         return fail(YF_E_WORKSPACE, "workspace of %zu bytes (16-byte aligned) needed, %zu given", need,
                     ws ? ws_bytes : (size_t)0);
@@ -520,6 +522,7 @@ static int run_attn(yf_pool* pool, int32_t layer, const void* q, int32_t hq, con
     a.part_lse = part_lse;
     a.trie = trie;
     if (tc) return launch_prefill_tc(a);
+    if (tc256) return launch_prefill_tc256(a);
     if (vtc) return launch_verify_tc(a, vplan);
     return launch_splitkv(a, plan);
 }

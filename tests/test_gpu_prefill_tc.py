@@ -79,15 +79,46 @@ def test_prefill_tc_row_scale(yf, oracle, cuda, P):
     pool.close()
 
 
-def test_prefill_d256_against_oracle(yf, oracle, cuda):
-    """Causal chunked prefill at D 256 (Hq 16, Hkv 2: decode_long's head shape), which the
-    split-KV kernel serves: ragged chunks over prefixes against the oracle."""
-    wl = W.Workload("pf256", 16, 2, 256, ctx=[300, 2257, 129, 1], q_rows=[300, 257, 128, 1], seed=161)
+@pytest.mark.parametrize("group,P", [(32, 16), (256, 16), (32, 64)])
+def test_prefill_d256_against_oracle(yf, oracle, cuda, group, P):
+    """Causal chunked prefill at D 256 (Hq 16, Hkv 2: decode_long's head shape) on the D=256
+    tcgen05 kernel: ragged chunks over prefixes (full and partial 64-key tiles, a one-row chunk),
+    32-dim scale groups and one scale per row, 16- and 64-token pages, against the oracle and
+    against the split-KV kernel."""
+    wl = W.Workload("pf256", 16, 2, 256, ctx=[300, 2257, 129, 1, 5000], q_rows=[300, 257, 128, 1, 1000],
+                    group_size=group, page_size=P, seed=161)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=162)
     q = queries(wl, 163)
     got = run_prefill(yf, pool, wl, q, cuda)
     ref = oracle.c_attn(desc, img, 0, q, wl.cu_q, wl.cu_k, wl.block_table, yf.default_scale(256))
     assert np.isfinite(got).all()
     assert np.abs(got - ref).max() <= TOL
+    alt = run_prefill(yf, pool, wl, q, cuda, tc=False)
+    assert np.abs(got - alt).max() <= TOL
+    again = run_prefill(yf, pool, wl, q, cuda)
+    assert np.array_equal(got, again)
+    assert pool.status() == 0
+    pool.close()
+
+
+def test_prefill_d256_full_size(yf, oracle, cuda):
+    """The 4 x (8192 prefix + 2048 chunk) D=256 workload: the tensor-core kernel agrees with the
+    split-KV kernel on every row and with the oracle on windows of rows."""
+    wl = W.prefill_d256()
+    pool, _, desc, _, _ = filled_pool(yf, oracle, wl, seed=171, oracle_image=False)
+    q = queries(wl, 172)
+    got = run_prefill(yf, pool, wl, q, cuda)
+    alt = run_prefill(yf, pool, wl, q, cuda, tc=False)
+    assert np.isfinite(got).all()
+    assert np.abs(got - alt).max() <= TOL
+    img = pool.layer_bytes_view(0).cpu().numpy()
+    for b in range(wl.batch):
+        q0, tq, tk = int(wl.cu_q[b]), int(wl.q_rows[b]), int(wl.ctx[b])
+        for start in (0, 777, tq - 4):
+            n = 4
+            rows = slice(q0 + start, q0 + start + n)
+            ref = oracle.c_attn(desc, img, 0, q[rows], np.array([0, n]), np.array([0, tk - tq + start + n]),
+                                wl.block_table[b:b + 1], yf.default_scale(256))
+            assert np.abs(got[rows] - ref).max() <= TOL, (b, start)
     assert pool.status() == 0
     pool.close()
