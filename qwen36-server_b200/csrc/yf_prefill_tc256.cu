@@ -14,9 +14,12 @@
 //   O += P_j V_j           A = P_j from TMEM, B = V_j^T from shared memory (256 dims x 64 keys),
 //                          M = 128, N = 256, K = 64.
 // S is double-buffered: QK(j+1) runs while the softmax of tile j does.  CTAs come in clusters
-// of two covering adjacent row blocks of the same (entry, kv head); each CTA of the pair copies
-// and dequantizes dims [128e, 128e + 128) of every key (its half of each pool tile's K and V
-// bytes, plus the tile's scales) and writes the f16 result into both CTAs' shared memory.
+// of kCln covering adjacent row blocks of the same (entry, kv head); CTA e of a cluster copies
+// and dequantizes dims [e 256/kCln, (e+1) 256/kCln) of every key (its share of each pool tile's
+// K and V bytes, plus the tile's scales) and writes the f16 result into every CTA's shared
+// memory, so each pool byte is dequantized once for kCln x 128 query rows (a CTA holds one query
+// tile at D=256, so clusters of 4 bring the dequant per MMA flop down to the D=128 kernel's with
+// its pairs of two-tile CTAs).
 //
 // Warp roles (10 warps):
 //   * warps 0-3, softmax: thread r owns row r (TMEM lane r): Q row into TMEM at the start, then
@@ -24,7 +27,8 @@
 //     the previous PV has completed), exponentials, f16 P into TMEM; the output row at the end;
 //   * warps 4-7, dequant: this CTA's dims of each key tile -> f16 K [key][dim] and V^T [dim][key];
 //   * warp 8, control (one lane): every MMA and commit;
-//   * warp 9, copies (one lane): bulk copies of this CTA's half of the 4 pool tiles of a key tile.
+//   * warp 9, copies: page ids a chunk ahead in its lanes; one lane bulk-copies the 4 pool tiles
+//     of a key tile.
 #include <cstdint>
 
 #include "yf_device.cuh"
@@ -42,18 +46,21 @@ constexpr int kTmemCols = 512;
 constexpr int kTmO = 0, kTmQ = 256, kTmS = 384;  // S_b at kTmS + 64 b
 constexpr float kRescale = 8.0f;
 
-// A CTA's staged half of a 16-token pool tile: [K dims 128e.. 2048 B][K scales 32 NB]
-// [V dims 128e.. 2048 B][V scales 32 NB]; staged tiles 16 B apart modulo 128 B.
+constexpr int kCln = 2;              // CTAs per cluster
+constexpr int kDpc = kD / kCln;       // dims each CTA dequantizes
+static_assert(kDpc % 64 == 0 && kDpc >= 64, "whole K column blocks per CTA");
+// Every CTA stages whole 16-token pool tiles (one bulk copy each: a copy costs ~50 ns to issue,
+// so four per key tile rather than one per piece of a tile); staged tiles 16 B apart modulo 128 B.
 template <int NB>
-constexpr int half_bytes() { return 4096 + 64 * NB; }
+constexpr int tile_bytes() { return 32 * kD + 64 * NB; }
 template <int NB>
-constexpr int half_pitch() { return (half_bytes<NB>() - 16 + 127) / 128 * 128 + 16; }
+constexpr int raw_pitch() { return (tile_bytes<NB>() - 16 + 127) / 128 * 128 + 16; }
 
 constexpr int kSmK = 0;                    // K   [2 stages][4 col blocks of 64 dims][64 keys][128 B]
 constexpr int kSmVt = kSmK + 2 * 32768;    // V^T [2 stages][256 dims][128 B]
-constexpr int kSmRaw = kSmVt + 2 * 32768;  // raw [2 slots][4 pool tiles][pitch]
+constexpr int kSmRaw = kSmVt + 2 * 32768;  // raw [2 slots][4 pool tiles][pitch] (whole tiles)
 template <int NB>
-constexpr int sm_misc() { return kSmRaw + 2 * 4 * half_pitch<NB>(); }
+constexpr int sm_misc() { return kSmRaw + 2 * 4 * raw_pitch<NB>(); }
 template <int NB>
 constexpr int sm_alloc() { return sm_misc<NB>() + 256; }
 constexpr int kWarps = 10;
@@ -82,9 +89,9 @@ struct Params {
 };
 
 struct Bars {
-    uint64_t raw_full[2], raw_free[2];  // staged halves of the 4 pool tiles of a key tile
-    uint64_t k_full[2], v_full[2];      // K / V^T stage written (own half + the peer's copy)
-    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its MMA, here and in the peer
+    uint64_t raw_full[2], raw_free[2];  // the 4 staged pool tiles of a key tile
+    uint64_t k_full[2], v_full[2];      // K / V^T stage written (own share + the peers' copies)
+    uint64_t k_free[2], v_free[2];      // K / V^T stage read by its MMA in every CTA of the cluster
     uint64_t s_full[2], p_full[2];      // per S buffer
     uint64_t q_ready;                   // Q rows in TMEM
     uint64_t pv_done;                   // every PV completion (the rescale waits for the last)
@@ -94,9 +101,9 @@ struct Bars {
 static_assert(sizeof(Bars) <= 160, "barrier area");
 
 template <int NB>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_tc256_kernel(const Params p) {
-    constexpr int HB = half_bytes<NB>(), PITCH = half_pitch<NB>();
-    constexpr int TB = 32 * kD + 64 * NB;  // a whole pool tile
+__global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefill_tc256_kernel(const Params p) {
+    constexpr int TB = tile_bytes<NB>(), PITCH = raw_pitch<NB>();
+    static_assert(TB % 16 == 0 && PITCH >= TB, "staged tile");
     constexpr int SMISC = sm_misc<NB>();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = smem_raw;
@@ -125,18 +132,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
         return;
     }
     const int qrow0 = (int)p.cu_q[b];
-    const int rank = (int)(blockIdx.x & 1);  // rank in the cluster pair; dims [128 rank, +128)
-    const uint32_t peer = (uint32_t)(rank ^ 1);
-    const int pos0 = blockIdx.x * ppb, pair_pos0 = (blockIdx.x & ~1u) * ppb;
-    if (pair_pos0 >= Tq) return;  // both CTAs of the pair: no rows
-    const int npos = max(0, min(ppb, Tq - pos0));  // a pair's second CTA may have none
+    const int rank = (int)(blockIdx.x % kCln);  // rank in the cluster; dims [kDpc rank, +kDpc)
+    const int pos0 = blockIdx.x * ppb, cl_pos0 = (blockIdx.x / kCln) * kCln * ppb;
+    if (cl_pos0 >= Tq) return;  // every CTA of the cluster: no rows
+    const int npos = max(0, min(ppb, Tq - pos0));  // a cluster's later CTAs may have none
     const int rows = npos * p.G;
     const int kv0 = Tk - Tq;  // keys before the chunk
-    // both CTAs stream the key tiles of the pair's last row
-    const int kv_hi = max(0, min(Tk, kv0 + pair_pos0 + min(2 * ppb, Tq - pair_pos0)));
+    // every CTA streams the key tiles of the cluster's last row
+    const int kv_hi = max(0, min(Tk, kv0 + cl_pos0 + min(kCln * ppb, Tq - cl_pos0)));
     const int n_kt = (kv_hi + kKeys - 1) / kKeys;
     const int pt_total = (Tk + 15) / 16;
-    const int pt_need = (kv_hi + 15) / 16;  // pool tiles the pair reads
+    const int pt_need = (kv_hi + 15) / 16;  // pool tiles the cluster reads
     const uint32_t* btrow = p.bt + (size_t)b * p.max_blocks;
     const uint8_t* head_base = p.layer_base + (size_t)h * p.phb;
     const long long page_stride = p.phb * p.H;
@@ -146,10 +152,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_free[i], 4);
-            mbar_init(&bars->k_full[i], 4);  // the dequant warps; the peer's half comes as bytes
+            mbar_init(&bars->k_full[i], 4);  // the dequant warps; the peers' shares come as bytes
             mbar_init(&bars->v_full[i], 4);
-            mbar_init(&bars->k_free[i], 2);  // this CTA's and the peer's QK / PV of the stage
-            mbar_init(&bars->v_free[i], 2);
+            mbar_init(&bars->k_free[i], kCln);  // every CTA's QK / PV of the stage
+            mbar_init(&bars->v_free[i], kCln);
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->p_full[i], 4);
         }
@@ -174,7 +180,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
     tc_fence_before();
     const bool pages_ok = __syncthreads_or(bad) == 0;
     tc_fence_after();
-    cluster_sync();  // the peer's barriers are initialised before any remote arrival
+    cluster_sync();  // the peers' barriers are initialised before any remote arrival
     const uint32_t tmem = *tmem_slot;
 
     if (warp == kCtlWarp) {
@@ -198,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
                         const uint64_t bd = umma_desc_sw128(sbase + kSmVt + (j & 1) * 32768 + ks * 32);
                         umma_ts(tmem + kTmO, tP + ks * 8, bd, IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
                     }
-                    umma_commit_pair(&bars->v_free[j & 1]);
+                    umma_commit_mc(&bars->v_free[j & 1], (1u << kCln) - 1u);
                     umma_commit(&bars->pv_done);
                     if (j == n_kt - 1) umma_commit(&bars->o_done);
                     pv = j + 1;
@@ -216,7 +222,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
                         umma_ts(tS, tmem + kTmQ + ks * 8, bd, IDESC_S, ks > 0 ? 1u : 0u);
                     }
                     umma_commit(&bars->s_full[j & 1]);
-                    umma_commit_pair(&bars->k_free[j & 1]);
+                    umma_commit_mc(&bars->k_free[j & 1], (1u << kCln) - 1u);
                     qk = j + 1;
                     prog = true;
                 }
@@ -234,26 +240,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
         }
         __syncwarp();
     } else if (warp == kCopyWarp) {
-        // ================= copies: this CTA's half of the 4 pool tiles of each key tile =================
-        if (lane == 0) {
-            uint32_t page[4];
-            auto fetch_pages = [&](int kt) {  // page ids of pool tiles 4kt .. 4kt+3 (n_pages: skip)
+        // ================= copies: the 4 pool tiles of each key tile =================
+        // page ids of pool tiles [32c, 32c + 32) sit in the lanes' registers, the next chunk's
+        // loads in flight one chunk ahead; lane 0 issues the copies
+        auto load_chunk = [&](int c) -> uint32_t {
+            const int pt = c * 32 + lane;
+            return pt < pt_need ? __ldg(btrow + pt / p.tpp) : (uint32_t)p.n_pages;
+        };
+        uint32_t pg_cur = load_chunk(0), pg_next = load_chunk(1);
+        for (int kt = 0; kt < n_kt; ++kt) {
+            const int slot = kt & 1;
+            if (kt > 0 && (kt & 7) == 0) {
+                pg_cur = pg_next;
+                pg_next = load_chunk((kt >> 3) + 1);
+            }
+            uint32_t cur[4];
 #pragma unroll
-                for (int jt = 0; jt < 4; ++jt) {
-                    const int pt = kt * 4 + jt;
-                    page[jt] = pt < pt_need ? __ldg(btrow + pt / p.tpp) : (uint32_t)p.n_pages;
-                }
-            };
-            if (n_kt > 0) fetch_pages(0);
-            for (int kt = 0; kt < n_kt; ++kt) {
-                const int slot = kt & 1;
-                uint32_t cur[4];
-#pragma unroll
-                for (int jt = 0; jt < 4; ++jt) cur[jt] = page[jt];
-                if (kt + 1 < n_kt) fetch_pages(kt + 1);  // in flight while this tile waits
-                if (kt >= 2 &&
-                    !wait_phase(&bars->raw_free[slot], (kt >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(1, kBarRawFree, kt)))
-                    break;
+            for (int jt = 0; jt < 4; ++jt) cur[jt] = __shfl_sync(0xffffffffu, pg_cur, ((kt & 7) << 2) + jt);
+            bool ok = true;
+            if (lane == 0 && kt >= 2)
+                ok = wait_phase(&bars->raw_free[slot], (kt >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(1, kBarRawFree, kt));
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            if (lane == 0) {
                 uint8_t* dst = base + kSmRaw + slot * 4 * PITCH;
                 uint32_t bytes = 0;
                 const uint8_t* src[4];
@@ -266,59 +274,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
                     else if (pt < pt_need)
                         atomicOr(p.status, YF_DEV_BAD_PAGE);
                     s_valid[slot * 4 + jt] = src[jt] != nullptr;
-                    bytes += src[jt] ? HB : 0;
+                    bytes += src[jt] ? TB : 0;
                 }
                 mbar_arrive_expect_tx(&bars->raw_full[slot], bytes);
 #pragma unroll
-                for (int jt = 0; jt < 4; ++jt) {
-                    if (!src[jt]) continue;
-                    uint8_t* d = dst + jt * PITCH;
-                    const uint8_t* s = src[jt];
-                    // K dims of this half, all K scales, V dims of this half, all V scales
-                    bulk_g2s(d, s + 2048 * rank, 2048, &bars->raw_full[slot]);
-                    bulk_g2s(d + 2048, s + 16 * kD, 32 * NB, &bars->raw_full[slot]);
-                    bulk_g2s(d + 2048 + 32 * NB, s + 16 * kD + 32 * NB + 2048 * rank, 2048, &bars->raw_full[slot]);
-                    bulk_g2s(d + 4096 + 32 * NB, s + 32 * kD + 32 * NB, 32 * NB, &bars->raw_full[slot]);
-                }
+                for (int jt = 0; jt < 4; ++jt)
+                    if (src[jt]) bulk_g2s(dst + jt * PITCH, src[jt], TB, &bars->raw_full[slot]);
             }
         }
         __syncwarp();
     } else if (warp >= 4) {
-        // ================= dequant: raw halves -> f16 K and V^T of this CTA's dims =================
-        const int t = tid - 128, dw = t >> 5;  // warp dw: dims 32dw .. 32dw+31 of this CTA's half
-        const int sg = NB == 1 ? 0 : 4 * rank + dw;  // their scale group
+        // ================= dequant: staged tiles -> f16 K and V^T of this CTA's dims =================
+        // kDpc / 32 blocks of 32 dims; warp dw takes block db = dw / WPB and, when two warps share
+        // a block, half of its pool tiles (K) and half of its dim steps (V)
+        constexpr int NBLK = kDpc / 32, WPB = 4 / NBLK, JT = 4 / WPB;
+        const int t = tid - 128, dw = t >> 5, db = dw / WPB, part = dw % WPB;
+        const int sg = NB == 1 ? 0 : kDpc / 32 * rank + db;  // the scale group of the block
         // K: lane -> (token g, dim octet tig) of a 512-byte block, paired so that each
         // quarter-warp's loads and swizzled stores hit eight distinct 16-byte bank groups
         const int qw = lane >> 3, k8 = lane & 7;
         const int kg = (k8 < 4) ? qw : (qw ^ 5), ktig = k8 & 3;
-        // V: lane -> (dim bits 4, 3, 0; staged tile); warp and step give dim bits 5-6, 1-2
+        // V: lane -> (dim bits 4, 3, 0; staged tile); block and step give dim bits 5-6, 1-2
         const int vm1 = lane >> 4, vdh = (lane >> 3) & 1, vjt = (lane >> 1) & 3, vg1 = lane & 1;
-        const uint32_t peer_sbase = peer_addr(sbase, peer);
-        const uint32_t peer_k_full[2] = {peer_addr(smem_u32(&bars->k_full[0]), peer),
-                                         peer_addr(smem_u32(&bars->k_full[1]), peer)};
-        const uint32_t peer_v_full[2] = {peer_addr(smem_u32(&bars->v_full[0]), peer),
-                                         peer_addr(smem_u32(&bars->v_full[1]), peer)};
-        // K column: global dims 128 rank + 32 dw + 8 ktig .. +7 -> column block 2 rank + dw/2,
-        // 16-byte chunk (dw & 1) * 4 + ktig of the 128-byte row
-        const int kc = (2 * rank + (dw >> 1)) * 8 + (dw & 1) * 4 + ktig;
+        // K column: global dims kDpc rank + 32 db + 8 ktig .. +7 -> column block and chunk
+        const int kdim = kDpc * rank + 32 * db + 8 * ktig;
+        const int kc = (kdim >> 6) * 8 + ((kdim & 63) >> 3);
+        constexpr uint32_t SHARE = kDpc * 128;  // bytes of this CTA's K columns, and of its V^T rows
         for (int j = 0; j < n_kt; ++j) {
             const int slot = j & 1;
             (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarRawFull, j));
-            // K stage j&1 was last read by QK(j-2), here and in the peer
+            // K stage j&1 was last read by QK(j-2), in every CTA of the cluster
             if (j >= 2)
                 (void)wait_phase(&bars->k_free[slot], (j >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarKFree, j));
             const uint8_t* raw = base + kSmRaw + slot * 4 * PITCH;
             const uint32_t kdst = sbase + kSmK + slot * 32768, vdst = sbase + kSmVt + slot * 32768;
 #pragma unroll
-            for (int jt = 0; jt < 4; ++jt) {
-                // K: tokens kg, kg+8 x dims 32dw + 8ktig .. +7 (of this half) of pool tile jt
+            for (int i = 0; i < JT; ++i) {
+                // K: tokens kg, kg+8 x dims 32db + 8ktig .. +7 (of this share) of pool tile jt
+                const int jt = part * JT + i;
                 const uint8_t* T = raw + jt * PITCH;
                 uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
                 if (s_valid[slot * 4 + jt]) {
-                    const uint4 kw = lds128(T + dw * 512 + (kg * 4 + ktig) * 16);
+                    const uint4 kw = lds128(T + (kDpc / 32 * rank + db) * 512 + (kg * 4 + ktig) * 16);
                     // K scales [token%8][token/8][group]
-                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(T + 2048 + 2 * ((kg * 2) * NB + sg));
-                    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(T + 2048 + 2 * ((kg * 2 + 1) * NB + sg));
+                    const uint8_t* ks = T + 16 * kD;
+                    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(ks + 2 * ((kg * 2) * NB + sg));
+                    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(ks + 2 * ((kg * 2 + 1) * NB + sg));
                     const uint32_t d0 = (uint32_t)s0 | ((uint32_t)s0 << 16), d1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
                     o0 = make_uint4(dq2(kw.x, 0, d0), dq2(kw.x, 1, d0), dq2(kw.y, 0, d0), dq2(kw.y, 1, d0));
                     o1 = make_uint4(dq2(kw.z, 0, d1), dq2(kw.z, 1, d1), dq2(kw.w, 0, d1), dq2(kw.w, 1, d1));
@@ -328,26 +329,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
                 sts128(kdst + sw128_off(key + 8, kc, kKeys), o1);
             }
             fence_proxy_async_smem();
-            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' K columns precede the copy
+            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' K columns precede the copies
             if (t == 0) {
-                // this half's K columns (column blocks 2 rank, 2 rank + 1: 16 KB) into the peer; its
-                // bytes complete the peer's k_full, as the peer's do this CTA's (armed here)
-                const uint32_t k0 = kdst + 2 * rank * 8192;
-                bulk_s2peer(peer_sbase + (k0 - sbase), k0, 16384, peer_k_full[slot]);
-                mbar_arrive_expect_tx(&bars->k_full[slot], 16384);
+                // this CTA's K columns into every other CTA of the cluster; their bytes complete
+                // those CTAs' k_full, as theirs do this CTA's (armed here)
+                const uint32_t k0 = kdst + (kDpc * rank / 64) * 8192;
+#pragma unroll
+                for (int q = 1; q < kCln; ++q) {
+                    const uint32_t peer = (uint32_t)((rank + q) % kCln);
+                    bulk_s2peer(peer_addr(k0, peer), k0, SHARE, peer_addr(smem_u32(&bars->k_full[slot]), peer));
+                }
+                mbar_arrive_expect_tx(&bars->k_full[slot], (kCln - 1) * SHARE);
             } else if (lane == 0) {
                 mbar_arrive(&bars->k_full[slot]);
             }
-            // V^T stage j&1 was last read by PV(j-2), here and in the peer
+            // V^T stage j&1 was last read by PV(j-2), in every CTA of the cluster
             if (j >= 2)
                 (void)wait_phase(&bars->v_free[slot], (j >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarVFree, j));
-            // V: the thread's dims share one scale group; tile vjt
+            // V: the block's dims share one scale group; tile vjt
             const uint8_t* TV = raw + vjt * PITCH;
             const bool vvalid = s_valid[slot * 4 + vjt] != 0;
             uint32_t sp[8];  // (token 2k, 2k+1) f16x2 for k = 0..7
             if (vvalid) {
                 // V scales [tig][group][j]: pairs (2tig, 2tig+8), (2tig+1, 2tig+9)
-                const uint8_t* vsc = TV + 4096 + 32 * NB + sg * 8;
+                const uint8_t* vsc = TV + 32 * kD + 32 * NB + sg * 8;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const uint2 pr = lds64(vsc + q * 8 * NB);
@@ -356,13 +361,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
                 }
             }
 #pragma unroll
-            for (int st = 0; st < 4; ++st) {
-                // V^T row 128 rank + d, keys 16vjt .. +15 of the tile
-                const int d = 32 * dw + 16 * vm1 + 8 * vdh + 2 * st + vg1;
+            for (int i = 0; i < 4 / WPB; ++i) {
+                // V^T row kDpc rank + d, keys 16vjt .. +15 of the tile
+                const int st = part * (4 / WPB) + i;
+                const int d = 32 * db + 16 * vm1 + 8 * vdh + 2 * st + vg1;
                 const int m = d >> 4, gp = d & 7;
                 uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
                 if (vvalid) {
-                    const uint8_t* vb = TV + 2048 + 32 * NB + (m >> 1) * 512 + ((m & 1) * 2 + vdh) * 4;
+                    // V of global dim kDpc rank + d: 512-byte block (kDpc rank + d) / 32
+                    const uint8_t* vb = TV + 16 * kD + 32 * NB + (kDpc / 32 * rank + (m >> 1)) * 512 + ((m & 1) * 2 + vdh) * 4;
                     uint32_t wv[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) wv[q] = lds32(vb + (gp * 4 + q) * 16);
@@ -372,15 +379,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
                     lo = make_uint4(dq2(k03, 0, sp[0]), dq2(k03, 1, sp[1]), dq2(k47, 0, sp[2]), dq2(k47, 1, sp[3]));
                     hi = make_uint4(dq2(k8b, 0, sp[4]), dq2(k8b, 1, sp[5]), dq2(kcf, 0, sp[6]), dq2(kcf, 1, sp[7]));
                 }
-                sts128(vdst + sw128_off(128 * rank + d, 2 * vjt, kD), lo);
-                sts128(vdst + sw128_off(128 * rank + d, 2 * vjt + 1, kD), hi);
+                sts128(vdst + sw128_off(kDpc * rank + d, 2 * vjt, kD), lo);
+                sts128(vdst + sw128_off(kDpc * rank + d, 2 * vjt + 1, kD), hi);
             }
             fence_proxy_async_smem();
-            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' V^T rows precede the copy
+            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' V^T rows precede the copies
             if (t == 0) {
-                const uint32_t v0 = vdst + 128 * rank * 128;  // rows 128 rank .. +127: 16 KB
-                bulk_s2peer(peer_sbase + (v0 - sbase), v0, 16384, peer_v_full[slot]);
-                mbar_arrive_expect_tx(&bars->v_full[slot], 16384);
+                const uint32_t v0 = vdst + kDpc * rank * 128;  // rows kDpc rank .. +kDpc-1
+#pragma unroll
+                for (int q = 1; q < kCln; ++q) {
+                    const uint32_t peer = (uint32_t)((rank + q) % kCln);
+                    bulk_s2peer(peer_addr(v0, peer), v0, SHARE, peer_addr(smem_u32(&bars->v_full[slot]), peer));
+                }
+                mbar_arrive_expect_tx(&bars->v_full[slot], (kCln - 1) * SHARE);
                 mbar_arrive(&bars->raw_free[slot]);
             } else if (lane == 0) {
                 mbar_arrive(&bars->v_full[slot]);
@@ -509,7 +520,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBlock, 1) prefill_t
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
-    cluster_sync();  // no CTA leaves while its peer may still address its shared memory
+    cluster_sync();  // no CTA leaves while a peer may still address its shared memory
 }
 
 }  // namespace
@@ -551,7 +562,7 @@ int launch_prefill_tc256(const AttnArgs& a) {
     if (rc) return rc;
     const int ppb = kQRows / p.G;
     const long long blocks = (a.max_seqlen_q + ppb - 1) / ppb;
-    const dim3 grid((unsigned)((blocks + 1) / 2 * 2), d.n_kv_heads, a.batch);  // clusters of 2 along x
+    const dim3 grid((unsigned)((blocks + kCln - 1) / kCln * kCln), d.n_kv_heads, a.batch);  // clusters along x
     if (grid.x > 0x7fffffffu) return fail(YF_E_UNSUPPORTED, "too many query rows");
     if (row_scale)
         prefill_tc256_kernel<1><<<grid, kBlock, smem, a.stream>>>(p);
