@@ -658,8 +658,9 @@ def long_sharded_leg(args, rank: int, world: int, local_rank: int) -> dict:
     hbm, _, _ = peaks()
     shard_bytes = wl.kv_bytes(1) // world
     if step.transport == "p2p":
-        limiter = ("the peer-memory push of the packed partials (a few KB stored over NVLink) and the "
-                   "combine's wait for every rank's flag, on top of the shard's partial decode")
+        limiter = ("the shard's own decode (one kv head x key range: launch, stream and merge tail); the "
+                   "exchange is fused into its last slice merges (partial stored into every rank's area "
+                   "over NVLink as value+step words, polled and merged in place)")
     else:
         limiter = ("the NCCL all-gather of the packed partials plus the combine launch (latency, a few KB "
                    "moved) on top of the shard's partial decode")

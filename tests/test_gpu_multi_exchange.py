@@ -1,8 +1,8 @@
-"""The sharded long-context decode on two GPUs, one process per GPU: the fused exchange
+"""The sharded long-context decode on two and four GPUs, one process per GPU: the fused exchange
 (yf_exchange_decode: each rank's cluster decode stores its partial into every rank's exchange
 area over NVLink and merges in its last CTA) and the NCCL all-gather transport against the
-unsharded decode on each rank's own GPU.  Split by kv heads (2 kv heads) and by key ranges
-(1 kv head).  Skipped with fewer than two GPUs."""
+unsharded decode on each rank's own GPU.  Split by kv heads and by key ranges.  Skipped with
+fewer GPUs than ranks."""
 import multiprocessing as mp
 import os
 import socket
@@ -80,10 +80,13 @@ def _rank_main(rank: int, world: int, port: int, H: int, transport: str, q_out):
 
 @pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("H", [2, 1])
-def test_sharded_decode_two_gpus(H, transport):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world, port = 2, _free_port()
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_decode_multi_gpu(world, H, transport):
+    """world 2: kv heads split (H 2) or key ranges split (H 1); world 4: both (H 2: 2 head
+    groups x 2 key ranges) or four key ranges (H 1)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     procs = [ctx.Process(target=_rank_main, args=(r, world, port, H, transport, q_out)) for r in range(world)]
