@@ -21,13 +21,14 @@
 // tile at D=256, so clusters of 4 bring the dequant per MMA flop down to the D=128 kernel's with
 // its pairs of two-tile CTAs).
 //
-// Warp roles (10 warps):
+// Warp roles (14 warps):
 //   * warps 0-3, softmax: thread r owns row r (TMEM lane r): Q row into TMEM at the start, then
 //     per tile the row max, a lazy base-2 rescale of the running max (O rescaled in TMEM, after
 //     the previous PV has completed), exponentials, f16 P into TMEM; the output row at the end;
-//   * warps 4-7, dequant: this CTA's dims of each key tile -> f16 K [key][dim] and V^T [dim][key];
-//   * warp 8, control (one lane): every MMA and commit;
-//   * warp 9, copies: page ids a chunk ahead in its lanes; one lane bulk-copies the 4 pool tiles
+//   * warps 4-7 / 8-11, dequant: this CTA's dims of each key tile -> f16 K [key][dim] / V^T
+//     [dim][key], the two groups in parallel;
+//   * warp 12, control (one lane): every MMA and commit;
+//   * warp 13, copies: page ids a chunk ahead in its lanes; one lane bulk-copies the 4 pool tiles
 //     of a key tile.
 #include <cstdint>
 
@@ -63,10 +64,10 @@ template <int NB>
 constexpr int sm_misc() { return kSmRaw + 2 * 4 * raw_pitch<NB>(); }
 template <int NB>
 constexpr int sm_alloc() { return sm_misc<NB>() + 256; }
-constexpr int kWarps = 10;
+constexpr int kWarps = 14;
 constexpr int kBlock = kWarps * 32;
-constexpr int kCtlWarp = 8;
-constexpr int kCopyWarp = 9;
+constexpr int kCtlWarp = 12;
+constexpr int kCopyWarp = 13;
 
 struct Params {
     const uint8_t* layer_base;
@@ -151,7 +152,7 @@ __global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefil
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->raw_full[i], 1);
-            mbar_init(&bars->raw_free[i], 4);
+            mbar_init(&bars->raw_free[i], 8);  // the K and the V dequant warps
             mbar_init(&bars->k_full[i], 4);  // the dequant warps; the peers' shares come as bytes
             mbar_init(&bars->v_full[i], 4);
             mbar_init(&bars->k_free[i], kCln);  // every CTA's QK / PV of the stage
@@ -284,11 +285,13 @@ __global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefil
         }
         __syncwarp();
     } else if (warp >= 4) {
-        // ================= dequant: staged tiles -> f16 K and V^T of this CTA's dims =================
-        // kDpc / 32 blocks of 32 dims; warp dw takes block db = dw / WPB and, when two warps share
-        // a block, half of its pool tiles (K) and half of its dim steps (V)
+        // ================= dequant: staged tiles -> f16 K (warps 4-7) and V^T (warps 8-11) =================
+        // The two groups convert the same staged tiles in parallel.  kDpc / 32 blocks of 32 dims;
+        // warp dw of a group takes block db = dw / WPB and, when two warps share a block, half of
+        // its pool tiles (K) or half of its dim steps (V)
         constexpr int NBLK = kDpc / 32, WPB = 4 / NBLK, JT = 4 / WPB;
-        const int t = tid - 128, dw = t >> 5, db = dw / WPB, part = dw % WPB;
+        const bool kgrp = warp < 8;
+        const int t = tid - (kgrp ? 128 : 256), dw = t >> 5, db = dw / WPB, part = dw % WPB;
         const int sg = NB == 1 ? 0 : kDpc / 32 * rank + db;  // the scale group of the block
         // K: lane -> (token g, dim octet tig) of a 512-byte block, paired so that each
         // quarter-warp's loads and swizzled stores hit eight distinct 16-byte bank groups
@@ -303,11 +306,12 @@ __global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefil
         for (int j = 0; j < n_kt; ++j) {
             const int slot = j & 1;
             (void)wait_phase(&bars->raw_full[slot], j >> 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarRawFull, j));
+            const uint8_t* raw = base + kSmRaw + slot * 4 * PITCH;
+            const uint32_t kdst = sbase + kSmK + slot * 32768, vdst = sbase + kSmVt + slot * 32768;
+            if (kgrp) {
             // K stage j&1 was last read by QK(j-2), in every CTA of the cluster
             if (j >= 2)
                 (void)wait_phase(&bars->k_free[slot], (j >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarKFree, j));
-            const uint8_t* raw = base + kSmRaw + slot * 4 * PITCH;
-            const uint32_t kdst = sbase + kSmK + slot * 32768, vdst = sbase + kSmVt + slot * 32768;
 #pragma unroll
             for (int i = 0; i < JT; ++i) {
                 // K: tokens kg, kg+8 x dims 32db + 8ktig .. +7 (of this share) of pool tile jt
@@ -340,9 +344,12 @@ __global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefil
                     bulk_s2peer(peer_addr(k0, peer), k0, SHARE, peer_addr(smem_u32(&bars->k_full[slot]), peer));
                 }
                 mbar_arrive_expect_tx(&bars->k_full[slot], (kCln - 1) * SHARE);
+                mbar_arrive(&bars->raw_free[slot]);
             } else if (lane == 0) {
                 mbar_arrive(&bars->k_full[slot]);
+                mbar_arrive(&bars->raw_free[slot]);
             }
+            } else {
             // V^T stage j&1 was last read by PV(j-2), in every CTA of the cluster
             if (j >= 2)
                 (void)wait_phase(&bars->v_free[slot], (j >> 1) - 1, s_abort, p.status, p.wait_ns, wait_tag(2, kBarVFree, j));
@@ -383,7 +390,7 @@ __global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefil
                 sts128(vdst + sw128_off(kDpc * rank + d, 2 * vjt + 1, kD), hi);
             }
             fence_proxy_async_smem();
-            asm volatile("bar.sync 2, 128;" ::: "memory");  // the four warps' V^T rows precede the copies
+            asm volatile("bar.sync 3, 128;" ::: "memory");  // the four warps' V^T rows precede the copies
             if (t == 0) {
                 const uint32_t v0 = vdst + kDpc * rank * 128;  // rows kDpc rank .. +kDpc-1
 #pragma unroll
@@ -396,6 +403,7 @@ __global__ void __cluster_dims__(kCln, 1, 1) __launch_bounds__(kBlock, 1) prefil
             } else if (lane == 0) {
                 mbar_arrive(&bars->v_full[slot]);
                 mbar_arrive(&bars->raw_free[slot]);
+            }
             }
         }
     } else {
