@@ -1250,6 +1250,7 @@ __device__ __forceinline__ void last_merge(const SplitParams& p, const UnitGeom&
 template <int D, int NB, int TPP, int STAGES>
 __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads, 2)  // 2 per SM: kClusterSmemFloor
     decode_cluster_kernel(const SplitParams p) {
+    pdl_wait();  // before any global access: the previous kernel (a KV write) has completed
     constexpr int NT = 1, RPC = 8, CL = kClusterCtas;
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int DP = D + 4;
@@ -1363,6 +1364,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kThreads,
 
 template <int D, int NB, int NT, int TPP, int STAGES, bool TREE = false>
 __global__ void __launch_bounds__(kThreads) splitkv_kernel(const SplitParams p) {
+    pdl_wait();  // before any global access: the previous kernel (a KV write) has completed
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int RPC = 8 * NT;
     constexpr int DP = D + 4;
@@ -1453,8 +1455,17 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
             if (rc) return rc;
             const long long units = (long long)a.batch * a.pool->desc.n_kv_heads;
             const long long ctas = units * plan.max_chunks * kClusterCtas;
-            kern<<<(unsigned)ctas, kThreads, SMEM_C, a.stream>>>(p);
-            e = cudaGetLastError();
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)ctas);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = SMEM_C;
+            cfg.stream = a.stream;
+            cudaLaunchAttribute attr[1];
+            pdl_attr(attr[0]);
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, kern, p);
+            if (e == cudaSuccess) e = cudaGetLastError();
             return e == cudaSuccess ? YF_OK : cuda_fail(e, "decode_cluster launch");
         }
     }
@@ -1482,6 +1493,9 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = a.stream;
+        // no programmatic (early) launch here: the grid is sized to exactly one resident wave, and
+        // CTAs launched while the previous kernel still holds SMs start late and end late
+        // (decode_batch's step: 112.7 against 108.5 us)
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeCooperative;
         attr[0].val.cooperative = 1;
@@ -1495,9 +1509,17 @@ static int launch_t(const AttnArgs& a, const SplitPlan& plan, const SplitParams&
     static LaunchCache cache2;
     const int rc = raise_smem_attr((const void*)kern, SMEM, dev, cache2);
     if (rc) return rc;
-    const dim3 grid(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch, plan.max_chunks);
-    kern<<<grid, kThreads, SMEM, a.stream>>>(p);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch, plan.max_chunks);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = SMEM;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    pdl_attr(attr[0]);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "splitkv launch");
     if (plan.max_chunks > 1 && !p.counters) {
         const dim3 cg(a.pool->desc.n_kv_heads * plan.n_row_groups, a.batch);

@@ -37,6 +37,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization may
+// start while the previous kernel of its stream still runs; pdl_wait blocks until that kernel
+// has completed and its memory is visible (a no-op for a kernel launched without the attribute),
+// so the decode kernels call it before their first global-memory access.  pdl_trigger lets the
+// next kernel's CTAs launch early (a KV write before the attention that reads it).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");

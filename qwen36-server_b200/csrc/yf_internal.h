@@ -170,6 +170,13 @@ struct AttnArgs {
     const XFuse* xf = nullptr;
 };
 
+// Programmatic stream serialization: the kernel may be scheduled while the previous kernel of
+// its stream runs (it calls pdl_wait before touching global memory).
+inline void pdl_attr(cudaLaunchAttribute& a) {
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+}
+
 // Split-KV attention for decode / verify / small query blocks (yf_decode.cu).
 int launch_splitkv(const AttnArgs& a, const SplitPlan& plan);
 // A sharded decode's partial with the exchange fused in (yf_pool.cu): *fused = false and nothing

@@ -35,6 +35,7 @@ struct WriteParams {
 
 template <int D, int NB, int TPP, bool MULTI>
 __global__ void __launch_bounds__(kWriteWarps * 32) kv_write_kernel(const WriteParams p) {
+    pdl_trigger();  // the attention kernel that follows may be scheduled now (it waits for this one)
     constexpr int E = D / 32;   // elements per lane
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int P = TPP * 16;
@@ -93,6 +94,7 @@ constexpr int stage_pitch() { return 2 * D + 16; }  // bytes per staged row (16 
 
 template <int D, int NB, int TPP>
 __global__ void __launch_bounds__(kTileThreads) kv_write_tiles_kernel(const WriteParams p) {
+    pdl_trigger();  // the attention kernel that follows may be scheduled now (it waits for this one)
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int P = TPP * 16;
     constexpr int G = D / NB;

@@ -113,6 +113,7 @@ __device__ __forceinline__ void load_row_consts(const PrepParams& p, const float
 
 template <int D, int NB, int TPP>
 __global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const PrepParams p) {
+    pdl_trigger();  // the attention kernel that follows may be scheduled now (it waits for this one)
     constexpr int E = D / 32;
     constexpr int TB = 32 * D + 64 * NB;
     constexpr int P = TPP * 16;
