@@ -117,11 +117,14 @@ SplitPlan plan_split(const yf_pool* pool, int n_q_heads, int batch, int max_seql
     p.persistent = !tree && o.schedule != YF_SCHED_CHUNKED && p.n_row_groups == 1 && batch <= kPersistentMaxBatch &&
                    units <= kMaxCombineUnits && in_kernel_merge;
     if (p.persistent) p.fused_combine = true;
-    // A few long units (long-context decode, one rank's shard, a small decode): whole clusters of
-    // kClusterCtas CTAs per unit, at least 16 tiles per CTA and about two CTAs per SM in all (a
-    // third CTA per SM measured slower: more partials to merge, uneven CTAs per SM).
-    p.cluster = p.persistent && o.schedule == YF_SCHED_AUTO && p.rows_per_cta == 8 && units <= kClusterMaxUnits &&
-                tiles > 0;
+    // A few long units of one entry (long-context decode, one rank's shard, a small decode): whole
+    // clusters of kClusterCtas CTAs per unit, at least 16 tiles per CTA and about two CTAs per SM
+    // in all (a third CTA per SM measured slower: more partials to merge, uneven CTAs per SM).
+    // One entry only: its units (kv heads) have equal lengths, while clusters sized for the
+    // longest of several entries leave the shorter ones' CTAs idle (a 4-slot share of
+    // decode_batch: 52.0 us clustered, 42.3 us persistent).
+    p.cluster = p.persistent && o.schedule == YF_SCHED_AUTO && p.rows_per_cta == 8 && batch == 1 &&
+                units <= kClusterMaxUnits && tiles > 0;
     if (p.cluster) {
         p.persistent = false;
         // one wave of clusters: cluster placement is per GPC, so the device's cluster capacity,

@@ -162,9 +162,9 @@ def test_long_context_split_merges(yf, oracle, cuda, schedule):
 
 @pytest.mark.parametrize("ctx", [[1], [15, 16, 17], [0, 300, 5000, 1], [65, 1025, 40000, 7, 130, 2049, 0, 4096]])
 def test_cluster_schedule_ragged_few_units(yf, oracle, cuda, ctx):
-    """Few units of very different lengths (one to eight entries x 2 kv heads) on the cluster
-    schedule: short units use one cluster (output written by the cluster merge), long ones several
-    (merged per column slice by the last arrival); zero-length entries give zeros."""
+    """Few units of very different lengths (one to eight entries x 2 kv heads): one entry runs on
+    the cluster schedule (one cluster per unit: output written by the cluster merge), several on
+    the persistent schedule, which balances unequal lengths; zero-length entries give zeros."""
     n = len(ctx)
     wl = W.Workload("fu", 16, 2, 256, ctx=ctx, q_rows=np.ones(n), seed=124 + n)
     pool, img, desc, _, _ = filled_pool(yf, oracle, wl, seed=125)
