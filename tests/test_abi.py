@@ -106,6 +106,8 @@ def test_workspace_size_plan(yf):
     row = 8 * 129 * 4   # one partial: rows_per_cta x (D + 1) floats
     # few units: the cluster schedule, one cluster per unit for 8 units of 4 tiles (no partials)
     assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 0
+    # the same units over two entries (lengths may differ): persistent, 4 CTAs x 2 partial slots
+    assert L.yf_attn_workspace_size(pool.handle, 32, 2, 1, 64) == 4 * 2 * row
     # persistent decode: two partial slots per CTA, at least 16 tiles per CTA, at most 4 CTAs/SM
     pool.set_options(schedule=_abi.YF_SCHED_PERSISTENT)
     assert L.yf_attn_workspace_size(pool.handle, 32, 1, 1, 64) == 2 * 2 * row   # 32 tiles -> 2 CTAs
