@@ -615,7 +615,10 @@ def gpu_arm(args, rank: int, world: int, local_rank: int):
     if world > 1 and args.config == "decode_batch" and not args.no_long:
         del step
         torch.cuda.empty_cache()
-        line["decode_long_sharded"] = long_sharded_leg(args, rank, world, local_rank)
+        try:
+            line["decode_long_sharded"] = long_sharded_leg(args, rank, world, local_rank)
+        except Exception as exc:  # reported in the line; the decode_batch result above stands
+            line["decode_long_sharded"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(wl_full, args.cpu_seconds)
     return line
