@@ -155,3 +155,21 @@ def test_attention_options_are_explicit_and_validated(yf):
     persistent = L.yf_attn_workspace_size(pool.handle, 32, 16, 1, 32768)
     assert chunked > 0 and persistent > 0 and chunked != persistent
     assert L.yf_pool_plant_counter(pool.handle, 0, 1, None) == _abi.YF_E_INVALID   # host-only pool
+
+
+def test_exchange_arguments_are_validated_without_a_device(yf):
+    """yf_exchange_create refuses a bad rank, world or slot size before any CUDA call, leaving
+    the output null; the other exchange entry points refuse null handles."""
+    L = yf.lib()
+    h = ctypes.c_void_p()
+    for device, rank, world, slot in [(0, 0, 0, 16), (0, 2, 2, 16), (0, -1, 2, 16), (0, 0, 65, 16),
+                                      (0, 0, 2, 6), (0, 0, 2, 0)]:
+        assert L.yf_exchange_create(device, rank, world, slot, ctypes.byref(h)) == _abi.YF_E_INVALID
+        assert not h.value
+    assert L.yf_exchange_create(0, 0, 2, 16, None) == _abi.YF_E_INVALID
+    buf = (ctypes.c_uint8 * _abi.YF_EXCHANGE_HANDLE_BYTES)()
+    assert L.yf_exchange_handle(None, buf) == _abi.YF_E_INVALID
+    assert L.yf_exchange_push(None, None, None) == _abi.YF_E_INVALID
+    bits = ctypes.c_uint32()
+    assert L.yf_exchange_status(None, ctypes.byref(bits), 0) == _abi.YF_E_INVALID
+    assert L.yf_exchange_destroy(None) == _abi.YF_OK
